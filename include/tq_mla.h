@@ -1,0 +1,181 @@
+/*
+ * tq_mla.h - C ABI of the B200 (sm_100a) absorbed-MLA paged-attention library (libtq_mla.so).
+ *
+ * Plain C types only: numeric device addresses, byte sizes, status codes. No exceptions cross
+ * this boundary and the library allocates no device memory on the launch path: the caller owns
+ * every buffer, including the workspace whose size tq_mla_workspace_bytes reports.
+ *
+ * Reference interfaces each entry point replaces (paths inside TensorQuay/tensorquay-engine):
+ *   tq_mla_validate          SmlaParams::new            crates/tq-core/src/contracts.rs:437-493
+ *   tq_mla_prefill_validate  the SMLA-PF contract       docs/TEST-PLAN.md:195,410-413 (planned)
+ *   tq_mla_should_launch     SmlaParams::should_launch  crates/tq-core/src/contracts.rs:509-511
+ *   tq_mla_decode            sparse_mla_decode launcher docs/ARCHITECTURE.md:111-113 (planned),
+ *                            dense paged form; numerics reference/src/tq_reference/
+ *                            mla_attention.py:135-169
+ *   tq_mla_prefill           SMLA-PF launcher           docs/TEST-PLAN.md:410-413 (planned)
+ *   tq_mla_combine           split-K merge              docs/TEST-PLAN.md:206-207,220,247
+ *   tq_philox_words          tq_testkit::philox::fill_words crates/tq-testkit/src/philox.rs:78-98
+ *   tq_philox_block          tq_testkit::philox::block      crates/tq-testkit/src/philox.rs:57-70
+ *   tq_philox_uniform_f32    tq_testkit::philox::uniform_f32 crates/tq-testkit/src/philox.rs:109-111
+ */
+#ifndef TQ_MLA_H
+#define TQ_MLA_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Storage element types (contracts.rs:41-50). */
+enum { TQ_DTYPE_BF16 = 0, TQ_DTYPE_I32 = 1, TQ_DTYPE_F32 = 2, TQ_DTYPE_U8 = 3 };
+
+/* Paged row formats (contracts.rs:129-144), plus the 576-wide DeepSeek-style row. */
+enum {
+  TQ_KV_BF16 = 0,         /* 512 bf16 latent values, 1024 B, q width 512, scale 0.0625   */
+  TQ_KV_FP8_E4M3 = 1,     /* 512 E4M3 codes + 4 f32 scales, 528 B (validated; not launched) */
+  TQ_KV_BF16_ROPE576 = 2  /* 512 latent + 64 RoPE bf16, 1152 B, q width 576, any scale > 0  */
+};
+
+/* Status codes. 1..12 are the contract violations (contracts.rs:65-90) in declaration order. */
+enum {
+  TQ_OK = 0,
+  TQ_SHAPE = 1, TQ_DTYPE = 2, TQ_DIMENSION = 3, TQ_STRIDE = 4, TQ_ALIGNMENT = 5,
+  TQ_ADDRESS = 6, TQ_CAPACITY = 7, TQ_OVERFLOW = 8, TQ_QUERY_COUNT = 9, TQ_SCALE = 10,
+  TQ_GROUP = 11, TQ_ALIAS = 12,
+  TQ_ERR_INVALID_ARGUMENT = 100, /* null pointer or malformed argument                   */
+  TQ_ERR_UNSUPPORTED = 101,      /* validated layout that no kernel here launches        */
+  TQ_ERR_WORKSPACE = 102,        /* workspace missing, misaligned or too small           */
+  TQ_ERR_CUDA = 103,             /* a CUDA runtime/driver call failed                    */
+  TQ_ERR_PARAMS = 104,           /* params not produced by a validate call, or altered   */
+  TQ_ERR_RANGE = 105             /* Philox word range exceeds u64 (philox.md:69-75)      */
+};
+
+/* Device error flag bits, read back with tq_mla_read_device_error. */
+enum {
+  TQ_DEV_WAIT_TIMEOUT = 1,  /* a bounded wait gave up; the kernel aborted cleanly          */
+  TQ_DEV_PAGE_RANGE = 2,    /* a page-table entry outside [0, pages); the tile read zeros */
+  TQ_DEV_SEQ_RANGE = 4,     /* a seq_id outside [0, sequences); the token was left empty  */
+  TQ_DEV_TABLE_SHORT = 8,   /* kv_len beyond 64 * page-table width; clamped              */
+  TQ_DEV_WORK_OVERFLOW = 16 /* total page work does not fit 31 bits; nothing computed     */
+};
+
+/* One tensor declaration (contracts.rs:109-125). rank <= 3; unused trailing axes ignored. */
+typedef struct {
+  uint64_t shape[3];
+  uint64_t strides_bytes[3];
+  int32_t rank;
+  int32_t dtype;
+  uint64_t device_address;
+  uint64_t buffer_bytes;
+} TqTensorSpec;
+
+/* Dense paged MLA launch metadata (the dense form of SmlaSpec, contracts.rs:182-209).
+ *   q          bf16 [T, H, Dqk]   Dqk = 512 (TQ_KV_BF16) or 576 (TQ_KV_BF16_ROPE576)
+ *   kv         u8   [P, 64, payload] with strides [64 r, r, 1], r >= payload, r % 16 == 0
+ *   page_table i32  [S, L]
+ *   seq_id     i32  [T]      q_pos i32 [T]      kv_len i32 [S]
+ *   out        bf16 or f32 [T, H, 512]          lse   f32 [T, H] (natural log)
+ * Token t attends to positions [0, min(kv_len[seq_id[t]], q_pos[t] + 1)) of its sequence. */
+typedef struct {
+  TqTensorSpec q, kv, page_table, seq_id, q_pos, kv_len, out, lse;
+  int32_t kv_format;
+  float softmax_scale;
+} TqMlaSpec;
+
+/* A rejected contract: stable field name (static storage) and violation kind. */
+typedef struct {
+  const char* field;
+  int32_t kind;
+} TqContractError;
+
+/* Validated parameters. Produced only by the validate calls; launches re-check the digest. */
+typedef struct {
+  TqMlaSpec spec;
+  uint64_t tokens, heads, sequences, slots, pages, qk_width, row_stride;
+  int32_t max_queries_per_sequence; /* 4 for decode plans, 0 for prefill plans */
+  int32_t should_launch;            /* tokens != 0                              */
+  uint64_t digest;
+} TqMlaParams;
+
+/* Merge of G partial results (fp32 outputs normalised per part, natural-log lse):
+ *   part_out f32 [G, T, H, 512] packed, part_lse f32 [G, T, H] packed,
+ *   out bf16 or f32 [T, H, 512] (padded outer strides allowed), lse f32 [T, H] packed. */
+typedef struct {
+  uint64_t parts, tokens, heads;
+  uint64_t part_out, part_lse; /* device addresses */
+  uint64_t out, lse;
+  uint64_t out_stride_token, out_stride_head; /* bytes */
+  int32_t out_dtype;
+} TqCombineParams;
+
+/* Byte offsets of the scheduler metadata inside a workspace (for inspection and tests). */
+typedef struct {
+  uint64_t total_bytes;
+  uint64_t header;        /* int32[16]: error, total pages, quota, n_combine, n_empty, pairs */
+  uint64_t unit_n;        /* int32[T]  visible keys per token                               */
+  uint64_t unit_pages;    /* int32[T]                                                       */
+  uint64_t unit_gstart;   /* int32[T]  first global page                                    */
+  uint64_t unit_first;    /* int32[T]  first CTA pair touching the token (-1 if none)       */
+  uint64_t unit_nsplit;   /* int32[T]                                                       */
+  uint64_t unit_split_off;/* int32[T]                                                       */
+  uint64_t pair_begin;    /* int32[pairs] first token of each CTA pair (-1 if idle)          */
+  uint64_t combine_list;  /* int32[T]                                                       */
+  uint64_t empty_list;    /* int32[T]                                                       */
+  uint64_t part_lse;      /* f32[2*pairs, 128]                                              */
+  uint64_t part_out;      /* f32[2*pairs, 128, 512]                                         */
+  int32_t pairs;          /* CTA pairs of the main kernel on this device                    */
+} TqWorkspaceLayout;
+
+/* Decode plan: query_counts[n] with n == S, each <= 4, sum == T (contracts.rs:477-490). */
+int32_t tq_mla_validate(const TqMlaSpec* spec, const uint8_t* query_counts, uint64_t n,
+                        TqMlaParams* params, TqContractError* err);
+/* Prefill plan: query_counts[n] with n == S and sum == T; no per-sequence limit. */
+int32_t tq_mla_prefill_validate(const TqMlaSpec* spec, const uint32_t* query_counts, uint64_t n,
+                                TqMlaParams* params, TqContractError* err);
+int32_t tq_mla_should_launch(const TqMlaParams* params);
+
+/* Workspace size and layout for a validated launch on `device` (0-based CUDA ordinal). */
+int32_t tq_mla_workspace_bytes(const TqMlaParams* params, int32_t device, uint64_t* bytes);
+int32_t tq_mla_workspace_layout(const TqMlaParams* params, int32_t device,
+                                TqWorkspaceLayout* layout);
+
+/* Launch on `stream` (a cudaStream_t; NULL = legacy default stream) of the current device.
+ * The workspace must be 256-byte aligned and at least tq_mla_workspace_bytes long; calls that
+ * share a workspace must be ordered on one stream. `err` (optional) names the field when a
+ * launch-time layout requirement fails (q needs 16-byte aligned address and strides for TMA). */
+int32_t tq_mla_decode(const TqMlaParams* params, void* workspace, uint64_t workspace_bytes,
+                      void* stream, TqContractError* err);
+int32_t tq_mla_prefill(const TqMlaParams* params, void* workspace, uint64_t workspace_bytes,
+                       void* stream, TqContractError* err);
+int32_t tq_mla_combine(const TqCombineParams* params, void* stream);
+
+/* Device error flag of the last launch that used `workspace` (synchronises `stream`). */
+int32_t tq_mla_read_device_error(const void* workspace, void* stream, int32_t* flags);
+
+/* Philox4x32-10 test stream (host). tq_philox_words fills out[count]; an overflowing range
+ * returns TQ_ERR_RANGE and leaves `out` untouched. */
+void tq_philox_block(const uint32_t counter[4], const uint32_t key[2], uint32_t out[4]);
+int32_t tq_philox_words(uint64_t seed, uint64_t stream_id, uint64_t start, uint32_t* out,
+                        uint64_t count);
+float tq_philox_uniform_f32(uint32_t word);
+
+/* Seeded synthetic inputs on the device (Box-Muller normals rounded to bf16; see DESIGN).
+ *   tq_gen_normal_bf16: dst[i] = normal(seed, stream_id, start + i) for i < count.
+ *   tq_gen_kv_pool: fills every row of the pool with NaN, then writes normal rows for each
+ *   sequence's cached positions through the page table (normal index (tok_off[b]+p)*width+d). */
+int32_t tq_gen_normal_bf16(void* dst, uint64_t count, uint64_t seed, uint64_t stream_id,
+                           uint64_t start, void* stream);
+int32_t tq_gen_kv_pool(void* pool, uint64_t pool_pages, uint64_t row_stride, uint64_t width,
+                       const void* page_table, uint64_t slots, const void* kv_len,
+                       const void* tok_off, uint64_t sequences, uint64_t seed, void* stream);
+
+const char* tq_mla_status_string(int32_t status);
+/* Library build identity: "tq_mla <version> sm_100a". */
+const char* tq_mla_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TQ_MLA_H */

@@ -1,0 +1,350 @@
+// Host contract validation for the dense paged MLA launch, and the Philox4x32-10 test stream.
+//
+// Validation restates SmlaParams::new (crates/tq-core/src/contracts.rs:437-493) and its helpers
+// check (:262-325), check_strides (:331-356), check_kv_strides (:359-371) and check_aliases
+// (:407-421): same field names, same violation kinds, same checked 64-bit span arithmetic, same
+// empty-launch rule (docs/HOST-CONTRACTS.md:96-102). The generalisations (576-wide rows, 16/128
+// heads, runtime scale for the 576 format, no sparse index tensors, f32 partial outputs,
+// unbounded prefill plans) are listed in tq_contracts.h.
+//
+// Philox restates crates/tq-testkit/src/philox.rs:57-111 (block, fill_words, uniform_f32).
+
+#include "tq_contracts.h"
+
+#include <cmath>
+#include <cstring>
+
+namespace tq {
+
+namespace {
+
+constexpr uint64_t kDimensionLimit = uint64_t(1) << 31;
+constexpr uint64_t kPageRows = 64;
+constexpr uint64_t kKvGranularity = 16;
+constexpr uint32_t kGlmScaleBits = 0x3D800000u;  // 0.0625f
+constexpr uint64_t kDigestSalt = 0x7C3A5E1B9D2F4861ull;
+
+enum class Layout { Packed, PaddedOuter, Checked };
+
+struct Extent {
+  const char* field;
+  uint64_t start, end;
+  bool present;
+};
+
+struct Failure {
+  const char* field;
+  int32_t kind;
+};
+
+uint64_t element_bytes(int32_t dtype) {
+  switch (dtype) {
+    case TQ_DTYPE_U8: return 1;
+    case TQ_DTYPE_BF16: return 2;
+    case TQ_DTYPE_I32:
+    case TQ_DTYPE_F32: return 4;
+    default: return 0;
+  }
+}
+
+bool mul_overflows(uint64_t a, uint64_t b, uint64_t* out) {
+  return __builtin_mul_overflow(a, b, out);
+}
+bool add_overflows(uint64_t a, uint64_t b, uint64_t* out) {
+  return __builtin_add_overflow(a, b, out);
+}
+
+// Innermost stride is the element size; each outer stride spans the axis inside it.
+bool check_strides(const TqTensorSpec& t, int rank, Layout layout, uint64_t element,
+                   int32_t* kind) {
+  if (t.strides_bytes[rank - 1] != element) { *kind = TQ_STRIDE; return false; }
+  for (int axis = rank - 2; axis >= 0; --axis) {
+    uint64_t inner = t.strides_bytes[axis + 1];
+    uint64_t extent = t.shape[axis + 1] > 1 ? t.shape[axis + 1] : 1;
+    uint64_t needed;
+    if (mul_overflows(inner, extent, &needed)) { *kind = TQ_OVERFLOW; return false; }
+    uint64_t stride = t.strides_bytes[axis];
+    bool fits = layout == Layout::Packed ? stride == needed
+                                         : (stride >= needed && stride % element == 0);
+    if (!fits) { *kind = TQ_STRIDE; return false; }
+  }
+  return true;
+}
+
+// Checks one tensor; on success fills `ext` (present only when launching and non-empty).
+bool check(const char* field, const TqTensorSpec& t, const uint64_t* shape, int rank,
+           int32_t dtype, Layout layout, bool launching, Extent* ext, Failure* f) {
+  ext->present = false;
+  ext->field = field;
+  if (t.rank != rank) { *f = {field, TQ_SHAPE}; return false; }
+  if (t.dtype != dtype) { *f = {field, TQ_DTYPE}; return false; }
+  for (int i = 0; i < rank; ++i)
+    if (t.shape[i] != shape[i]) { *f = {field, TQ_SHAPE}; return false; }
+  for (int i = 0; i < rank; ++i)
+    if (t.shape[i] >= kDimensionLimit) { *f = {field, TQ_DIMENSION}; return false; }
+  const uint64_t element = element_bytes(dtype);
+  int32_t kind = 0;
+  if (layout != Layout::Checked && !check_strides(t, rank, layout, element, &kind)) {
+    *f = {field, kind};
+    return false;
+  }
+  bool empty = false;
+  for (int i = 0; i < rank; ++i) empty |= t.shape[i] == 0;
+  if (!launching || empty) return true;
+  uint64_t span = element;
+  for (int i = 0; i < rank; ++i) {
+    uint64_t reach;
+    if (mul_overflows(t.shape[i] - 1, t.strides_bytes[i], &reach) ||
+        add_overflows(span, reach, &span)) {
+      *f = {field, TQ_OVERFLOW};
+      return false;
+    }
+  }
+  if (t.device_address == 0) { *f = {field, TQ_ADDRESS}; return false; }
+  const uint64_t granularity = layout == Layout::Checked ? kKvGranularity : element;
+  if (t.device_address % granularity != 0) { *f = {field, TQ_ALIGNMENT}; return false; }
+  if (t.buffer_bytes < span) { *f = {field, TQ_CAPACITY}; return false; }
+  uint64_t end;
+  if (add_overflows(t.device_address, t.buffer_bytes, &end)) {
+    *f = {field, TQ_OVERFLOW};
+    return false;
+  }
+  // The bytes the tensor covers, not the capacity behind it (contracts.rs:318-324).
+  *ext = {field, t.device_address, t.device_address + span, true};
+  return true;
+}
+
+// Paged KV rows are [64 r, r, 1] with r at least the payload and a multiple of 16.
+bool check_kv_strides(const TqTensorSpec& t, uint64_t payload, Failure* f) {
+  if (t.rank != 3) { *f = {"kv", TQ_SHAPE}; return false; }
+  const uint64_t row = t.strides_bytes[1];
+  if (t.strides_bytes[2] != 1 || row < payload || row % kKvGranularity != 0) {
+    *f = {"kv", TQ_STRIDE};
+    return false;
+  }
+  uint64_t page;
+  if (mul_overflows(kPageRows, row, &page)) { *f = {"kv", TQ_OVERFLOW}; return false; }
+  if (t.strides_bytes[0] != page) { *f = {"kv", TQ_STRIDE}; return false; }
+  return true;
+}
+
+bool check_aliases(const Extent* inputs, int n_in, const Extent* outputs, int n_out, Failure* f) {
+  for (int o = 0; o < n_out; ++o) {
+    const Extent& out = outputs[o];
+    if (!out.present) continue;
+    for (int i = 0; i < n_in + o; ++i) {
+      const Extent& other = i < n_in ? inputs[i] : outputs[i - n_in];
+      if (!other.present) continue;
+      if (out.start < other.end && other.start < out.end) {
+        *f = {out.field, TQ_ALIAS};
+        return false;
+      }
+    }
+  }
+  return true;
+}
+
+uint32_t f32_bits(float x) {
+  uint32_t b;
+  std::memcpy(&b, &x, 4);
+  return b;
+}
+
+bool scale_ok(int32_t format, float scale) {
+  if (format == TQ_KV_BF16 || format == TQ_KV_FP8_E4M3) return f32_bits(scale) == kGlmScaleBits;
+  return std::isfinite(scale) && scale > 0.0f;
+}
+
+// FNV-1a over the bytes of the params (digest field excluded).
+uint64_t digest_of(const TqMlaParams& p) {
+  const unsigned char* b = reinterpret_cast<const unsigned char*>(&p);
+  const size_t n = offsetof(TqMlaParams, digest);
+  uint64_t h = 0xCBF29CE484222325ull ^ kDigestSalt;
+  for (size_t i = 0; i < n; ++i) {
+    h ^= b[i];
+    h *= 0x100000001B3ull;
+  }
+  return h;
+}
+
+template <typename Count>
+int32_t validate_impl(const TqMlaSpec* spec, const Count* counts, uint64_t n, int max_per_seq,
+                      TqMlaParams* params, TqContractError* err) {
+  Failure f{nullptr, TQ_OK};
+  auto fail = [&](const char* field, int32_t kind) {
+    if (err) { err->field = field; err->kind = kind; }
+    return kind;
+  };
+  if (!spec || (!counts && n != 0)) return fail("spec", TQ_ERR_INVALID_ARGUMENT);
+  const TqMlaSpec& s = *spec;
+  if (s.q.rank != 3) return fail("q", TQ_SHAPE);
+  const uint64_t tokens = s.q.shape[0], heads = s.q.shape[1], width = s.q.shape[2];
+  uint64_t payload = 0, qk_width = 0;
+  switch (s.kv_format) {
+    case TQ_KV_BF16: payload = 1024; qk_width = 512; break;
+    case TQ_KV_FP8_E4M3: payload = 528; qk_width = 512; break;
+    case TQ_KV_BF16_ROPE576: payload = 1152; qk_width = 576; break;
+    default: return fail("kv_format", TQ_SHAPE);
+  }
+  if ((heads != 16 && heads != 32 && heads != 64 && heads != 128) || width != qk_width)
+    return fail("q", TQ_SHAPE);
+  if (!scale_ok(s.kv_format, s.softmax_scale)) return fail("softmax_scale", TQ_SCALE);
+  if (s.page_table.rank != 2) return fail("page_table", TQ_SHAPE);
+  const uint64_t sequences = s.page_table.shape[0], slots = s.page_table.shape[1];
+  const bool launching = tokens != 0;
+  if (!check_kv_strides(s.kv, payload, &f)) return fail(f.field, f.kind);
+
+  const uint64_t query[3] = {tokens, heads, width};
+  const uint64_t pool[3] = {s.kv.shape[0], kPageRows, payload};
+  const uint64_t table[2] = {sequences, slots};
+  const uint64_t tok[1] = {tokens};
+  const uint64_t seqs[1] = {sequences};
+  const uint64_t outshape[3] = {tokens, heads, 512};
+  const uint64_t lseshape[2] = {tokens, heads};
+  Extent in[6], out[2];
+  if (!check("q", s.q, query, 3, TQ_DTYPE_BF16, Layout::PaddedOuter, launching, &in[0], &f) ||
+      !check("kv", s.kv, pool, 3, TQ_DTYPE_U8, Layout::Checked, launching, &in[1], &f) ||
+      !check("page_table", s.page_table, table, 2, TQ_DTYPE_I32, Layout::Packed, launching,
+             &in[2], &f) ||
+      !check("seq_id", s.seq_id, tok, 1, TQ_DTYPE_I32, Layout::Packed, launching, &in[3], &f) ||
+      !check("q_pos", s.q_pos, tok, 1, TQ_DTYPE_I32, Layout::Packed, launching, &in[4], &f) ||
+      !check("kv_len", s.kv_len, seqs, 1, TQ_DTYPE_I32, Layout::Packed, launching, &in[5], &f))
+    return fail(f.field, f.kind);
+  // The output may be bf16 (final) or f32 (a partial result to merge across devices).
+  const int32_t out_dtype = s.out.dtype == TQ_DTYPE_F32 ? TQ_DTYPE_F32 : TQ_DTYPE_BF16;
+  if (!check("out", s.out, outshape, 3, out_dtype, Layout::PaddedOuter, launching, &out[0], &f) ||
+      !check("lse", s.lse, lseshape, 2, TQ_DTYPE_F32, Layout::Packed, launching, &out[1], &f))
+    return fail(f.field, f.kind);
+
+  if (n != sequences) return fail("query_counts", TQ_QUERY_COUNT);
+  uint64_t planned = 0;
+  for (uint64_t i = 0; i < n; ++i) {
+    const uint64_t c = counts[i];
+    if (max_per_seq > 0 && c > uint64_t(max_per_seq)) return fail("query_counts", TQ_QUERY_COUNT);
+    planned += c;  // n < 2^31 and c < 2^32: cannot wrap
+  }
+  if (planned != tokens) return fail("query_counts", TQ_QUERY_COUNT);
+  if (!check_aliases(in, 6, out, 2, &f)) return fail(f.field, f.kind);
+
+  if (params) {
+    std::memset(params, 0, sizeof(*params));
+    params->spec = s;
+    params->tokens = tokens;
+    params->heads = heads;
+    params->sequences = sequences;
+    params->slots = slots;
+    params->pages = s.kv.shape[0];
+    params->qk_width = qk_width;
+    params->row_stride = s.kv.strides_bytes[1];
+    params->max_queries_per_sequence = max_per_seq;
+    params->should_launch = launching ? 1 : 0;
+    params->digest = digest_of(*params);
+  }
+  if (err) { err->field = nullptr; err->kind = TQ_OK; }
+  return TQ_OK;
+}
+
+}  // namespace
+
+bool params_intact(const TqMlaParams* p) { return p && p->digest == digest_of(*p); }
+
+// ---------------------------------------------------------------------------------------------
+// Philox4x32-10: ten rounds, key bumped by (W0, W1) per round (philox.rs:57-70).
+
+void philox_block(const uint32_t counter[4], const uint32_t key[2], uint32_t out[4]) {
+  uint32_t c0 = counter[0], c1 = counter[1], c2 = counter[2], c3 = counter[3];
+  uint32_t k0 = key[0], k1 = key[1];
+  for (int r = 0; r < 10; ++r) {
+    const uint64_t p0 = uint64_t(0xD2511F53u) * c0;
+    const uint64_t p1 = uint64_t(0xCD9E8D57u) * c2;
+    const uint32_t n0 = uint32_t(p1 >> 32) ^ c1 ^ k0;
+    const uint32_t n2 = uint32_t(p0 >> 32) ^ c3 ^ k1;
+    c1 = uint32_t(p1);
+    c3 = uint32_t(p0);
+    c0 = n0;
+    c2 = n2;
+    k0 += 0x9E3779B9u;
+    k1 += 0xBB67AE85u;
+  }
+  out[0] = c0; out[1] = c1; out[2] = c2; out[3] = c3;
+}
+
+int32_t philox_words(uint64_t seed, uint64_t stream, uint64_t start, uint32_t* out,
+                     uint64_t count) {
+  if (count == 0) return TQ_OK;
+  uint64_t last;
+  if (add_overflows(start, count - 1, &last)) return TQ_ERR_RANGE;
+  if (!out) return TQ_ERR_INVALID_ARGUMENT;
+  const uint32_t key[2] = {uint32_t(seed), uint32_t(seed >> 32)};
+  uint64_t i = start, written = 0;
+  while (written < count) {
+    const uint64_t group = i >> 2;
+    const uint32_t counter[4] = {uint32_t(group), uint32_t(group >> 32), uint32_t(stream),
+                                 uint32_t(stream >> 32)};
+    uint32_t lanes[4];
+    philox_block(counter, key, lanes);
+    for (unsigned lane = unsigned(i & 3); lane < 4 && written < count; ++lane) {
+      out[written++] = lanes[lane];
+      ++i;
+    }
+  }
+  return TQ_OK;
+}
+
+float philox_uniform_f32(uint32_t word) { return float(word >> 8) * (1.0f / 16777216.0f); }
+
+}  // namespace tq
+
+extern "C" {
+
+int32_t tq_mla_validate(const TqMlaSpec* spec, const uint8_t* query_counts, uint64_t n,
+                        TqMlaParams* params, TqContractError* err) {
+  return tq::validate_impl(spec, query_counts, n, 4, params, err);
+}
+
+int32_t tq_mla_prefill_validate(const TqMlaSpec* spec, const uint32_t* query_counts, uint64_t n,
+                                TqMlaParams* params, TqContractError* err) {
+  return tq::validate_impl(spec, query_counts, n, 0, params, err);
+}
+
+int32_t tq_mla_should_launch(const TqMlaParams* params) {
+  return tq::params_intact(params) ? params->should_launch : 0;
+}
+
+void tq_philox_block(const uint32_t counter[4], const uint32_t key[2], uint32_t out[4]) {
+  tq::philox_block(counter, key, out);
+}
+
+int32_t tq_philox_words(uint64_t seed, uint64_t stream_id, uint64_t start, uint32_t* out,
+                        uint64_t count) {
+  return tq::philox_words(seed, stream_id, start, out, count);
+}
+
+float tq_philox_uniform_f32(uint32_t word) { return tq::philox_uniform_f32(word); }
+
+const char* tq_mla_status_string(int32_t status) {
+  switch (status) {
+    case TQ_OK: return "ok";
+    case TQ_SHAPE: return "Shape";
+    case TQ_DTYPE: return "Dtype";
+    case TQ_DIMENSION: return "Dimension";
+    case TQ_STRIDE: return "Stride";
+    case TQ_ALIGNMENT: return "Alignment";
+    case TQ_ADDRESS: return "Address";
+    case TQ_CAPACITY: return "Capacity";
+    case TQ_OVERFLOW: return "Overflow";
+    case TQ_QUERY_COUNT: return "QueryCount";
+    case TQ_SCALE: return "Scale";
+    case TQ_GROUP: return "Group";
+    case TQ_ALIAS: return "Alias";
+    case TQ_ERR_INVALID_ARGUMENT: return "invalid argument";
+    case TQ_ERR_UNSUPPORTED: return "unsupported layout";
+    case TQ_ERR_WORKSPACE: return "workspace missing, misaligned or too small";
+    case TQ_ERR_CUDA: return "CUDA error";
+    case TQ_ERR_PARAMS: return "params not produced by validation";
+    case TQ_ERR_RANGE: return "word range exceeds u64";
+    default: return "unknown status";
+  }
+}
+
+}  // extern "C"

@@ -1,0 +1,28 @@
+// Internal declarations shared by the host validation (tq_contracts.cpp) and the CUDA launch
+// glue (tq_mla_kernels.cu). The public ABI is include/tq_mla.h.
+//
+// Generalisations of SmlaParams::new (crates/tq-core/src/contracts.rs:437-493) for the dense
+// paged path:
+//   - row format TQ_KV_BF16_ROPE576 (1152-byte rows); q is [T, H, 576] for it, out [T, H, 512];
+//   - heads in {16, 32, 64, 128} (the reference accepts {32, 64});
+//   - softmax scale: exactly 0.0625f for the reference's 512-wide formats (contracts.rs:446),
+//     any finite positive f32 for TQ_KV_BF16_ROPE576;
+//   - no idx / k_len tensors: dense attention over [0, min(kv_len, q_pos + 1));
+//   - out may be f32 (a partial result merged later by tq_mla_combine);
+//   - prefill plans (tq_mla_prefill_validate) have no 4-queries-per-sequence limit.
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+
+#include "../../include/tq_mla.h"
+
+namespace tq {
+
+bool params_intact(const TqMlaParams* p);
+void philox_block(const uint32_t counter[4], const uint32_t key[2], uint32_t out[4]);
+int32_t philox_words(uint64_t seed, uint64_t stream, uint64_t start, uint32_t* out,
+                     uint64_t count);
+float philox_uniform_f32(uint32_t word);
+
+}  // namespace tq

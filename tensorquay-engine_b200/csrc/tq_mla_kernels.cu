@@ -1,0 +1,1220 @@
+// Paged absorbed-MLA attention for B200 (sm_100a): scheduler, main tcgen05 kernel, combine.
+//
+// Numerics follow reference/src/tq_reference/mla_attention.py:135-169 with identity key
+// absorption (q arrives absorbed) and value projection [I_512 | 0]: per query token and head,
+//   s = (q . k) * scale,  p = exp(s - m) / sum(exp(s - m)),  out = sum p v,  lse = m + ln sum.
+// Storage precision follows docs/TEST-PLAN.md:61-63 (f32 scores, f32 softmax, P rounded to bf16,
+// f32 accumulation of P.V, output rounded once). A token with no visible key gets zeros and
+// lse = -inf (mla_attention.py:147-148). The launch grid depends only on the device, never on the
+// data (docs/TEST-PLAN.md:205-206); split-KV partial results merge by log-sum-exp.
+//
+// Kernel structure (one CTA pair = cluster of 2, one CTA per SM):
+//   warp 0      TMA producer: Q slice per token, then 64-row KV pages through the page table
+//               (3-stage ring); pages outside the pool are fetched fully out of bounds (zeros)
+//               and flagged.
+//   warp 1      MMA issuer: S = Q_slice K_slice^T into TMEM (M=128 heads, N=64 keys), then
+//               O_half += P V_half with P read from TMEM (M=128, N=256, K=16 keys per step).
+//               It zeroes the rows of a partial last page before the MMAs read them, so the NaN
+//               poison of unused slots never reaches an accumulator.
+//   warps 2-5   softmax and epilogue: one thread per head row (its TMEM lane). Partial scores
+//               of the heads owned by the peer are sent to it through distributed shared memory;
+//               the owner adds both halves, applies the mask and an online softmax whose running
+//               maximum is only raised when it grows by more than 2^8 (exact after the final
+//               normalisation), and sends the bf16 probabilities back.
+// Every wait is bounded (globaltimer); on timeout the CTA pair records TQ_DEV_WAIT_TIMEOUT,
+// drains its in-flight TMA and MMA work, frees TMEM and exits.
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstring>
+#include <mutex>
+
+#include "tq_contracts.h"
+#include "tq_mla_layout.h"
+#include "tq_ptx.cuh"
+
+namespace tq {
+namespace mla {
+
+constexpr uint64_t kWaitTimeoutNs = 2000000000ull;   // 2 s: a wait this long means a fault
+constexpr uint64_t kDrainTimeoutNs = 200000000ull;   // 0.2 s for draining in-flight copies
+constexpr uint32_t kWaitMaxPolls = 1u << 22;          // second bound, independent of the timer
+constexpr uint32_t kDrainMaxPolls = 1u << 20;
+constexpr float kLn2 = 0.69314718055994530942f;
+constexpr float kRescaleThreshold = 8.0f;            // log2 units
+
+struct Meta {
+  int* header;
+  int* unit_n;
+  int* unit_pages;
+  int* unit_gstart;
+  int* unit_first;
+  int* unit_nsplit;
+  int* unit_split_off;
+  int* pair_begin;
+  int* combine_list;
+  int* empty_list;
+  float* part_lse;
+  float* part_out;
+};
+
+struct MainArgs {
+  Meta meta;
+  const int* page_table;
+  const int* seq_id;
+  long long slots;
+  long long pool_rows;
+  int tokens;
+  int heads;
+  char* out;
+  long long out_stride_t;
+  long long out_stride_h;
+  int out_f32;
+  float* lse;
+  float scale_log2;
+};
+
+// ---------------------------------------------------------------------------------------------
+// Scheduler: one block of 1024 threads.
+
+__device__ long long block_exclusive_scan(long long v, long long* total, long long* sh) {
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  long long x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    long long y = __shfl_up_sync(0xFFFFFFFFu, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) sh[w] = x;
+  __syncthreads();
+  if (w == 0) {
+    long long t = sh[lane];
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      long long y = __shfl_up_sync(0xFFFFFFFFu, t, o);
+      if (lane >= o) t += y;
+    }
+    sh[lane] = t;
+  }
+  __syncthreads();
+  const long long before = w ? sh[w - 1] : 0;
+  *total = sh[31];
+  __syncthreads();
+  return before + x - v;
+}
+
+__global__ void __launch_bounds__(1024) schedule_kernel(Meta m, const int* __restrict__ seq_id,
+                                                        const int* __restrict__ q_pos,
+                                                        const int* __restrict__ kv_len, int T,
+                                                        int S, long long slots, long long pool_pages,
+                                                        int pairs) {
+  __shared__ long long sh[32];
+  __shared__ int s_err;
+  if (threadIdx.x == 0) s_err = 0;
+  for (int c = threadIdx.x; c < pairs; c += blockDim.x) m.pair_begin[c] = -1;
+  __syncthreads();
+  const int per = (T + 1023) / 1024;
+  const int lo = min(T, int(threadIdx.x) * per), hi = min(T, lo + per);
+
+  long long my_pages = 0;
+  for (int u = lo; u < hi; ++u) {
+    const int s = seq_id[u];
+    long long n = 0;
+    if (s < 0 || s >= S) {
+      atomicOr(&s_err, TQ_DEV_SEQ_RANGE);
+    } else {
+      long long kl = kv_len[s];
+      const long long cap = pool_pages > 0 ? slots * kPageRows : 0;
+      if (kl > cap) {
+        atomicOr(&s_err, pool_pages > 0 ? TQ_DEV_TABLE_SHORT : TQ_DEV_PAGE_RANGE);
+        kl = cap;
+      }
+      n = min(kl, (long long)q_pos[u] + 1);
+      if (n < 0) n = 0;
+    }
+    const int pages = int((n + kPageRows - 1) / kPageRows);
+    m.unit_n[u] = int(n);
+    m.unit_pages[u] = pages;
+    my_pages += pages;
+  }
+  long long total = 0;
+  long long g = block_exclusive_scan(my_pages, &total, sh);
+  if (total >= (1ll << 31)) {
+    if (threadIdx.x == 0) atomicOr(&s_err, TQ_DEV_WORK_OVERFLOW);
+    total = 0;
+  }
+  const long long quota = total ? (total + pairs - 1) / pairs : 0;
+  long long my_split = 0;
+  for (int u = lo; u < hi; ++u) {
+    const int pages = total ? m.unit_pages[u] : 0;
+    m.unit_gstart[u] = int(g);
+    int first = -1, ns = 0;
+    if (pages > 0) {
+      first = int(g / quota);
+      ns = int((g + pages - 1) / quota) - first + 1;
+      const long long c_lo = (g + quota - 1) / quota, c_hi = (g + pages - 1) / quota;
+      for (long long c = c_lo; c <= c_hi; ++c) m.pair_begin[c] = u;
+    }
+    m.unit_first[u] = first;
+    m.unit_nsplit[u] = ns;
+    my_split += ns >= 2 ? ns : 0;
+    g += pages;
+  }
+  long long tmp;
+  long long off = block_exclusive_scan(my_split, &tmp, sh);
+  long long my_comb = 0, my_empty = 0;
+  for (int u = lo; u < hi; ++u) {
+    m.unit_split_off[u] = int(off);
+    const int ns = m.unit_nsplit[u];
+    off += ns >= 2 ? ns : 0;
+    my_comb += ns >= 2;
+    my_empty += (total ? m.unit_pages[u] : 0) == 0;
+  }
+  long long n_comb = 0, n_empty = 0;
+  long long comb_at = block_exclusive_scan(my_comb, &n_comb, sh);
+  long long empty_at = block_exclusive_scan(my_empty, &n_empty, sh);
+  for (int u = lo; u < hi; ++u) {
+    if (m.unit_nsplit[u] >= 2) m.combine_list[comb_at++] = u;
+    if ((total ? m.unit_pages[u] : 0) == 0) m.empty_list[empty_at++] = u;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    m.header[kHdrError] = s_err;
+    m.header[kHdrTotalPages] = int(total);
+    m.header[kHdrQuota] = int(quota);
+    m.header[kHdrNumCombine] = int(n_comb);
+    m.header[kHdrNumEmpty] = int(n_empty);
+    m.header[kHdrPairs] = pairs;
+    m.header[kHdrTokens] = T;
+    m.header[kHdrTimeoutWhere] = 0;
+    m.header[kHdrTimeoutBar] = 0;
+    m.header[kHdrTimeoutCta] = 0;
+  }
+}
+
+// ---------------------------------------------------------------------------------------------
+// Segment walk: the (token, first page, page count, partial slot) pieces a CTA pair processes.
+
+struct Seg {
+  int u, p0, np, slot;
+};
+
+struct SegWalker {
+  long long g, g_end;
+  int u, p, T, c;
+  __device__ void init(const Meta& m, int pair, int tokens) {
+    const long long total = m.header[kHdrTotalPages], quota = m.header[kHdrQuota];
+    c = pair;
+    T = tokens;
+    g = g_end = 0;
+    u = p = 0;
+    if (quota == 0 || (long long)pair * quota >= total) return;
+    u = m.pair_begin[pair];
+    if (u < 0 || u >= tokens) return;  // inconsistent metadata: process nothing
+    g = (long long)pair * quota;
+    g_end = min(g + quota, total);
+    p = int(g - m.unit_gstart[u]);
+  }
+  __device__ bool next(const Meta& m, Seg& s) {
+    if (g >= g_end || u >= T) return false;
+    const int pages = m.unit_pages[u];
+    if (p < 0 || p >= pages) return false;
+    const int n = int(min((long long)(pages - p), g_end - g));
+    s.u = u;
+    s.p0 = p;
+    s.np = n;
+    const int ns = m.unit_nsplit[u];
+    s.slot = ns >= 2 ? m.unit_split_off[u] + c - m.unit_first[u] : -1;
+    g += n;
+    p = 0;
+    if (g < g_end) {
+      do { ++u; } while (u < T && m.unit_pages[u] == 0);
+    }
+    return true;
+  }
+};
+
+// ---------------------------------------------------------------------------------------------
+// Bounded waits.
+
+struct Waiter {
+  volatile int* abort_flag;
+  int* header;          // workspace header: error bits, then the first timeout's location
+  uint32_t peer_abort;  // shared::cluster address of the peer's abort flag
+  int where;            // caller role and page counter, recorded on timeout
+  uint32_t bar_base;    // shared address of barrier 0
+
+  __device__ void fail(uint32_t bar, uint32_t parity) {
+    if (!*abort_flag) {
+      *abort_flag = 1;
+      ptx::st_cluster_u32(peer_abort, 1u);
+      atomicOr(header + kHdrError, TQ_DEV_WAIT_TIMEOUT);
+      if (atomicCAS(header + kHdrTimeoutWhere, 0, where | int(0x40000000)) == 0) {
+        header[kHdrTimeoutBar] = int((bar - bar_base) / 8u) | int(parity << 16);
+        header[kHdrTimeoutCta] = int(blockIdx.x) * 1024 + int(threadIdx.x);
+      }
+    }
+  }
+
+  // Bounded twice: by the global timer and by an iteration count, so a stalled timer cannot
+  // turn a missed phase into an endless spin.
+  template <bool kCluster>
+  __device__ bool wait(uint32_t bar, uint32_t parity) {
+    if (kCluster ? ptx::mbar_test_cluster(bar, parity) : ptx::mbar_test(bar, parity)) return true;
+    const uint64_t t0 = ptx::global_timer_ns();
+    for (uint32_t i = 1;; ++i) {
+      if (kCluster ? ptx::mbar_test_cluster(bar, parity) : ptx::mbar_test(bar, parity))
+        return true;
+      if ((i & 63) == 0) {
+        if (*abort_flag) return false;
+        if (ptx::global_timer_ns() - t0 > kWaitTimeoutNs || i >= kWaitMaxPolls) {
+          fail(bar, parity);
+          return false;
+        }
+      }
+    }
+  }
+
+  // Ignores the abort flag: used to drain work already in flight before the CTA exits.
+  __device__ bool drain(uint32_t bar, uint32_t parity) {
+    const uint64_t t0 = ptx::global_timer_ns();
+    for (uint32_t i = 1; !ptx::mbar_test(bar, parity); ++i) {
+      if (ptx::global_timer_ns() - t0 > kDrainTimeoutNs || i >= kDrainMaxPolls) {
+        fail(bar, parity);
+        return false;
+      }
+    }
+    return true;
+  }
+};
+
+// ---------------------------------------------------------------------------------------------
+// Main kernel.
+
+template <bool kRope>
+__global__ void __launch_bounds__(kThreads, 1)
+    mla_paged_kernel(const __grid_constant__ CUtensorMap tm_q,
+                     const __grid_constant__ CUtensorMap tm_q_rope,
+                     const __grid_constant__ CUtensorMap tm_kv,
+                     const __grid_constant__ CUtensorMap tm_kv_rope, const MainArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = ptx::smem_addr(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  uint8_t* sm = smem_raw + (base - raw);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = ptx::cluster_rank(), peer = rank ^ 1u;
+  const int pair = int(ptx::cluster_id_x());
+  auto bar = [&](int i) -> uint32_t { return base + kSmBars + 8u * uint32_t(i); };
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(sm + kSmMisc + 4);
+  const uint32_t* tmem_holder = reinterpret_cast<const uint32_t*>(sm + kSmMisc);
+  Waiter wt{abort_flag, a.meta.header, ptx::map_peer(base + kSmMisc + 4, peer), 0,
+            base + kSmBars};
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      ptx::mbar_init(bar(kBarKvFull + s), 1);
+      ptx::mbar_init(bar(kBarKvEmpty + s), 1);
+    }
+    ptx::mbar_init(bar(kBarQFull), 1);
+    ptx::mbar_init(bar(kBarQEmpty), 1);
+    for (int b = 0; b < 2; ++b) {
+      ptx::mbar_init(bar(kBarSFull + b), 1);
+      ptx::mbar_init(bar(kBarSFree + b), kSoftmaxThreads);
+      ptx::mbar_init(bar(kBarPFull + b), kSoftmaxThreads);
+      ptx::mbar_init(bar(kBarPvDone + b), 1);
+    }
+    ptx::mbar_init(bar(kBarOFull), 1);
+    ptx::mbar_init(bar(kBarOFree), kSoftmaxThreads);
+    for (int b = kBarXbFull; b <= kBarStFree; ++b) ptx::mbar_init(bar(b), kOwnedRows);
+    ptx::mbar_init(bar(kBarDrain), 1);
+    *abort_flag = 0;
+    ptx::fence_mbar_init_cluster();
+    ptx::tma_prefetch_desc(&tm_q);
+    ptx::tma_prefetch_desc(&tm_kv);
+    if (kRope) {
+      ptx::tma_prefetch_desc(&tm_q_rope);
+      ptx::tma_prefetch_desc(&tm_kv_rope);
+    }
+  }
+  // Query rows past the head count stay zero for the whole kernel (TMA writes rows < heads).
+  if (a.heads < kHeadsTile) {
+    const int rows = kHeadsTile - a.heads;
+    const int main_words = rows * 128 / 16, rope_words = rows * 64 / 16;
+    for (int i = threadIdx.x; i < 4 * main_words; i += kThreads) {
+      const int chunk = i / main_words, w = i % main_words;
+      reinterpret_cast<uint4*>(sm + kSmQMain + chunk * kQChunkBytes + a.heads * 128)[w] =
+          make_uint4(0, 0, 0, 0);
+    }
+    if (kRope)
+      for (int i = threadIdx.x; i < rope_words; i += kThreads)
+        reinterpret_cast<uint4*>(sm + kSmQRope + a.heads * 64)[i] = make_uint4(0, 0, 0, 0);
+    ptx::fence_proxy_async_smem();
+  }
+  if (warp == 1) {
+    ptx::tmem_alloc(base + kSmMisc, kTmemCols);
+    ptx::tmem_relinquish();
+  }
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::cluster_sync();
+  ptx::tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+
+  SegWalker walker;
+  walker.init(a.meta, pair, a.tokens);
+  const Meta& meta = a.meta;
+  const int k_main0 = 256 * int(rank);      // first latent dim of this CTA's slice
+  const int k_rope0 = 512 + 32 * int(rank); // first RoPE dim of this CTA's slice
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      const uint32_t q_bytes = uint32_t(a.heads) * (kRope ? (256 + 32) * 2 : 256 * 2);
+      const uint32_t stage_bytes = kRope ? kStageBytes : 4 * kKvChunkBytes;
+      uint32_t it = 0, useq = 0;
+      Seg s;
+      bool ok = true;
+      while (ok && walker.next(meta, s)) {
+        wt.where = (1 << 24) | int(it & 0xFFFFFF);
+        if (!wt.wait<false>(bar(kBarQEmpty), (useq & 1u) ^ 1u)) break;
+        ptx::mbar_expect_tx(bar(kBarQFull), q_bytes);
+        for (int k = 0; k < 4; ++k)
+          ptx::tma_load_3d(base + kSmQMain + k * kQChunkBytes, &tm_q, bar(kBarQFull),
+                           k_main0 + 64 * k, 0, s.u);
+        if (kRope)
+          ptx::tma_load_3d(base + kSmQRope, &tm_q_rope, bar(kBarQFull), k_rope0, 0, s.u);
+        ++useq;
+        const int* pt = a.page_table + (long long)a.seq_id[s.u] * a.slots;
+        for (int j = 0; j < s.np; ++j, ++it) {
+          const uint32_t stage = it % kStages;
+          wt.where = (1 << 24) | int(it & 0xFFFFFF);
+          if (!wt.wait<false>(bar(kBarKvEmpty + stage), ((it / kStages) & 1u) ^ 1u)) {
+            ok = false;
+            break;
+          }
+          const int page = pt[s.p0 + j];
+          long long row = (long long)page * kPageRows;
+          if (page < 0 || row >= a.pool_rows) {
+            atomicOr(a.meta.header + kHdrError, TQ_DEV_PAGE_RANGE);
+            row = a.pool_rows;  // a box entirely out of bounds: TMA fills zeros
+          }
+          const uint32_t dst = base + kSmKv + stage * kStageBytes;
+          ptx::mbar_expect_tx(bar(kBarKvFull + stage), stage_bytes);
+          for (int k = 0; k < 4; ++k)
+            ptx::tma_load_2d(dst + k * kKvChunkBytes, &tm_kv, bar(kBarKvFull + stage),
+                             k_main0 + 64 * k, int(row));
+          if (kRope)
+            ptx::tma_load_2d(dst + kKvRopeOffset, &tm_kv_rope, bar(kBarKvFull + stage), k_rope0,
+                             int(row));
+        }
+      }
+      // Drain: every issued copy has landed before the CTA may exit.
+      for (uint32_t st = 0; st < kStages && st < it; ++st) {
+        const uint32_t last = it - 1 - ((it - 1 - st) % kStages);
+        wt.drain(bar(kBarKvFull + st), (last / kStages) & 1u);
+      }
+      if (useq) wt.drain(bar(kBarQFull), (useq - 1) & 1u);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer
+    constexpr uint32_t idesc_qk = ptx::idesc_bf16(128, 64, 0);
+    constexpr uint32_t idesc_pv = ptx::idesc_bf16(128, 256, 1);
+    uint32_t it = 0, useq = 0;
+    Seg s;
+    bool ok = true;
+    while (ok && walker.next(meta, s)) {
+      const int n = meta.unit_n[s.u];
+      if (!wt.wait<false>(bar(kBarQFull), useq & 1u)) break;
+      const uint32_t it0 = it;
+      for (int j = 0; j <= s.np && ok; ++j) {
+        wt.where = (2 << 24) | int((it0 + j) & 0xFFFFFF);
+        if (j < s.np) {
+          const uint32_t itq = it0 + j, stage = itq % kStages, sb = itq & 1u;
+          if (!wt.wait<false>(bar(kBarKvFull + stage), (itq / kStages) & 1u)) { ok = false; break; }
+          const uint32_t stage_base = base + kSmKv + stage * kStageBytes;
+          const int valid = min(kPageRows, n - (s.p0 + j) * kPageRows);
+          if (valid < kPageRows) {
+            uint8_t* st_ptr = sm + kSmKv + stage * kStageBytes;
+            const int main_words = (kPageRows - valid) * 128 / 16;
+            for (int i = lane; i < 4 * main_words; i += 32) {
+              const int chunk = i / main_words, w = i % main_words;
+              reinterpret_cast<uint4*>(st_ptr + chunk * kKvChunkBytes + valid * 128)[w] =
+                  make_uint4(0, 0, 0, 0);
+            }
+            if (kRope)
+              for (int i = lane; i < (kPageRows - valid) * 4; i += 32)
+                reinterpret_cast<uint4*>(st_ptr + kKvRopeOffset + valid * 64)[i] =
+                    make_uint4(0, 0, 0, 0);
+            ptx::fence_proxy_async_smem();
+            __syncwarp();
+          }
+          if (!wt.wait<false>(bar(kBarSFree + sb), ((itq >> 1) & 1u) ^ 1u)) { ok = false; break; }
+          ptx::tc_fence_after();
+          if (lane == 0) {
+            const uint32_t d = tmem + kTmemS + sb * 64;
+            for (int k = 0; k < 4; ++k)
+              for (int kk = 0; kk < 4; ++kk) {
+                const uint64_t ad = ptx::smem_desc(base + kSmQMain + k * kQChunkBytes + kk * 32,
+                                                   16, 1024, 2);
+                const uint64_t bd =
+                    ptx::smem_desc(stage_base + k * kKvChunkBytes + kk * 32, 16, 1024, 2);
+                ptx::mma_ss(d, ad, bd, idesc_qk, (k | kk) != 0);
+              }
+            if (kRope)
+              for (int kk = 0; kk < 2; ++kk) {
+                const uint64_t ad = ptx::smem_desc(base + kSmQRope + kk * 32, 16, 512, 4);
+                const uint64_t bd =
+                    ptx::smem_desc(stage_base + kKvRopeOffset + kk * 32, 16, 512, 4);
+                ptx::mma_ss(d, ad, bd, idesc_qk, 1);
+              }
+            ptx::mma_commit(bar(kBarSFull + sb));
+            if (j == s.np - 1) ptx::mma_commit(bar(kBarQEmpty));
+          }
+          __syncwarp();
+        }
+        if (j > 0) {
+          const uint32_t itp = it0 + j - 1, stage = itp % kStages, pb = itp & 1u;
+          if (j == 1 && !wt.wait<false>(bar(kBarOFree), (useq & 1u) ^ 1u)) { ok = false; break; }
+          if (!wt.wait<false>(bar(kBarPFull + pb), (itp >> 1) & 1u)) { ok = false; break; }
+          ptx::tc_fence_after();
+          if (lane == 0) {
+            const uint32_t stage_base = base + kSmKv + stage * kStageBytes;
+            for (int kk = 0; kk < 4; ++kk) {
+              // V as B, MN-major: 64-dim chunks 8 KB apart (LBO), 8-key groups 1 KB apart (SBO).
+              const uint64_t bd = ptx::smem_desc(stage_base + kk * 2048, kKvChunkBytes, 1024, 2);
+              ptx::mma_ts(tmem + kTmemO, tmem + kTmemP + pb * 32 + kk * 8, bd, idesc_pv,
+                          (j > 1 || kk > 0) ? 1u : 0u);
+            }
+            ptx::mma_commit(bar(kBarKvEmpty + stage));
+            ptx::mma_commit(bar(kBarPvDone + pb));
+            if (j == s.np) ptx::mma_commit(bar(kBarOFull));
+          }
+          __syncwarp();
+        }
+      }
+      it = it0 + s.np;
+      ++useq;
+    }
+    if (lane == 0) ptx::mma_commit(bar(kBarDrain));
+    __syncwarp();
+    wt.drain(bar(kBarDrain), 0);
+  } else {
+    // ------------------------------------------------------------------ softmax + epilogue
+    const int qd = warp & 3;
+    const int h = 32 * qd + lane;
+    const bool owner = (qd >> 1) == int(rank);
+    const int orow = h - 64 * int(owner ? rank : peer);
+    const uint32_t lane_base = uint32_t(32 * qd) << 16;
+    const uint32_t xb_local = base + kSmXbuf + orow * kXRowBytes;
+    const uint32_t pr_local = base + kSmPrx + orow * kPRowBytes;
+    const uint32_t st_local = base + kSmStats + orow * 8;
+    const uint32_t xb_remote = ptx::map_peer(xb_local, peer);
+    const uint32_t pr_remote = ptx::map_peer(pr_local, peer);
+    const uint32_t st_remote = ptx::map_peer(st_local, peer);
+    const uint32_t xb_full_r = ptx::map_peer(bar(kBarXbFull), peer);
+    const uint32_t xb_free_r = ptx::map_peer(bar(kBarXbFree), peer);
+    const uint32_t pr_full_r = ptx::map_peer(bar(kBarPrFull), peer);
+    const uint32_t pr_free_r = ptx::map_peer(bar(kBarPrFree), peer);
+    const uint32_t st_full_r = ptx::map_peer(bar(kBarStFull), peer);
+    const uint32_t st_free_r = ptx::map_peer(bar(kBarStFree), peer);
+    const float c2 = a.scale_log2;
+    uint32_t it = 0, useq = 0;
+    Seg s;
+    bool ok = true;
+    while (ok && walker.next(meta, s)) {
+      const int n = meta.unit_n[s.u];
+      float m_used = -INFINITY, l = 0.f;
+      for (int j = 0; j < s.np; ++j) {
+        const uint32_t itq = it + j, sb = itq & 1u;
+        const int valid = min(kPageRows, n - (s.p0 + j) * kPageRows);
+        wt.where = ((owner ? 4 : 3) << 24) | int(itq & 0xFFFFFF);
+        if (!wt.wait<false>(bar(kBarSFull + sb), (itq >> 1) & 1u)) { ok = false; break; }
+        __syncwarp();
+        ptx::tc_fence_after();
+        uint32_t sr[64];
+        {
+          uint32_t(&r0)[16] = *reinterpret_cast<uint32_t(*)[16]>(&sr[0]);
+          uint32_t(&r1)[16] = *reinterpret_cast<uint32_t(*)[16]>(&sr[16]);
+          uint32_t(&r2)[16] = *reinterpret_cast<uint32_t(*)[16]>(&sr[32]);
+          uint32_t(&r3)[16] = *reinterpret_cast<uint32_t(*)[16]>(&sr[48]);
+          const uint32_t t = tmem + lane_base + kTmemS + sb * 64;
+          ptx::tmem_ld16(t, r0);
+          ptx::tmem_ld16(t + 16, r1);
+          ptx::tmem_ld16(t + 32, r2);
+          ptx::tmem_ld16(t + 48, r3);
+          ptx::tmem_wait_ld();
+        }
+        ptx::tc_fence_before();
+        ptx::mbar_arrive(bar(kBarSFree + sb));
+        uint32_t pk[32];
+        float corr = 1.f;
+        if (!owner) {
+          if (!wt.wait<true>(bar(kBarXbFree), (itq & 1u) ^ 1u)) { ok = false; break; }
+#pragma unroll
+          for (int k = 0; k < 16; ++k)
+            ptx::st_cluster_v4(xb_remote + 16 * k, sr[4 * k], sr[4 * k + 1], sr[4 * k + 2],
+                               sr[4 * k + 3]);
+          ptx::mbar_arrive_cluster(xb_full_r);
+          if (!wt.wait<true>(bar(kBarPrFull), itq & 1u)) { ok = false; break; }
+          const uint4* src = reinterpret_cast<const uint4*>(sm + kSmPrx + orow * kPRowBytes);
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            const uint4 v = src[k];
+            pk[4 * k] = v.x; pk[4 * k + 1] = v.y; pk[4 * k + 2] = v.z; pk[4 * k + 3] = v.w;
+          }
+          corr = *reinterpret_cast<const float*>(sm + kSmPrx + orow * kPRowBytes + 128);
+          ptx::mbar_arrive_cluster(pr_free_r);
+        } else {
+          if (!wt.wait<true>(bar(kBarXbFull), itq & 1u)) { ok = false; break; }
+          const float4* xs = reinterpret_cast<const float4*>(sm + kSmXbuf + orow * kXRowBytes);
+          float sv[64];
+#pragma unroll
+          for (int k = 0; k < 16; ++k) {
+            const float4 v = xs[k];
+            sv[4 * k] = __uint_as_float(sr[4 * k]) + v.x;
+            sv[4 * k + 1] = __uint_as_float(sr[4 * k + 1]) + v.y;
+            sv[4 * k + 2] = __uint_as_float(sr[4 * k + 2]) + v.z;
+            sv[4 * k + 3] = __uint_as_float(sr[4 * k + 3]) + v.w;
+          }
+          ptx::mbar_arrive_cluster(xb_free_r);
+          float mx = -INFINITY;
+#pragma unroll
+          for (int i = 0; i < 64; ++i) {
+            sv[i] = i < valid ? sv[i] * c2 : -INFINITY;
+            mx = fmaxf(mx, sv[i]);
+          }
+          if (j == 0) {
+            m_used = mx;
+          } else if (mx > m_used + kRescaleThreshold) {
+            corr = ptx::ex2(m_used - mx);
+            m_used = mx;
+            l *= corr;
+          }
+          // The row sum uses the f32 probabilities (softmax in f32); only the PV operand is
+          // rounded to bf16 (docs/TEST-PLAN.md:61-63).
+          float sum0 = 0.f, sum1 = 0.f;
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const float p0 = ptx::ex2(sv[2 * i] - m_used), p1 = ptx::ex2(sv[2 * i + 1] - m_used);
+            pk[i] = ptx::pack_bf16x2(p0, p1);
+            sum0 += p0;
+            sum1 += p1;
+          }
+          l += sum0 + sum1;
+          if (!wt.wait<true>(bar(kBarPrFree), (itq & 1u) ^ 1u)) { ok = false; break; }
+#pragma unroll
+          for (int k = 0; k < 8; ++k)
+            ptx::st_cluster_v4(pr_remote + 16 * k, pk[4 * k], pk[4 * k + 1], pk[4 * k + 2],
+                               pk[4 * k + 3]);
+          ptx::st_cluster_u32(pr_remote + 128, __float_as_uint(corr));
+          ptx::mbar_arrive_cluster(pr_full_r);
+        }
+        // The running maximum moved for some row of this warp: rescale those rows of O once
+        // PV(itq-1) has landed. The decision is per lane but tcgen05.ld/st are warp-collective,
+        // so the whole warp takes the branch (a factor of exactly 1 leaves a row unchanged).
+        if (__any_sync(0xFFFFFFFFu, j > 0 && corr != 1.f)) {
+          const uint32_t prev = itq - 1;
+          if (!wt.wait<false>(bar(kBarPvDone + (prev & 1u)), (prev >> 1) & 1u)) { ok = false; break; }
+          __syncwarp();
+          ptx::tc_fence_after();
+          for (int c = 0; c < kValueHalf; c += 16) {
+            uint32_t v[16];
+            ptx::tmem_ld16(tmem + lane_base + kTmemO + c, v);
+            ptx::tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 16; ++i) v[i] = __float_as_uint(__uint_as_float(v[i]) * corr);
+            ptx::tmem_st16(tmem + lane_base + kTmemO + c, v);
+          }
+          ptx::tmem_wait_st();
+        }
+        if (itq >= 2) {
+          const uint32_t prev = itq - 2;
+          if (!wt.wait<false>(bar(kBarPvDone + sb), (prev >> 1) & 1u)) { ok = false; break; }
+        }
+        __syncwarp();
+        ptx::tc_fence_after();
+        {
+          const uint32_t t = tmem + lane_base + kTmemP + sb * 32;
+          ptx::tmem_st16(t, *reinterpret_cast<uint32_t(*)[16]>(&pk[0]));
+          ptx::tmem_st16(t + 16, *reinterpret_cast<uint32_t(*)[16]>(&pk[16]));
+          ptx::tmem_wait_st();
+        }
+        ptx::tc_fence_before();
+        ptx::mbar_arrive(bar(kBarPFull + sb));
+      }
+      if (!ok) break;
+      // Epilogue: normalise this CTA's half of O and write it.
+      wt.where = ((owner ? 6 : 5) << 24) | int(useq & 0xFFFFFF);
+      if (!wt.wait<false>(bar(kBarOFull), useq & 1u)) break;
+      __syncwarp();
+      ptx::tc_fence_after();
+      float inv_l;
+      if (owner) {
+        inv_l = 1.f / l;
+        const float lse = (m_used + log2f(l)) * kLn2;
+        if (!wt.wait<true>(bar(kBarStFree), (useq & 1u) ^ 1u)) break;
+        ptx::st_cluster_v2(st_remote, __float_as_uint(inv_l), __float_as_uint(lse));
+        ptx::mbar_arrive_cluster(st_full_r);
+        if (h < a.heads) {
+          if (s.slot >= 0) meta.part_lse[(long long)s.slot * kHeadsTile + h] = lse;
+          else a.lse[(long long)s.u * a.heads + h] = lse;
+        }
+      } else {
+        if (!wt.wait<true>(bar(kBarStFull), useq & 1u)) break;
+        inv_l = *reinterpret_cast<const float*>(sm + kSmStats + orow * 8);
+        ptx::mbar_arrive_cluster(st_free_r);
+      }
+      __syncwarp();
+      const int col0 = kValueHalf * int(rank);
+      for (int c = 0; c < kValueHalf; c += 32) {
+        uint32_t v[32];
+        __syncwarp();  // TMEM loads are warp-collective; lanes past the head count rejoin here
+        ptx::tmem_ld16(tmem + lane_base + kTmemO + c, *reinterpret_cast<uint32_t(*)[16]>(&v[0]));
+        ptx::tmem_ld16(tmem + lane_base + kTmemO + c + 16,
+                       *reinterpret_cast<uint32_t(*)[16]>(&v[16]));
+        ptx::tmem_wait_ld();
+        if (h >= a.heads) {
+          // padding row: nothing to store
+        } else if (s.slot >= 0 || a.out_f32) {
+          float4* dst =
+              s.slot >= 0
+                  ? reinterpret_cast<float4*>(meta.part_out +
+                                              ((long long)s.slot * kHeadsTile + h) * kValueDim +
+                                              col0 + c)
+                  : reinterpret_cast<float4*>(a.out + s.u * a.out_stride_t + h * a.out_stride_h +
+                                              (long long)(col0 + c) * 4);
+#pragma unroll
+          for (int k = 0; k < 8; ++k)
+            dst[k] = make_float4(__uint_as_float(v[4 * k]) * inv_l,
+                                 __uint_as_float(v[4 * k + 1]) * inv_l,
+                                 __uint_as_float(v[4 * k + 2]) * inv_l,
+                                 __uint_as_float(v[4 * k + 3]) * inv_l);
+        } else {
+          uint32_t pkd[16];
+#pragma unroll
+          for (int k = 0; k < 16; ++k)
+            pkd[k] = ptx::pack_bf16x2(__uint_as_float(v[2 * k]) * inv_l,
+                                      __uint_as_float(v[2 * k + 1]) * inv_l);
+          uint4* dst = reinterpret_cast<uint4*>(a.out + s.u * a.out_stride_t +
+                                                h * a.out_stride_h + (long long)(col0 + c) * 2);
+#pragma unroll
+          for (int k = 0; k < 4; ++k)
+            dst[k] = make_uint4(pkd[4 * k], pkd[4 * k + 1], pkd[4 * k + 2], pkd[4 * k + 3]);
+        }
+      }
+      ptx::tc_fence_before();
+      ptx::mbar_arrive(bar(kBarOFree));
+      it += s.np;
+      ++useq;
+    }
+  }
+
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::cluster_sync();
+  if (warp == 1) {
+    ptx::tc_fence_after();
+    ptx::tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+// ---------------------------------------------------------------------------------------------
+// Combine of split tokens, and zero-fill of tokens with no visible key.
+
+__device__ __forceinline__ void store8(char* base, int f32, const float (&v)[8]) {
+  if (f32) {
+    float4* d = reinterpret_cast<float4*>(base);
+    d[0] = make_float4(v[0], v[1], v[2], v[3]);
+    d[1] = make_float4(v[4], v[5], v[6], v[7]);
+  } else {
+    *reinterpret_cast<uint4*>(base) =
+        make_uint4(ptx::pack_bf16x2(v[0], v[1]), ptx::pack_bf16x2(v[2], v[3]),
+                   ptx::pack_bf16x2(v[4], v[5]), ptx::pack_bf16x2(v[6], v[7]));
+  }
+}
+
+__global__ void __launch_bounds__(256) combine_kernel(Meta m, char* out, long long st_t,
+                                                      long long st_h, int out_f32, float* lse,
+                                                      int heads) {
+  const int ncomb = m.header[kHdrNumCombine], nempty = m.header[kHdrNumEmpty];
+  const int esize = out_f32 ? 4 : 2;
+  for (int job = blockIdx.x; job < ncomb + nempty; job += gridDim.x) {
+    if (job < ncomb) {
+      const int u = m.combine_list[job];
+      const int ns = m.unit_nsplit[u], off = m.unit_split_off[u];
+      for (int task = threadIdx.x; task < heads * 64; task += blockDim.x) {
+        const int h = task >> 6, d0 = (task & 63) * 8;
+        float mx = -INFINITY;
+        for (int i = 0; i < ns; ++i) mx = fmaxf(mx, m.part_lse[(long long)(off + i) * kHeadsTile + h]);
+        float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+        float wsum = 0.f;
+        for (int i = 0; i < ns; ++i) {
+          const float li = m.part_lse[(long long)(off + i) * kHeadsTile + h];
+          const float w = li == -INFINITY ? 0.f : expf(li - mx);
+          wsum += w;
+          const float4* src = reinterpret_cast<const float4*>(
+              m.part_out + ((long long)(off + i) * kHeadsTile + h) * kValueDim + d0);
+          const float4 x0 = src[0], x1 = src[1];
+          acc[0] += w * x0.x; acc[1] += w * x0.y; acc[2] += w * x0.z; acc[3] += w * x0.w;
+          acc[4] += w * x1.x; acc[5] += w * x1.y; acc[6] += w * x1.z; acc[7] += w * x1.w;
+        }
+        const float inv = wsum > 0.f ? 1.f / wsum : 0.f;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) acc[k] *= inv;
+        store8(out + u * st_t + h * st_h + (long long)d0 * esize, out_f32, acc);
+        if (d0 == 0) lse[(long long)u * heads + h] = wsum > 0.f ? mx + logf(wsum) : -INFINITY;
+      }
+    } else {
+      const int u = m.empty_list[job - ncomb];
+      const float z[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+      for (int task = threadIdx.x; task < heads * 64; task += blockDim.x) {
+        const int h = task >> 6, d0 = (task & 63) * 8;
+        store8(out + u * st_t + h * st_h + (long long)d0 * esize, out_f32, z);
+        if (d0 == 0) lse[(long long)u * heads + h] = -INFINITY;
+      }
+    }
+  }
+}
+
+// Merge of G per-device partial results (cross-device split of one sequence's pages).
+__global__ void __launch_bounds__(256) merge_parts_kernel(const float* __restrict__ part_out,
+                                                          const float* __restrict__ part_lse,
+                                                          long long parts, long long tokens,
+                                                          long long heads, char* out,
+                                                          long long st_t, long long st_h,
+                                                          int out_f32, float* lse) {
+  const long long rows = tokens * heads;
+  const int esize = out_f32 ? 4 : 2;
+  for (long long task = blockIdx.x * (long long)blockDim.x + threadIdx.x; task < rows * 64;
+       task += (long long)gridDim.x * blockDim.x) {
+    const long long row = task >> 6;
+    const int d0 = int(task & 63) * 8;
+    const long long t = row / heads, h = row % heads;
+    float mx = -INFINITY;
+    for (long long g = 0; g < parts; ++g) mx = fmaxf(mx, part_lse[g * rows + row]);
+    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    float wsum = 0.f;
+    for (long long g = 0; g < parts; ++g) {
+      const float li = part_lse[g * rows + row];
+      const float w = li == -INFINITY ? 0.f : expf(li - mx);
+      if (w == 0.f) continue;
+      wsum += w;
+      const float4* src = reinterpret_cast<const float4*>(part_out + (g * rows + row) * kValueDim + d0);
+      const float4 x0 = src[0], x1 = src[1];
+      acc[0] += w * x0.x; acc[1] += w * x0.y; acc[2] += w * x0.z; acc[3] += w * x0.w;
+      acc[4] += w * x1.x; acc[5] += w * x1.y; acc[6] += w * x1.z; acc[7] += w * x1.w;
+    }
+    const float inv = wsum > 0.f ? 1.f / wsum : 0.f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) acc[k] *= inv;
+    store8(out + t * st_t + h * st_h + (long long)d0 * esize, out_f32, acc);
+    if (d0 == 0) lse[row] = wsum > 0.f ? mx + logf(wsum) : -INFINITY;
+  }
+}
+
+// ---------------------------------------------------------------------------------------------
+// Seeded synthetic inputs (device). Same stream and transform as the host generator.
+
+__device__ __forceinline__ void philox_block_dev(uint32_t c0, uint32_t c1, uint32_t c2, uint32_t c3,
+                                                 uint32_t k0, uint32_t k1, uint32_t (&o)[4]) {
+#pragma unroll
+  for (int r = 0; r < 10; ++r) {
+    const uint32_t lo0 = 0xD2511F53u * c0, hi0 = __umulhi(0xD2511F53u, c0);
+    const uint32_t lo1 = 0xCD9E8D57u * c2, hi1 = __umulhi(0xCD9E8D57u, c2);
+    const uint32_t n0 = hi1 ^ c1 ^ k0, n2 = hi0 ^ c3 ^ k1;
+    c1 = lo1;
+    c3 = lo0;
+    c0 = n0;
+    c2 = n2;
+    k0 += 0x9E3779B9u;
+    k1 += 0xBB67AE85u;
+  }
+  o[0] = c0; o[1] = c1; o[2] = c2; o[3] = c3;
+}
+
+// Round a finite double to bf16 bits, nearest with ties to even, straight from its bit pattern.
+__device__ __forceinline__ uint16_t double_to_bf16_bits(double x) {
+  unsigned long long b = __double_as_longlong(x);
+  const unsigned long long lsb = (b >> 45) & 1ull;
+  b += ((1ull << 44) - 1ull) + lsb;
+  b = (b >> 45) << 45;
+  const float f = float(__longlong_as_double(b));  // exact: at most 8 significant bits
+  return uint16_t(__float_as_uint(f) >> 16);
+}
+
+// Normal number `idx` of a stream: Box-Muller on words 2 idx and 2 idx + 1.
+__device__ __forceinline__ uint16_t normal_bf16_dev(uint64_t seed, uint64_t stream, uint64_t idx) {
+  const uint64_t w = 2 * idx, group = w >> 2;
+  uint32_t o[4];
+  philox_block_dev(uint32_t(group), uint32_t(group >> 32), uint32_t(stream), uint32_t(stream >> 32),
+                   uint32_t(seed), uint32_t(seed >> 32), o);
+  const uint32_t w0 = (w & 2) ? o[2] : o[0], w1 = (w & 2) ? o[3] : o[1];
+  const double u1 = (double(w0 >> 8) + 1.0) * (1.0 / 16777216.0);
+  const double u2 = double(w1 >> 8) * (1.0 / 16777216.0);
+  const double z = sqrt(-2.0 * log(u1)) * cos(2.0 * 3.141592653589793 * u2);
+  return double_to_bf16_bits(z);
+}
+
+__global__ void gen_normal_kernel(uint16_t* dst, uint64_t count, uint64_t seed, uint64_t stream,
+                                  uint64_t start) {
+  for (uint64_t i = blockIdx.x * uint64_t(blockDim.x) + threadIdx.x; i < count;
+       i += uint64_t(gridDim.x) * blockDim.x)
+    dst[i] = normal_bf16_dev(seed, stream, start + i);
+}
+
+__global__ void fill_u16_kernel(uint16_t* dst, uint64_t count, uint16_t v) {
+  for (uint64_t i = blockIdx.x * uint64_t(blockDim.x) + threadIdx.x; i < count;
+       i += uint64_t(gridDim.x) * blockDim.x)
+    dst[i] = v;
+}
+
+// grid (sequences, 64): block (b, y) writes positions y, y + 64, ... of sequence b.
+__global__ void gen_kv_rows_kernel(char* pool, uint64_t row_stride, uint64_t width,
+                                   const int* __restrict__ page_table, uint64_t slots,
+                                   const int* __restrict__ kv_len,
+                                   const long long* __restrict__ tok_off, uint64_t seed,
+                                   uint64_t stream, uint64_t pool_pages) {
+  const int b = blockIdx.x;
+  const long long n = kv_len[b];
+  for (long long p = blockIdx.y; p < n; p += gridDim.y) {
+    const int page = page_table[(long long)b * slots + p / kPageRows];
+    if (page < 0 || uint64_t(page) >= pool_pages) continue;
+    uint16_t* row = reinterpret_cast<uint16_t*>(
+        pool + (uint64_t(page) * kPageRows + uint64_t(p % kPageRows)) * row_stride);
+    const uint64_t e0 = (uint64_t(tok_off[b]) + uint64_t(p)) * width;
+    for (uint64_t d = threadIdx.x; d < width; d += blockDim.x)
+      row[d] = normal_bf16_dev(seed, stream, e0 + d);
+  }
+}
+
+// ---------------------------------------------------------------------------------------------
+// Host glue.
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+bool encode_bf16(CUtensorMap* map, const void* addr, int rank, const cuuint64_t* dims,
+                 const cuuint64_t* strides, const cuuint32_t* box, CUtensorMapSwizzle swz) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return false;
+  cuuint32_t elem_strides[3] = {1, 1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, cuuint32_t(rank), const_cast<void*>(addr), dims,
+            strides, box, elem_strides, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <bool kRope>
+cudaError_t prepare_kernel() {
+  return cudaFuncSetAttribute(mla_paged_kernel<kRope>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              int(kSmBytes));
+}
+
+// CTA pairs that are co-resident on `device` (the persistent grid size).
+int pairs_for_device(int device) {
+  static std::mutex mu;
+  static int cache[128] = {0};
+  std::lock_guard<std::mutex> lock(mu);
+  if (device < 0 || device >= 128) return 0;
+  if (cache[device]) return cache[device];
+  int prev = 0;
+  if (cudaGetDevice(&prev) != cudaSuccess) return 0;
+  if (prev != device && cudaSetDevice(device) != cudaSuccess) return 0;
+  int sms = 0;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+  int clusters = 0;
+  if (prepare_kernel<true>() == cudaSuccess && prepare_kernel<false>() == cudaSuccess) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * (sms / 2), 1, 1);
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = kSmBytes;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaOccupancyMaxActiveClusters(&clusters, mla_paged_kernel<true>, &cfg) != cudaSuccess)
+      clusters = 0;
+  }
+  cudaGetLastError();
+  if (prev != device) cudaSetDevice(prev);
+  if (clusters <= 0) return 0;
+  cache[device] = clusters;
+  return clusters;
+}
+
+uint64_t align256(uint64_t x) { return (x + 255) & ~uint64_t(255); }
+
+void layout_for(uint64_t tokens, int pairs, TqWorkspaceLayout* L) {
+  uint64_t o = 0;
+  auto take = [&](uint64_t bytes) {
+    const uint64_t at = o;
+    o = align256(o + bytes);
+    return at;
+  };
+  std::memset(L, 0, sizeof(*L));
+  L->header = take(kHdrWords * 4);
+  L->unit_n = take(tokens * 4);
+  L->unit_pages = take(tokens * 4);
+  L->unit_gstart = take(tokens * 4);
+  L->unit_first = take(tokens * 4);
+  L->unit_nsplit = take(tokens * 4);
+  L->unit_split_off = take(tokens * 4);
+  L->pair_begin = take(uint64_t(pairs) * 4);
+  L->combine_list = take(tokens * 4);
+  L->empty_list = take(tokens * 4);
+  L->part_lse = take(uint64_t(2 * pairs) * kHeadsTile * 4);
+  L->part_out = take(uint64_t(2 * pairs) * kHeadsTile * kValueDim * 4);
+  L->total_bytes = o;
+  L->pairs = pairs;
+}
+
+Meta meta_at(char* ws, const TqWorkspaceLayout& L) {
+  Meta m;
+  m.header = reinterpret_cast<int*>(ws + L.header);
+  m.unit_n = reinterpret_cast<int*>(ws + L.unit_n);
+  m.unit_pages = reinterpret_cast<int*>(ws + L.unit_pages);
+  m.unit_gstart = reinterpret_cast<int*>(ws + L.unit_gstart);
+  m.unit_first = reinterpret_cast<int*>(ws + L.unit_first);
+  m.unit_nsplit = reinterpret_cast<int*>(ws + L.unit_nsplit);
+  m.unit_split_off = reinterpret_cast<int*>(ws + L.unit_split_off);
+  m.pair_begin = reinterpret_cast<int*>(ws + L.pair_begin);
+  m.combine_list = reinterpret_cast<int*>(ws + L.combine_list);
+  m.empty_list = reinterpret_cast<int*>(ws + L.empty_list);
+  m.part_lse = reinterpret_cast<float*>(ws + L.part_lse);
+  m.part_out = reinterpret_cast<float*>(ws + L.part_out);
+  return m;
+}
+
+int32_t set_err(TqContractError* err, const char* field, int32_t kind) {
+  if (err) {
+    err->field = field;
+    err->kind = kind;
+  }
+  return kind;
+}
+
+int32_t launch(const TqMlaParams* params, void* workspace, uint64_t workspace_bytes, void* stream,
+               TqContractError* err) {
+  if (!params_intact(params)) return set_err(err, "params", TQ_ERR_PARAMS);
+  set_err(err, nullptr, TQ_OK);
+  if (!params->should_launch) return TQ_OK;
+  const TqMlaSpec& s = params->spec;
+  if (s.kv_format == TQ_KV_FP8_E4M3) return set_err(err, "kv_format", TQ_ERR_UNSUPPORTED);
+  const bool rope = s.kv_format == TQ_KV_BF16_ROPE576;
+  int device = 0;
+  if (cudaGetDevice(&device) != cudaSuccess) return set_err(err, "device", TQ_ERR_CUDA);
+  const int pairs = pairs_for_device(device);
+  if (pairs <= 0) return set_err(err, "device", TQ_ERR_CUDA);
+  TqWorkspaceLayout L;
+  layout_for(params->tokens, pairs, &L);
+  if (!workspace || (reinterpret_cast<uintptr_t>(workspace) & 255) ||
+      workspace_bytes < L.total_bytes)
+    return set_err(err, "workspace", TQ_ERR_WORKSPACE);
+  // TMA needs 16-byte aligned addresses and strides for q (natural alignment is 2 bytes).
+  if (s.q.device_address % 16) return set_err(err, "q", TQ_ALIGNMENT);
+  if (s.q.strides_bytes[0] % 16 || s.q.strides_bytes[1] % 16) return set_err(err, "q", TQ_STRIDE);
+  const uint64_t pool_rows = params->pages * kPageRows;
+  if (pool_rows >= (uint64_t(1) << 31) - kPageRows || params->tokens >= (uint64_t(1) << 31))
+    return set_err(err, "kv", TQ_ERR_UNSUPPORTED);
+  if (s.out.dtype == TQ_DTYPE_BF16 && (s.out.device_address % 16 || s.out.strides_bytes[0] % 16 ||
+                                       s.out.strides_bytes[1] % 16))
+    return set_err(err, "out", TQ_ALIGNMENT);
+  if (s.out.dtype == TQ_DTYPE_F32 && (s.out.device_address % 16 || s.out.strides_bytes[0] % 16 ||
+                                      s.out.strides_bytes[1] % 16))
+    return set_err(err, "out", TQ_ALIGNMENT);
+
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  char* ws = static_cast<char*>(workspace);
+  Meta m = meta_at(ws, L);
+  const int T = int(params->tokens), H = int(params->heads), S = int(params->sequences);
+
+  schedule_kernel<<<1, 1024, 0, st>>>(m, reinterpret_cast<const int*>(s.seq_id.device_address),
+                                      reinterpret_cast<const int*>(s.q_pos.device_address),
+                                      reinterpret_cast<const int*>(s.kv_len.device_address), T,
+                                      S, (long long)params->slots, (long long)params->pages,
+                                      pairs);
+  if (params->pages > 0) {
+    CUtensorMap tq_map, tq_rope, tkv, tkv_rope;
+    const uint64_t width = params->qk_width;
+    const cuuint64_t qdims[3] = {width, params->heads, params->tokens};
+    const cuuint64_t qstr[2] = {s.q.strides_bytes[1], s.q.strides_bytes[0]};
+    const cuuint32_t qbox[3] = {64, cuuint32_t(H), 1};
+    const cuuint32_t qbox_r[3] = {32, cuuint32_t(H), 1};
+    const cuuint64_t kdims[2] = {width, pool_rows};
+    const cuuint64_t kstr[1] = {params->row_stride};
+    const cuuint32_t kbox[2] = {64, 64};
+    const cuuint32_t kbox_r[2] = {32, 64};
+    const void* qa = reinterpret_cast<const void*>(s.q.device_address);
+    const void* ka = reinterpret_cast<const void*>(s.kv.device_address);
+    if (!encode_bf16(&tq_map, qa, 3, qdims, qstr, qbox, CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !encode_bf16(&tkv, ka, 2, kdims, kstr, kbox, CU_TENSOR_MAP_SWIZZLE_128B))
+      return set_err(err, "tensor_map", TQ_ERR_CUDA);
+    if (rope) {
+      if (!encode_bf16(&tq_rope, qa, 3, qdims, qstr, qbox_r, CU_TENSOR_MAP_SWIZZLE_64B) ||
+          !encode_bf16(&tkv_rope, ka, 2, kdims, kstr, kbox_r, CU_TENSOR_MAP_SWIZZLE_64B))
+        return set_err(err, "tensor_map", TQ_ERR_CUDA);
+    } else {
+      tq_rope = tq_map;
+      tkv_rope = tkv;
+    }
+    MainArgs a;
+    a.meta = m;
+    a.page_table = reinterpret_cast<const int*>(s.page_table.device_address);
+    a.seq_id = reinterpret_cast<const int*>(s.seq_id.device_address);
+    a.slots = (long long)params->slots;
+    a.pool_rows = (long long)pool_rows;
+    a.tokens = T;
+    a.heads = H;
+    a.out = reinterpret_cast<char*>(s.out.device_address);
+    a.out_stride_t = (long long)s.out.strides_bytes[0];
+    a.out_stride_h = (long long)s.out.strides_bytes[1];
+    a.out_f32 = s.out.dtype == TQ_DTYPE_F32;
+    a.lse = reinterpret_cast<float*>(s.lse.device_address);
+    a.scale_log2 = s.softmax_scale * 1.4426950408889634f;
+
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * pairs, 1, 1);
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = kSmBytes;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t e = rope ? cudaLaunchKernelEx(&cfg, mla_paged_kernel<true>, tq_map, tq_rope, tkv,
+                                              tkv_rope, a)
+                         : cudaLaunchKernelEx(&cfg, mla_paged_kernel<false>, tq_map, tq_rope, tkv,
+                                              tkv_rope, a);
+    if (e != cudaSuccess) return set_err(err, "launch", TQ_ERR_CUDA);
+  }
+  int sms = 0;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+  combine_kernel<<<sms > 0 ? sms : 148, 256, 0, st>>>(
+      m, reinterpret_cast<char*>(s.out.device_address), (long long)s.out.strides_bytes[0],
+      (long long)s.out.strides_bytes[1], s.out.dtype == TQ_DTYPE_F32,
+      reinterpret_cast<float*>(s.lse.device_address), H);
+  if (cudaGetLastError() != cudaSuccess) return set_err(err, "launch", TQ_ERR_CUDA);
+  return TQ_OK;
+}
+
+}  // namespace mla
+}  // namespace tq
+
+using namespace tq::mla;
+
+extern "C" {
+
+int32_t tq_mla_workspace_layout(const TqMlaParams* params, int32_t device,
+                                TqWorkspaceLayout* layout) {
+  if (!layout) return TQ_ERR_INVALID_ARGUMENT;
+  if (!tq::params_intact(params)) return TQ_ERR_PARAMS;
+  const int pairs = pairs_for_device(device);
+  if (pairs <= 0) return TQ_ERR_CUDA;
+  layout_for(params->tokens, pairs, layout);
+  return TQ_OK;
+}
+
+int32_t tq_mla_workspace_bytes(const TqMlaParams* params, int32_t device, uint64_t* bytes) {
+  if (!bytes) return TQ_ERR_INVALID_ARGUMENT;
+  TqWorkspaceLayout L;
+  const int32_t st = tq_mla_workspace_layout(params, device, &L);
+  if (st != TQ_OK) return st;
+  *bytes = L.total_bytes;
+  return TQ_OK;
+}
+
+int32_t tq_mla_decode(const TqMlaParams* params, void* workspace, uint64_t workspace_bytes,
+                      void* stream, TqContractError* err) {
+  if (params && tq::params_intact(params) && params->max_queries_per_sequence == 0)
+    return set_err(err, "params", TQ_ERR_PARAMS);  // a prefill plan
+  return launch(params, workspace, workspace_bytes, stream, err);
+}
+
+int32_t tq_mla_prefill(const TqMlaParams* params, void* workspace, uint64_t workspace_bytes,
+                       void* stream, TqContractError* err) {
+  return launch(params, workspace, workspace_bytes, stream, err);
+}
+
+int32_t tq_mla_combine(const TqCombineParams* p, void* stream) {
+  if (!p || !p->part_out || !p->part_lse || !p->out || !p->lse) return TQ_ERR_INVALID_ARGUMENT;
+  if (p->parts == 0 || p->tokens == 0 || p->heads == 0) return TQ_OK;
+  if ((p->part_out | p->out | p->out_stride_token | p->out_stride_head) % 16)
+    return TQ_ALIGNMENT;
+  const long long tasks = (long long)(p->tokens * p->heads * 64);
+  const int blocks = int(std::min<long long>((tasks + 255) / 256, 148 * 8));
+  merge_parts_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      reinterpret_cast<const float*>(p->part_out), reinterpret_cast<const float*>(p->part_lse),
+      (long long)p->parts, (long long)p->tokens, (long long)p->heads,
+      reinterpret_cast<char*>(p->out), (long long)p->out_stride_token,
+      (long long)p->out_stride_head, p->out_dtype == TQ_DTYPE_F32,
+      reinterpret_cast<float*>(p->lse));
+  return cudaGetLastError() == cudaSuccess ? TQ_OK : TQ_ERR_CUDA;
+}
+
+int32_t tq_mla_read_device_error(const void* workspace, void* stream, int32_t* flags) {
+  if (!workspace || !flags) return TQ_ERR_INVALID_ARGUMENT;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int32_t v = 0;
+  if (cudaMemcpyAsync(&v, workspace, 4, cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+      cudaStreamSynchronize(st) != cudaSuccess)
+    return TQ_ERR_CUDA;
+  *flags = v;
+  return TQ_OK;
+}
+
+int32_t tq_gen_normal_bf16(void* dst, uint64_t count, uint64_t seed, uint64_t stream_id,
+                           uint64_t start, void* stream) {
+  if (!dst && count) return TQ_ERR_INVALID_ARGUMENT;
+  if (!count) return TQ_OK;
+  const uint64_t blocks = std::min<uint64_t>((count + 255) / 256, 148 * 16);
+  gen_normal_kernel<<<unsigned(blocks), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<uint16_t*>(dst), count, seed, stream_id, start);
+  return cudaGetLastError() == cudaSuccess ? TQ_OK : TQ_ERR_CUDA;
+}
+
+int32_t tq_gen_kv_pool(void* pool, uint64_t pool_pages, uint64_t row_stride, uint64_t width,
+                       const void* page_table, uint64_t slots, const void* kv_len,
+                       const void* tok_off, uint64_t sequences, uint64_t seed, void* stream) {
+  if (!pool || row_stride % 2 || width * 2 > row_stride) return TQ_ERR_INVALID_ARGUMENT;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const uint64_t halves = pool_pages * kPageRows * row_stride / 2;
+  if (halves) {
+    const uint64_t blocks = std::min<uint64_t>((halves + 255) / 256, 148 * 16);
+    fill_u16_kernel<<<unsigned(blocks), 256, 0, st>>>(static_cast<uint16_t*>(pool), halves,
+                                                      uint16_t(0x7FC0));
+  }
+  if (sequences && pool_pages) {
+    gen_kv_rows_kernel<<<dim3(unsigned(sequences), 64), 256, 0, st>>>(
+        static_cast<char*>(pool), row_stride, width, static_cast<const int*>(page_table), slots,
+        static_cast<const int*>(kv_len), static_cast<const long long*>(tok_off), seed, 2,
+        pool_pages);
+  }
+  return cudaGetLastError() == cudaSuccess ? TQ_OK : TQ_ERR_CUDA;
+}
+
+const char* tq_mla_version(void) { return "tq_mla 0.1.0 sm_100a"; }
+
+}  // extern "C"

@@ -1,0 +1,49 @@
+"""Build libtq_mla.so in-tree with nvcc for sm_100a (run: ``python -m tq_mla.build``)."""
+
+import os
+import shutil
+import subprocess
+import sys
+from pathlib import Path
+
+PKG = Path(__file__).resolve().parent
+CSRC = PKG.parent / "csrc"
+SOURCES = ["tq_mla_kernels.cu", "tq_contracts.cpp"]
+HEADERS = ["tq_ptx.cuh", "tq_mla_layout.h", "tq_contracts.h"]
+TARGET = PKG / "libtq_mla.so"
+NVCC_FLAGS = [
+    "-gencode", "arch=compute_100a,code=sm_100a",
+    "-O3", "-lineinfo", "-std=c++17",
+    "-Xcompiler", "-fPIC,-O3",
+    "-shared",
+]
+
+
+def nvcc():
+    for cand in (os.environ.get("NVCC"), shutil.which("nvcc"), "/usr/local/cuda/bin/nvcc"):
+        if cand and Path(cand).exists():
+            return cand
+    raise RuntimeError("nvcc not found")
+
+
+def up_to_date():
+    if not TARGET.exists():
+        return False
+    built = TARGET.stat().st_mtime
+    deps = [CSRC / s for s in SOURCES + HEADERS] + [PKG.parent.parent / "include" / "tq_mla.h"]
+    return all(d.stat().st_mtime <= built for d in deps)
+
+
+def build(force=False, verbose=False):
+    if not force and up_to_date():
+        return TARGET
+    cmd = [nvcc(), *NVCC_FLAGS, "-o", str(TARGET), *[str(CSRC / s) for s in SOURCES]]
+    if verbose:
+        cmd.insert(1, "-Xptxas=-v")
+        print(" ".join(cmd))
+    subprocess.run(cmd, check=True)
+    return TARGET
+
+
+if __name__ == "__main__":
+    print(build(force="--force" in sys.argv, verbose="-v" in sys.argv))

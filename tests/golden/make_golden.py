@@ -1,0 +1,148 @@
+"""Regenerate the committed golden fixtures from the reference checkout.
+
+Run from the repository root, in a container where the reference is mounted:
+
+    python tests/golden/make_golden.py /root/reference
+
+It writes, under ``tests/golden/``:
+  - ``philox-v1/{blocks,streams,uniform}.tsv``: the reference's Random123 known-answer vectors,
+    copied byte for byte after checking each file's SHA-256 against the reference manifest;
+  - ``mla_upstream.npz``: the reference's pinned-Transformers MLA fixture cases
+    (``reference/tests/fixtures/transformers_mla_770e4c40_{core,glm_width}.json``), decoded to
+    float64 arrays: per case the query, latent rows, split key/value expansions, mask, scale and
+    the upstream SDPA output;
+  - ``paged_cases.npz``: paged bf16 cases whose inputs come from the seeded generator and whose
+    expected ``out``/``lse`` come from the reference's own ``mla_attention_core``, imported from
+    the checkout and called with identity key absorption and ``[I_512 | 0]`` value projection.
+Nothing at test time reads the reference checkout; the tests read only these files.
+"""
+
+import base64
+import hashlib
+import json
+import shutil
+import sys
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+sys.path.insert(0, str(HERE.parents[1]))
+
+from oracle import generate  # noqa: E402  (the generator's restatement defines the inputs)
+
+PAGED_CASES = {
+    # name: (seed, heads, kv_len list, queries per sequence, kv_format, pool pages or None)
+    "cfg1_decode_h16": (0, 16, [17, 64, 200, 1000], 1, "rope576", 64),
+    "mtp_h32": (4, 32, [65, 130], 2, "rope576", None),
+    "nope512_h32": (5, 32, [1, 63, 129], 1, "nope512", None),
+}
+
+
+def _array(record):
+    dtype = np.dtype(record["dtype"])
+    raw = base64.b64decode(record["b64"], validate=True)
+    return np.frombuffer(raw, dtype=dtype).reshape(tuple(record["shape"])).astype(
+        dtype.newbyteorder("=")
+    )
+
+
+def copy_philox(ref: Path):
+    src = ref / "tests/fixtures/philox-v1"
+    manifest = json.loads((src / "manifest.json").read_text())
+    dst = HERE / "philox-v1"
+    dst.mkdir(exist_ok=True)
+    for name, info in manifest["files"].items():
+        digest = hashlib.sha256((src / name).read_bytes()).hexdigest()
+        assert digest == info["sha256"], name
+        shutil.copyfile(src / name, dst / name)
+    (dst / "SHA256SUMS").write_text(
+        "".join(f"{info['sha256']}  {name}\n" for name, info in manifest["files"].items())
+    )
+
+
+def upstream_cases(ref: Path):
+    sys.path.insert(0, str(ref / "reference/src"))
+    from tq_reference import mla_attention
+
+    out = {}
+    for fixture in ("core", "glm_width"):
+        path = ref / f"reference/tests/fixtures/transformers_mla_770e4c40_{fixture}.json"
+        data = json.loads(path.read_text())
+        for case in data["cases"]:
+            dims = case["dims"]
+            w_uk, w_uv = mla_attention.split_kv_b(
+                _array(case["inputs"]["kv_b_proj_weight"]).astype(np.float64),
+                num_heads=dims["num_heads"],
+                qk_nope_head_dim=dims["qk_nope_head_dim"],
+                v_head_dim=dims["v_head_dim"],
+            )
+            scale = float(_array(case["scale"]["value"]).item())
+            q = _array(case["inputs"]["q"]).astype(np.float64)
+            latent = _array(case["inputs"]["latent"]).astype(np.float64)
+            mask = _array(case["upstream"]["mask"])
+            expected = _array(case["upstream"]["output"]).astype(np.float64)
+            for b in range(dims["batch"]):
+                key = f"{case['name']}_b{b}"
+                out[f"{key}__q"] = np.ascontiguousarray(q[b].transpose(1, 0, 2))
+                out[f"{key}__latent"] = np.ascontiguousarray(latent[b, 0])
+                out[f"{key}__w_uk"] = w_uk
+                out[f"{key}__w_uv"] = w_uv
+                out[f"{key}__mask"] = np.ascontiguousarray(mask[b, 0])
+                out[f"{key}__scale"] = np.array(scale)
+                out[f"{key}__expected"] = np.ascontiguousarray(expected[b])
+    np.savez_compressed(HERE / "mla_upstream.npz", **out)
+
+
+def paged_cases(ref: Path):
+    sys.path.insert(0, str(ref / "reference/src"))
+    from tq_reference import mla_attention
+
+    out = {}
+    for name, (seed, heads, lens, per_seq, fmt, pool) in PAGED_CASES.items():
+        width = 576 if fmt == "rope576" else 512
+        scale = 192 ** -0.5 if fmt == "rope576" else 0.0625
+        lens = np.array(lens, dtype=np.int64)
+        table, pool_pages = generate.page_tables(seed, lens, pool)
+        pool_bits = generate.kv_pool(seed, lens, table, pool_pages, width)
+        tokens = len(lens) * per_seq
+        q_bits = generate.queries(seed, tokens, heads, width)
+        seq_id = np.repeat(np.arange(len(lens)), per_seq).astype(np.int32)
+        q_pos = np.concatenate([lens[b] - per_seq + np.arange(per_seq) for b in range(len(lens))])
+        rows = generate.bf16_to_f64(pool_bits)
+        q = generate.bf16_to_f64(q_bits)
+        w_uk = np.broadcast_to(np.eye(width), (heads, width, width)).copy()
+        w_uv = np.broadcast_to(np.eye(512, width), (heads, 512, width)).copy()
+        exp_out = np.zeros((tokens, heads, 512))
+        exp_lse = np.zeros((tokens, heads))
+        for b in range(len(lens)):
+            pos = np.arange(lens[b])
+            latent = rows[table[b, pos // 64].astype(np.int64) * 64 + pos % 64]
+            t0 = b * per_seq
+            mask = np.zeros((per_seq, lens[b]), dtype=bool)
+            for i in range(per_seq):
+                mask[i, : q_pos[t0 + i] + 1] = True
+            res = mla_attention.mla_attention_core(
+                q[t0 : t0 + per_seq], latent, w_uk, w_uv, mask, scale=scale
+            )
+            exp_out[t0 : t0 + per_seq] = res.out
+            exp_lse[t0 : t0 + per_seq] = res.lse
+        out[f"{name}__meta"] = np.array([seed, heads, per_seq, width, pool_pages])
+        out[f"{name}__kv_len"] = lens
+        out[f"{name}__page_table"] = table
+        out[f"{name}__seq_id"] = seq_id
+        out[f"{name}__q_pos"] = q_pos.astype(np.int32)
+        out[f"{name}__scale"] = np.array(scale)
+        out[f"{name}__q_sha256"] = np.array(hashlib.sha256(q_bits.tobytes()).hexdigest())
+        out[f"{name}__pool_sha256"] = np.array(hashlib.sha256(pool_bits.tobytes()).hexdigest())
+        out[f"{name}__out"] = exp_out
+        out[f"{name}__lse"] = exp_lse
+    np.savez_compressed(HERE / "paged_cases.npz", **out)
+
+
+if __name__ == "__main__":
+    reference = Path(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    copy_philox(reference)
+    upstream_cases(reference)
+    paged_cases(reference)
+    print("golden fixtures written to", HERE)
