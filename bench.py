@@ -1,0 +1,424 @@
+"""Benchmark of the B200 paged-MLA attention path (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--config decode|mtp|prefill|longctx|cpu] [--cpu-sample S]
+
+A step is one launch of the attention path (scheduler, tcgen05 attention kernel, combine) over
+one batch of synthetic, seeded input already resident in HBM. The default workload is bf16 paged
+decode: 64 sequences x 1 query token, 128 heads, 576-wide latent+RoPE rows, 512-wide output,
+cached lengths uniform in [4096, 8192], 64-row pages from a permuted pool. The pool (~0.5 GB)
+exceeds L2 (126 MB), so every step reads its rows from HBM; no L2 flush is needed.
+
+With N ranks (torchrun, one GPU each) the job holds N x 64 sequences drawn from the same seeded
+stream and sharded by token count (weak scaling); there is no collective on the data path.
+``value`` is total query tokens / max-over-ranks device time. ``e2e`` is the same metric
+through the C ABI with the step's inputs (q, block tables, positions, lengths) copied from
+pinned host memory and the results (out, lse) copied back inside the timed region.
+``--impl reference`` times the reference's CPU algorithm (the oracle's float64 restatement of
+``mla_attention_core``; the reference itself is Python and is not present on the GPU host) on
+all host cores, on a bounded sample of the same workload, on rank 0 only.
+"""
+
+import argparse
+import json
+import math
+import multiprocessing as mp
+import os
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "tensorquay-engine_b200"))
+sys.path.insert(0, str(ROOT))
+
+METRIC = "MLA paged decode tokens/s"
+UNIT = "tokens/s"
+LAUNCHES_PER_STEP = 3  # scheduler + attention + combine
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d["hbm_gbs"], d["bf16_tflops"], d.get("bf16_tflops_sustained", d["bf16_tflops"]), \
+            "measured"
+    return 6650.0, 1590.0, 1400.0, "fallback"
+
+
+def workload_for(name, world, rank):
+    from tq_mla import inputs
+
+    if world == 1:
+        return inputs.config(name)
+    base = {"decode": 64, "mtp": 512, "prefill": 8, "longctx": 4, "cpu": 4}[name]
+    if name in ("cpu",):
+        return inputs.config(name)
+    full = inputs.config(name, batch=base * world)
+    return inputs.shard(full, world, rank)
+
+
+# ------------------------------------------------------------------------- clocks
+
+class ClockSampler:
+    def __init__(self, device_index, path):
+        self.path = path
+        self.proc = None
+        self.device_index = device_index
+
+    def __enter__(self):
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self.fh = open(self.path, "w")
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.device_index}", f"--query-gpu={q}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=self.fh, stderr=subprocess.DEVNULL)
+            time.sleep(0.3)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.fh.close()
+
+    def summary(self):
+        if self.proc is None or not Path(self.path).exists():
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in Path(self.path).read_text().splitlines():
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax.append(float(parts[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": max(smax),
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ------------------------------------------------------------------------- CPU leg
+
+def _cpu_worker(args):
+    """Time the oracle's float64 paged attention for a few sequences of a workload.
+
+    Inputs are regenerated here from the seed (untimed); the timed part is the gather through
+    the sequence's block table plus the attention, as the reference CPU path does per sequence.
+    """
+    os.environ.setdefault("OMP_NUM_THREADS", "1")
+    name, world, seqs = args
+    sys.path.insert(0, str(ROOT))
+    from oracle import generate as ogen, mla as omla
+    from tq_mla import inputs  # host metadata only (no device)
+
+    w = workload_for(name, world, 0) if world > 1 else inputs.config(name)
+    tok_global = np.concatenate([[0], np.cumsum(w.q_per_seq)[:-1]])
+    tok_off = np.concatenate([[0], np.cumsum(w.kv_len)[:-1]])
+    tokens = 0
+    elapsed = 0.0
+    for b in seqs:
+        n = int(w.kv_len[b])
+        t = int(w.q_per_seq[b])
+        rows = ogen.bf16_to_f64(ogen.normal_bf16(w.seed, ogen.STREAM_KV, int(tok_off[b]) * w.width,
+                                                 n * w.width)).reshape(n, w.width)
+        pages = (n + 63) // 64
+        perm = np.random.default_rng(b).permutation(pages)
+        pool = np.zeros((pages * 64, w.width))
+        pos = np.arange(n)
+        pool[perm[pos // 64] * 64 + pos % 64] = rows
+        table = perm[None, :].astype(np.int32)
+        q = ogen.bf16_to_f64(ogen.normal_bf16(w.seed, ogen.STREAM_Q,
+                                              int(tok_global[b]) * w.heads * w.width,
+                                              t * w.heads * w.width)).reshape(t, w.heads, w.width)
+        seq_id = np.zeros(t, np.int32)
+        q_pos = (w.prefix[b] + np.arange(t)).astype(np.int32)
+        t0 = time.perf_counter()
+        omla.paged_attention(q, pool, table, seq_id, q_pos, np.array([n]), scale=w.scale)
+        elapsed += time.perf_counter() - t0
+        tokens += t
+    return tokens, elapsed
+
+
+def cpu_baseline(name, world, budget_seqs=None, cores=None):
+    from tq_mla import inputs
+
+    w = inputs.config(name)
+    cores = cores or os.cpu_count() or 1
+    n_seq = budget_seqs or min(w.sequences, 64)
+    picks = np.linspace(0, w.sequences - 1, n_seq).astype(int)
+    chunks = [list(picks[i::cores]) for i in range(cores) if len(picks[i::cores])]
+    ctx = mp.get_context("spawn")
+    with ctx.Pool(len(chunks)) as pool:
+        res = pool.map(_cpu_worker, [(name, 1, c) for c in chunks])
+    tokens = sum(r[0] for r in res)
+    wall = max(r[1] for r in res)
+    return {
+        "value": tokens / wall if wall > 0 else None,
+        "unit": UNIT,
+        "cores": len(chunks),
+        "kind": "port",
+        "sample": f"{tokens} query tokens ({n_seq} of {w.sequences} sequences, spread over the "
+                  f"batch) of {w.name}; float64 oracle restatement of mla_attention_core with "
+                  f"block-table gather; {len(chunks)} spawn processes x 1 BLAS thread; "
+                  f"throughput = tokens / slowest process",
+        "seconds": wall,
+    }
+
+
+# ------------------------------------------------------------------------- reference arm
+
+def run_reference(args, world, rank):
+    if rank != 0:
+        return
+    cores = os.cpu_count() or 1
+    from tq_mla import inputs
+
+    w = inputs.config(args.config)
+    per_step = max(cores, 1)
+    picks_all = np.arange(w.sequences)
+    times, tokens = [], []
+    ctx = mp.get_context("spawn")
+    with ctx.Pool(cores) as pool:
+        for step in range(args.warmup + args.steps):
+            sample = np.roll(picks_all, -step * per_step)[:per_step]
+            chunks = [[int(s)] for s in sample]
+            t0 = time.perf_counter()
+            res = pool.map(_cpu_worker, [(args.config, 1, c) for c in chunks])
+            wall = time.perf_counter() - t0
+            if step >= args.warmup:
+                tok = sum(r[0] for r in res)
+                busy = max(r[1] for r in res)
+                times.append(busy)
+                tokens.append(tok)
+    value = sum(tokens) / sum(times)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT,
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1e3 * float(np.mean(times)), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
+        "config": {"workload": w.name, "heads": w.heads, "row_width": w.width,
+                   "sequences_per_step": per_step},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port",
+                         "sample": f"{per_step} sequences of {w.name} per step, one per spawn "
+                                   f"process (1 BLAS thread each); timed part = block-table "
+                                   f"gather + float64 attention per sequence"},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------------- our arm
+
+def traffic_from_profiles(workload_name):
+    p = ROOT / "profiles" / "ncu_traffic.txt"
+    if not p.exists():
+        return None
+    for line in p.read_text().splitlines():
+        kv = dict(x.split("=", 1) for x in line.split() if "=" in x)
+        if kv.get("workload") == workload_name and "dram_bytes_per_launch" in kv:
+            return float(kv["dram_bytes_per_launch"])
+    return None
+
+
+def run_ours(args, world, rank, local_rank):
+    import torch
+    import torch.distributed as dist
+    from tq_mla import inputs, ops
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    w = workload_for(args.config, world, rank)
+    batch = inputs.materialize(w, dev)
+    out = torch.empty((w.tokens, w.heads, 512), dtype=torch.bfloat16, device=dev)
+    lse = torch.empty((w.tokens, w.heads), dtype=torch.float32, device=dev)
+    launch = ops.MlaLaunch(batch.q, batch.kv, batch.page_table, batch.seq_id, batch.q_pos,
+                           batch.kv_len, out, lse, scale=w.scale,
+                           query_counts=batch.query_counts, prefill=args.config == "prefill")
+    stream = torch.cuda.current_stream(dev)
+
+    # Host copies for the end-to-end leg (pinned).
+    h_q = batch.q.cpu().pin_memory()
+    h_meta = [t.cpu().pin_memory() for t in (batch.page_table, batch.seq_id, batch.q_pos,
+                                             batch.kv_len)]
+    d_meta = [batch.page_table, batch.seq_id, batch.q_pos, batch.kv_len]
+    h_out = torch.empty_like(out, device="cpu").pin_memory()
+    h_lse = torch.empty_like(lse, device="cpu").pin_memory()
+    h2d = h_q.numel() * 2 + sum(t.numel() * t.element_size() for t in h_meta)
+    d2h = h_out.numel() * 2 + h_lse.numel() * 4
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def sum_over_ranks(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.SUM)
+        return float(t.item())
+
+    for _ in range(args.warmup):
+        launch(stream)
+    torch.cuda.synchronize(dev)
+    assert launch.device_error() == 0, "device error flag set during warm-up"
+
+    # ---- device-resident timing
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clock = ClockSampler(local_rank, str(ROOT / "gpurun_out" / f"clocks_rank{rank}.csv")) \
+        if (ROOT / "gpurun_out").exists() else ClockSampler(local_rank, f"/tmp/clocks{rank}.csv")
+    barrier()
+    torch.cuda.synchronize(dev)
+    with clock:
+        ev0.record(stream)
+        for _ in range(args.steps):
+            launch(stream)
+        ev1.record(stream)
+        torch.cuda.synchronize(dev)
+    barrier()
+    ms = ev0.elapsed_time(ev1)
+    ms_max = max_over_ranks(ms)
+    ms_step = ms_max / args.steps
+
+    # ---- end-to-end through the C ABI with host buffers
+    for _ in range(max(1, args.warmup)):
+        batch.q.copy_(h_q, non_blocking=True)
+        launch(stream)
+        h_out.copy_(out, non_blocking=True)
+    torch.cuda.synchronize(dev)
+    barrier()
+    torch.cuda.synchronize(dev)
+    ev0.record(stream)
+    for _ in range(args.steps):
+        batch.q.copy_(h_q, non_blocking=True)
+        for hd, dd in zip(h_meta, d_meta):
+            dd.copy_(hd, non_blocking=True)
+        launch(stream)
+        h_out.copy_(out, non_blocking=True)
+        h_lse.copy_(lse, non_blocking=True)
+    ev1.record(stream)
+    torch.cuda.synchronize(dev)
+    barrier()
+    e2e_ms = max_over_ranks(ev0.elapsed_time(ev1)) / args.steps
+    err = launch.device_error()
+
+    tokens_all = sum_over_ranks(float(w.tokens))
+    flops_all = sum_over_ranks(w.flops())
+    bytes_mine = w.bytes()
+    value = tokens_all / (ms_step * 1e-3)
+    e2e_value = tokens_all / (e2e_ms * 1e-3)
+    hbm, tc_burst, tc_sus, src = peaks()
+    # Dominant kernel: the attention kernel; its duration is bounded above by the step time
+    # (scheduler and combine included), so the fraction below is conservative.
+    ach_gbs = bytes_mine / (ms / args.steps * 1e-3) / 1e9
+    ach_tflops = w.flops() / (ms / args.steps * 1e-3) / 1e12
+    ai = w.flops() / bytes_mine
+    ridge = tc_burst * 1e12 / (hbm * 1e9)
+    bound = "hbm" if ai < ridge else "tensor"
+    traffic = traffic_from_profiles(w.name) if world == 1 else None
+    roofline = {
+        "bound": bound,
+        "achieved": ach_gbs if bound == "hbm" else ach_tflops,
+        "peak": hbm if bound == "hbm" else tc_burst,
+        "unit": "GB/s" if bound == "hbm" else "TFLOP/s",
+        "frac": (ach_gbs / hbm) if bound == "hbm" else (ach_tflops / tc_burst),
+        "traffic": traffic,
+        "peak_source": f"{src} (MEASURED_PEAKS.json)" if src == "measured" else "fallback",
+        "hbm_gbs": ach_gbs, "hbm_frac": ach_gbs / hbm,
+        "tflops": ach_tflops, "tensor_frac_burst": ach_tflops / tc_burst,
+        "tensor_frac_sustained": ach_tflops / tc_sus,
+        "roofline_time_us": 1e6 * max(bytes_mine / (hbm * 1e9), w.flops() / (tc_burst * 1e12)),
+        "roofline_frac": 1e6 * max(bytes_mine / (hbm * 1e9), w.flops() / (tc_burst * 1e12))
+        / (1e3 * ms / args.steps),
+        "algorithmic_bytes_per_launch": bytes_mine, "flops_per_launch": w.flops(),
+        "arithmetic_intensity": ai,
+    }
+    result = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {
+            "workload": w.name if world == 1 else f"{w.name} x{world} ranks (token-sharded)",
+            "sequences": int(sum_over_ranks(float(w.sequences))),
+            "query_tokens": int(tokens_all), "heads": w.heads, "row_width": w.width,
+            "value_width": 512, "page_rows": 64, "parallelism": f"sequence-shard x{world}",
+            "l2": "inputs larger than L2 (KV pool %.0f MB per GPU), no flush" %
+                  (w.pool_pages * 64 * w.width * 2 / 1e6),
+            "tflops_total": flops_all / (ms_step * 1e-3) / 1e12,
+        },
+        "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": int(h2d),
+                "d2h_bytes_per_step": int(d2h), "ms_per_step": e2e_ms},
+        "gpu_launches": LAUNCHES_PER_STEP * args.steps,
+        "roofline": roofline,
+        "clocks": clock.summary(),
+        "device_error_flags": err,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        result["cpu_baseline"] = cpu_baseline(args.config, world, args.cpu_sample)
+    if rank == 0:
+        print(json.dumps(result), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--config", default="decode",
+                    choices=["decode", "mtp", "prefill", "longctx", "cpu"])
+    ap.add_argument("--cpu-sample", type=int, default=None,
+                    help="sequences in the CPU baseline sample (default: up to 64)")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, world, rank)
+        return
+    if world > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local_rank))
+    try:
+        run_ours(args, world, rank, local_rank)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -321,13 +321,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     ptx::mbar_init(bar(kBarQEmpty), 1);
     for (int b = 0; b < 2; ++b) {
       ptx::mbar_init(bar(kBarSFull + b), 1);
-      ptx::mbar_init(bar(kBarSFree + b), kSoftmaxThreads);
-      ptx::mbar_init(bar(kBarPFull + b), kSoftmaxThreads);
+      ptx::mbar_init(bar(kBarSFree + b), kSoftmaxWarps);
+      ptx::mbar_init(bar(kBarPFull + b), kSoftmaxWarps);
       ptx::mbar_init(bar(kBarPvDone + b), 1);
     }
     ptx::mbar_init(bar(kBarOFull), 1);
-    ptx::mbar_init(bar(kBarOFree), kSoftmaxThreads);
-    for (int b = kBarXbFull; b <= kBarStFree; ++b) ptx::mbar_init(bar(b), kOwnedRows);
+    ptx::mbar_init(bar(kBarOFree), kSoftmaxWarps);
+    ptx::mbar_init(bar(kBarXbFull), kSoftmaxWarps);
+    ptx::mbar_init(bar(kBarXbFree), kSoftmaxWarps);
     ptx::mbar_init(bar(kBarDrain), 1);
     *abort_flag = 0;
     ptx::fence_mbar_init_cluster();
@@ -502,23 +503,19 @@ __global__ void __launch_bounds__(kThreads, 1)
     wt.drain(bar(kBarDrain), 0);
   } else {
     // ------------------------------------------------------------------ softmax + epilogue
+    // One thread per head row h (its TMEM lane). Per page: read this CTA's partial scores, send
+    // them to the peer, add the peer's partial scores, then an online softmax whose running
+    // maximum is raised only when it grows by more than 2^8 (exact after the final
+    // normalisation). Both CTAs compute identical statistics and probabilities.
     const int qd = warp & 3;
     const int h = 32 * qd + lane;
-    const bool owner = (qd >> 1) == int(rank);
-    const int orow = h - 64 * int(owner ? rank : peer);
     const uint32_t lane_base = uint32_t(32 * qd) << 16;
-    const uint32_t xb_local = base + kSmXbuf + orow * kXRowBytes;
-    const uint32_t pr_local = base + kSmPrx + orow * kPRowBytes;
-    const uint32_t st_local = base + kSmStats + orow * 8;
-    const uint32_t xb_remote = ptx::map_peer(xb_local, peer);
-    const uint32_t pr_remote = ptx::map_peer(pr_local, peer);
-    const uint32_t st_remote = ptx::map_peer(st_local, peer);
+    const uint32_t swz = uint32_t(h & 7);
+    const uint32_t xb_row = uint32_t(h) * kXRowBytes;
+    const uint32_t xb_remote = ptx::map_peer(base + kSmXbuf + xb_row, peer);
     const uint32_t xb_full_r = ptx::map_peer(bar(kBarXbFull), peer);
     const uint32_t xb_free_r = ptx::map_peer(bar(kBarXbFree), peer);
-    const uint32_t pr_full_r = ptx::map_peer(bar(kBarPrFull), peer);
-    const uint32_t pr_free_r = ptx::map_peer(bar(kBarPrFree), peer);
-    const uint32_t st_full_r = ptx::map_peer(bar(kBarStFull), peer);
-    const uint32_t st_free_r = ptx::map_peer(bar(kBarStFree), peer);
+    const float4* xb_local = reinterpret_cast<const float4*>(sm + kSmXbuf + xb_row);
     const float c2 = a.scale_log2;
     uint32_t it = 0, useq = 0;
     Seg s;
@@ -529,88 +526,68 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int j = 0; j < s.np; ++j) {
         const uint32_t itq = it + j, sb = itq & 1u;
         const int valid = min(kPageRows, n - (s.p0 + j) * kPageRows);
-        wt.where = ((owner ? 4 : 3) << 24) | int(itq & 0xFFFFFF);
+        wt.where = (3 << 24) | int(itq & 0xFFFFFF);
         if (!wt.wait<false>(bar(kBarSFull + sb), (itq >> 1) & 1u)) { ok = false; break; }
         __syncwarp();
         ptx::tc_fence_after();
         uint32_t sr[64];
         {
-          uint32_t(&r0)[16] = *reinterpret_cast<uint32_t(*)[16]>(&sr[0]);
-          uint32_t(&r1)[16] = *reinterpret_cast<uint32_t(*)[16]>(&sr[16]);
-          uint32_t(&r2)[16] = *reinterpret_cast<uint32_t(*)[16]>(&sr[32]);
-          uint32_t(&r3)[16] = *reinterpret_cast<uint32_t(*)[16]>(&sr[48]);
           const uint32_t t = tmem + lane_base + kTmemS + sb * 64;
-          ptx::tmem_ld16(t, r0);
-          ptx::tmem_ld16(t + 16, r1);
-          ptx::tmem_ld16(t + 32, r2);
-          ptx::tmem_ld16(t + 48, r3);
+          ptx::tmem_ld16(t, *reinterpret_cast<uint32_t(*)[16]>(&sr[0]));
+          ptx::tmem_ld16(t + 16, *reinterpret_cast<uint32_t(*)[16]>(&sr[16]));
+          ptx::tmem_ld16(t + 32, *reinterpret_cast<uint32_t(*)[16]>(&sr[32]));
+          ptx::tmem_ld16(t + 48, *reinterpret_cast<uint32_t(*)[16]>(&sr[48]));
           ptx::tmem_wait_ld();
         }
         ptx::tc_fence_before();
-        ptx::mbar_arrive(bar(kBarSFree + sb));
-        uint32_t pk[32];
-        float corr = 1.f;
-        if (!owner) {
-          if (!wt.wait<true>(bar(kBarXbFree), (itq & 1u) ^ 1u)) { ok = false; break; }
+        __syncwarp();
+        if (lane == 0) ptx::mbar_arrive(bar(kBarSFree + sb));
+        // Send this CTA's partial scores once the peer has read the previous page's.
+        if (!wt.wait<true>(bar(kBarXbFree), (itq & 1u) ^ 1u)) { ok = false; break; }
 #pragma unroll
-          for (int k = 0; k < 16; ++k)
-            ptx::st_cluster_v4(xb_remote + 16 * k, sr[4 * k], sr[4 * k + 1], sr[4 * k + 2],
-                               sr[4 * k + 3]);
-          ptx::mbar_arrive_cluster(xb_full_r);
-          if (!wt.wait<true>(bar(kBarPrFull), itq & 1u)) { ok = false; break; }
-          const uint4* src = reinterpret_cast<const uint4*>(sm + kSmPrx + orow * kPRowBytes);
+        for (int k = 0; k < 16; ++k)
+          ptx::st_cluster_v4(xb_remote + ((uint32_t(k) ^ swz) << 4), sr[4 * k], sr[4 * k + 1],
+                             sr[4 * k + 2], sr[4 * k + 3]);
+        __syncwarp();
+        if (lane == 0) ptx::mbar_arrive_cluster(xb_full_r);
+        if (!wt.wait<true>(bar(kBarXbFull), itq & 1u)) { ok = false; break; }
+        float sv[64];
 #pragma unroll
-          for (int k = 0; k < 8; ++k) {
-            const uint4 v = src[k];
-            pk[4 * k] = v.x; pk[4 * k + 1] = v.y; pk[4 * k + 2] = v.z; pk[4 * k + 3] = v.w;
-          }
-          corr = *reinterpret_cast<const float*>(sm + kSmPrx + orow * kPRowBytes + 128);
-          ptx::mbar_arrive_cluster(pr_free_r);
-        } else {
-          if (!wt.wait<true>(bar(kBarXbFull), itq & 1u)) { ok = false; break; }
-          const float4* xs = reinterpret_cast<const float4*>(sm + kSmXbuf + orow * kXRowBytes);
-          float sv[64];
-#pragma unroll
-          for (int k = 0; k < 16; ++k) {
-            const float4 v = xs[k];
-            sv[4 * k] = __uint_as_float(sr[4 * k]) + v.x;
-            sv[4 * k + 1] = __uint_as_float(sr[4 * k + 1]) + v.y;
-            sv[4 * k + 2] = __uint_as_float(sr[4 * k + 2]) + v.z;
-            sv[4 * k + 3] = __uint_as_float(sr[4 * k + 3]) + v.w;
-          }
-          ptx::mbar_arrive_cluster(xb_free_r);
-          float mx = -INFINITY;
-#pragma unroll
-          for (int i = 0; i < 64; ++i) {
-            sv[i] = i < valid ? sv[i] * c2 : -INFINITY;
-            mx = fmaxf(mx, sv[i]);
-          }
-          if (j == 0) {
-            m_used = mx;
-          } else if (mx > m_used + kRescaleThreshold) {
-            corr = ptx::ex2(m_used - mx);
-            m_used = mx;
-            l *= corr;
-          }
-          // The row sum uses the f32 probabilities (softmax in f32); only the PV operand is
-          // rounded to bf16 (docs/TEST-PLAN.md:61-63).
-          float sum0 = 0.f, sum1 = 0.f;
-#pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const float p0 = ptx::ex2(sv[2 * i] - m_used), p1 = ptx::ex2(sv[2 * i + 1] - m_used);
-            pk[i] = ptx::pack_bf16x2(p0, p1);
-            sum0 += p0;
-            sum1 += p1;
-          }
-          l += sum0 + sum1;
-          if (!wt.wait<true>(bar(kBarPrFree), (itq & 1u) ^ 1u)) { ok = false; break; }
-#pragma unroll
-          for (int k = 0; k < 8; ++k)
-            ptx::st_cluster_v4(pr_remote + 16 * k, pk[4 * k], pk[4 * k + 1], pk[4 * k + 2],
-                               pk[4 * k + 3]);
-          ptx::st_cluster_u32(pr_remote + 128, __float_as_uint(corr));
-          ptx::mbar_arrive_cluster(pr_full_r);
+        for (int k = 0; k < 16; ++k) {
+          const float4 v = xb_local[k ^ int(swz)];
+          sv[4 * k] = __uint_as_float(sr[4 * k]) + v.x;
+          sv[4 * k + 1] = __uint_as_float(sr[4 * k + 1]) + v.y;
+          sv[4 * k + 2] = __uint_as_float(sr[4 * k + 2]) + v.z;
+          sv[4 * k + 3] = __uint_as_float(sr[4 * k + 3]) + v.w;
         }
+        __syncwarp();
+        if (lane == 0) ptx::mbar_arrive_cluster(xb_free_r);
+        float mx = -INFINITY;
+#pragma unroll
+        for (int i = 0; i < 64; ++i) {
+          sv[i] = i < valid ? sv[i] * c2 : -INFINITY;
+          mx = fmaxf(mx, sv[i]);
+        }
+        float corr = 1.f;
+        if (j == 0) {
+          m_used = mx;
+        } else if (mx > m_used + kRescaleThreshold) {
+          corr = ptx::ex2(m_used - mx);
+          m_used = mx;
+          l *= corr;
+        }
+        // The row sum uses the f32 probabilities (softmax in f32); only the PV operand is
+        // rounded to bf16 (docs/TEST-PLAN.md:61-63).
+        uint32_t pk[32];
+        float sum0 = 0.f, sum1 = 0.f;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const float p0 = ptx::ex2(sv[2 * i] - m_used), p1 = ptx::ex2(sv[2 * i + 1] - m_used);
+          pk[i] = ptx::pack_bf16x2(p0, p1);
+          sum0 += p0;
+          sum1 += p1;
+        }
+        l += sum0 + sum1;
         // The running maximum moved for some row of this warp: rescale those rows of O once
         // PV(itq-1) has landed. The decision is per lane but tcgen05.ld/st are warp-collective,
         // so the whole warp takes the branch (a factor of exactly 1 leaves a row unchanged).
@@ -642,31 +619,21 @@ __global__ void __launch_bounds__(kThreads, 1)
           ptx::tmem_wait_st();
         }
         ptx::tc_fence_before();
-        ptx::mbar_arrive(bar(kBarPFull + sb));
+        __syncwarp();
+        if (lane == 0) ptx::mbar_arrive(bar(kBarPFull + sb));
       }
       if (!ok) break;
       // Epilogue: normalise this CTA's half of O and write it.
-      wt.where = ((owner ? 6 : 5) << 24) | int(useq & 0xFFFFFF);
+      wt.where = (5 << 24) | int(useq & 0xFFFFFF);
       if (!wt.wait<false>(bar(kBarOFull), useq & 1u)) break;
       __syncwarp();
       ptx::tc_fence_after();
-      float inv_l;
-      if (owner) {
-        inv_l = 1.f / l;
+      const float inv_l = 1.f / l;
+      if (rank == 0 && h < a.heads) {
         const float lse = (m_used + log2f(l)) * kLn2;
-        if (!wt.wait<true>(bar(kBarStFree), (useq & 1u) ^ 1u)) break;
-        ptx::st_cluster_v2(st_remote, __float_as_uint(inv_l), __float_as_uint(lse));
-        ptx::mbar_arrive_cluster(st_full_r);
-        if (h < a.heads) {
-          if (s.slot >= 0) meta.part_lse[(long long)s.slot * kHeadsTile + h] = lse;
-          else a.lse[(long long)s.u * a.heads + h] = lse;
-        }
-      } else {
-        if (!wt.wait<true>(bar(kBarStFull), useq & 1u)) break;
-        inv_l = *reinterpret_cast<const float*>(sm + kSmStats + orow * 8);
-        ptx::mbar_arrive_cluster(st_free_r);
+        if (s.slot >= 0) meta.part_lse[(long long)s.slot * kHeadsTile + h] = lse;
+        else a.lse[(long long)s.u * a.heads + h] = lse;
       }
-      __syncwarp();
       const int col0 = kValueHalf * int(rank);
       for (int c = 0; c < kValueHalf; c += 32) {
         uint32_t v[32];
@@ -705,7 +672,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       ptx::tc_fence_before();
-      ptx::mbar_arrive(bar(kBarOFree));
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(bar(kBarOFree));
       it += s.np;
       ++useq;
     }
@@ -735,46 +703,66 @@ __device__ __forceinline__ void store8(char* base, int f32, const float (&v)[8])
   }
 }
 
+// Grid: kCombineBlocksPerJob blocks per possible split token (2 x pairs of them, an upper bound
+// that does not depend on the data). Block b merges heads [16 g, 16 g + 16), g = b % 8, of split
+// token b / 8: one warp per head row, 16 value dims per lane. Blocks without a split token
+// zero-fill the tokens that see no key.
+constexpr int kCombineBlocksPerJob = 8;
+
 __global__ void __launch_bounds__(256) combine_kernel(Meta m, char* out, long long st_t,
                                                       long long st_h, int out_f32, float* lse,
                                                       int heads) {
   const int ncomb = m.header[kHdrNumCombine], nempty = m.header[kHdrNumEmpty];
   const int esize = out_f32 ? 4 : 2;
-  for (int job = blockIdx.x; job < ncomb + nempty; job += gridDim.x) {
-    if (job < ncomb) {
-      const int u = m.combine_list[job];
-      const int ns = m.unit_nsplit[u], off = m.unit_split_off[u];
-      for (int task = threadIdx.x; task < heads * 64; task += blockDim.x) {
-        const int h = task >> 6, d0 = (task & 63) * 8;
-        float mx = -INFINITY;
-        for (int i = 0; i < ns; ++i) mx = fmaxf(mx, m.part_lse[(long long)(off + i) * kHeadsTile + h]);
-        float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-        float wsum = 0.f;
-        for (int i = 0; i < ns; ++i) {
-          const float li = m.part_lse[(long long)(off + i) * kHeadsTile + h];
-          const float w = li == -INFINITY ? 0.f : expf(li - mx);
-          wsum += w;
-          const float4* src = reinterpret_cast<const float4*>(
-              m.part_out + ((long long)(off + i) * kHeadsTile + h) * kValueDim + d0);
-          const float4 x0 = src[0], x1 = src[1];
-          acc[0] += w * x0.x; acc[1] += w * x0.y; acc[2] += w * x0.z; acc[3] += w * x0.w;
-          acc[4] += w * x1.x; acc[5] += w * x1.y; acc[6] += w * x1.z; acc[7] += w * x1.w;
-        }
-        const float inv = wsum > 0.f ? 1.f / wsum : 0.f;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int job = blockIdx.x / kCombineBlocksPerJob, group = blockIdx.x % kCombineBlocksPerJob;
+  if (job < ncomb) {
+    const int u = m.combine_list[job];
+    const int ns = m.unit_nsplit[u], off = m.unit_split_off[u];
+    for (int h = group * 16 + warp; h < min(heads, group * 16 + 16); h += 8) {
+      float mx = -INFINITY;
+      for (int i = 0; i < ns; ++i) mx = fmaxf(mx, m.part_lse[(long long)(off + i) * kHeadsTile + h]);
+      float acc[16];
 #pragma unroll
-        for (int k = 0; k < 8; ++k) acc[k] *= inv;
-        store8(out + u * st_t + h * st_h + (long long)d0 * esize, out_f32, acc);
-        if (d0 == 0) lse[(long long)u * heads + h] = wsum > 0.f ? mx + logf(wsum) : -INFINITY;
+      for (int k = 0; k < 16; ++k) acc[k] = 0.f;
+      float wsum = 0.f;
+      for (int i = 0; i < ns; ++i) {
+        const float li = m.part_lse[(long long)(off + i) * kHeadsTile + h];
+        const float w = li == -INFINITY ? 0.f : expf(li - mx);
+        wsum += w;
+        const float4* src = reinterpret_cast<const float4*>(
+            m.part_out + ((long long)(off + i) * kHeadsTile + h) * kValueDim + lane * 16);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const float4 x = src[k];
+          acc[4 * k] += w * x.x;
+          acc[4 * k + 1] += w * x.y;
+          acc[4 * k + 2] += w * x.z;
+          acc[4 * k + 3] += w * x.w;
+        }
       }
-    } else {
-      const int u = m.empty_list[job - ncomb];
-      const float z[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-      for (int task = threadIdx.x; task < heads * 64; task += blockDim.x) {
-        const int h = task >> 6, d0 = (task & 63) * 8;
-        store8(out + u * st_t + h * st_h + (long long)d0 * esize, out_f32, z);
-        if (d0 == 0) lse[(long long)u * heads + h] = -INFINITY;
+      const float inv = wsum > 0.f ? 1.f / wsum : 0.f;
+      float lo[8], hi[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        lo[k] = acc[k] * inv;
+        hi[k] = acc[8 + k] * inv;
       }
+      char* dst = out + u * st_t + h * st_h + (long long)(lane * 16) * esize;
+      store8(dst, out_f32, lo);
+      store8(dst + 8 * esize, out_f32, hi);
+      if (lane == 0) lse[(long long)u * heads + h] = wsum > 0.f ? mx + logf(wsum) : -INFINITY;
     }
+  }
+  // Tokens with no visible key: zeros and lse = -inf, spread over every block.
+  const float z[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  const long long tasks = (long long)nempty * heads * 64;
+  for (long long t = blockIdx.x * 256ll + threadIdx.x; t < tasks; t += (long long)gridDim.x * 256) {
+    const int e = int(t / (heads * 64));
+    const int rem = int(t % (heads * 64));
+    const int u = m.empty_list[e], h = rem >> 6, d0 = (rem & 63) * 8;
+    store8(out + u * st_t + h * st_h + (long long)d0 * esize, out_f32, z);
+    if (d0 == 0) lse[(long long)u * heads + h] = -INFINITY;
   }
 }
 
@@ -1110,9 +1098,7 @@ int32_t launch(const TqMlaParams* params, void* workspace, uint64_t workspace_by
                                               tkv_rope, a);
     if (e != cudaSuccess) return set_err(err, "launch", TQ_ERR_CUDA);
   }
-  int sms = 0;
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
-  combine_kernel<<<sms > 0 ? sms : 148, 256, 0, st>>>(
+  combine_kernel<<<2 * pairs * kCombineBlocksPerJob, 256, 0, st>>>(
       m, reinterpret_cast<char*>(s.out.device_address), (long long)s.out.strides_bytes[0],
       (long long)s.out.strides_bytes[1], s.out.dtype == TQ_DTYPE_F32,
       reinterpret_cast<float*>(s.lse.device_address), H);

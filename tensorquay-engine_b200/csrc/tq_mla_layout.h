@@ -4,10 +4,11 @@
 // range of 64-row KV pages. CTA rank r owns
 //   - the K-slice of QK^T: dims [256r, 256r+256) of the latent part, plus dims [512+32r, +32) of
 //     the RoPE part for 576-wide rows;
-//   - the V-slice of PV and of the output: dims [256r, 256r+256);
-//   - the softmax of heads [64r, 64r+64).
-// The two partial score tiles are summed through distributed shared memory, and the owner of a
-// head sends its bf16 probabilities to the peer, so both halves of O see the same P.
+//   - the V-slice of PV and of the output: dims [256r, 256r+256).
+// Each CTA sends its partial score tile (all 128 heads) to the peer through distributed shared
+// memory and adds the peer's tile to its own. f32 addition is commutative, so both CTAs hold
+// bit-identical scores and compute bit-identical softmax statistics and probabilities; each then
+// runs PV for its half of the value dimension.
 #pragma once
 
 #include <cstdint>
@@ -22,7 +23,7 @@ constexpr int kValueHalf = 256;  // per CTA
 constexpr int kStages = 3;
 constexpr int kThreads = 192;    // warp 0 TMA, warp 1 MMA, warps 2-5 softmax/epilogue
 constexpr int kSoftmaxThreads = 128;
-constexpr int kOwnedRows = 64;
+constexpr int kSoftmaxWarps = 4;
 
 // Shared memory (byte offsets from a 1024-aligned base).
 constexpr uint32_t kSmQMain = 0;             // 4 chunks x [128 rows x 128 B], 128B swizzle
@@ -33,18 +34,17 @@ constexpr uint32_t kKvChunkBytes = 8192;     // [64 rows x 128 B]
 constexpr uint32_t kKvRopeOffset = 32768;    // [64 rows x 64 B] inside a stage
 constexpr uint32_t kKvRopeBytes = 4096;
 constexpr uint32_t kStageBytes = 36864;
-constexpr uint32_t kSmXbuf = kSmKv + kStages * kStageBytes;  // peer partial scores, f32
-constexpr uint32_t kXRowBytes = 272;                         // 256 B + 16 B pad (bank spread)
-constexpr uint32_t kSmPrx = kSmXbuf + kOwnedRows * kXRowBytes;  // peer probabilities, bf16
-constexpr uint32_t kPRowBytes = 144;                            // 128 B P + f32 correction + pad
-constexpr uint32_t kSmStats = kSmPrx + kOwnedRows * kPRowBytes; // peer (1/l, lse)
-constexpr uint32_t kSmBars = kSmStats + kOwnedRows * 8;
-constexpr int kNumBars = 25;
+// Peer partial scores, f32 [128 rows x 64 keys]; 16-byte chunk k of row h is stored at chunk
+// k ^ (h & 7) so that eight consecutive rows read eight different bank groups.
+constexpr uint32_t kSmXbuf = kSmKv + kStages * kStageBytes;
+constexpr uint32_t kXRowBytes = 256;
+constexpr uint32_t kSmBars = kSmXbuf + kHeadsTile * kXRowBytes;
+constexpr int kNumBars = 21;
 constexpr uint32_t kSmMisc = kSmBars + kNumBars * 8;  // tmem base holder, abort flag
 constexpr uint32_t kSmUsed = kSmMisc + 16;
 constexpr uint32_t kSmBytes = kSmUsed + 1024;          // slack for 1024-byte alignment
 
-static_assert(kSmXbuf % 16 == 0 && kSmPrx % 16 == 0 && kSmStats % 16 == 0, "alignment");
+static_assert(kSmXbuf % 1024 == 0, "alignment");
 static_assert(kSmBars % 8 == 0, "mbarrier alignment");
 static_assert(kSmBytes <= 232448, "shared memory per CTA");
 
@@ -55,17 +55,13 @@ enum Bar : int {
   kBarQFull = kBarKvEmpty + kStages,
   kBarQEmpty,
   kBarSFull,                       // [2]
-  kBarSFree = kBarSFull + 2,       // [2], 128 arrivals
-  kBarPFull = kBarSFree + 2,       // [2], 128 arrivals
+  kBarSFree = kBarSFull + 2,       // [2], one arrival per softmax warp
+  kBarPFull = kBarSFree + 2,       // [2], one arrival per softmax warp
   kBarPvDone = kBarPFull + 2,      // [2]
   kBarOFull = kBarPvDone + 2,
-  kBarOFree,                       // 128 arrivals
-  kBarXbFull,                      // 64 remote arrivals: peer partial scores landed
-  kBarXbFree,                      // 64 remote arrivals: peer consumed my partial scores
-  kBarPrFull,                      // 64 remote arrivals: peer probabilities landed
-  kBarPrFree,                      // 64 remote arrivals: peer consumed my probabilities
-  kBarStFull,                      // 64 remote arrivals: peer row statistics landed
-  kBarStFree,                      // 64 remote arrivals: peer consumed my statistics
+  kBarOFree,                       // one arrival per softmax warp
+  kBarXbFull,                      // one remote arrival per peer softmax warp: its scores landed
+  kBarXbFree,                      // one remote arrival per peer softmax warp: it read my scores
   kBarDrain,
   kBarCount
 };

@@ -18,7 +18,6 @@ import ctypes
 from dataclasses import dataclass, field
 
 import numpy as np
-import torch
 
 from ._abi import lib, raise_for
 
@@ -196,17 +195,19 @@ def shard(w: Workload, ranks: int, rank: int) -> Workload:
 
 @dataclass
 class DeviceBatch:
-    q: torch.Tensor
-    kv: torch.Tensor
-    page_table: torch.Tensor
-    seq_id: torch.Tensor
-    q_pos: torch.Tensor
-    kv_len: torch.Tensor
+    q: "torch.Tensor"
+    kv: "torch.Tensor"
+    page_table: "torch.Tensor"
+    seq_id: "torch.Tensor"
+    q_pos: "torch.Tensor"
+    kv_len: "torch.Tensor"
     query_counts: list
 
 
 def materialize(w: Workload, device, *, row_stride=None, q_seed=None):
     """Allocate and fill the device tensors of ``w`` with the seeded generator."""
+    import torch
+
     dev = torch.device(device)
     stream = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
     width = w.width
