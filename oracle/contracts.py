@@ -19,6 +19,7 @@ the reference's rules for its own format):
   - the softmax scale stays the exact GLM constant ``0.0625`` for the reference's 512-wide
     formats and is any finite positive ``f32`` for ``BF16_ROPE576``;
   - no sparse ``idx``/``k_len`` tensors (dense attention over ``[0, min(kv_len, q_pos+1))``);
+  - ``out`` may be f32 (a partial result that a later log-sum-exp merge combines);
   - a prefill plan (``max_per_seq=None``) lifts the 4-queries-per-sequence decode limit.
 """
 
@@ -177,14 +178,14 @@ def _check_aliases(inputs, outputs):
 
 
 def _scale_ok(spec):
-    bits = struct.unpack("<I", struct.pack("<f", spec.scale))[0] if math.isfinite(spec.scale) \
-        else None
+    """The scale as the f32 the C ABI carries (out-of-range values become infinities)."""
+    import numpy as np
+
+    with np.errstate(over="ignore"):
+        f32 = np.float32(spec.scale)
     if spec.kv_format in (KV_BF16, KV_FP8_E4M3):
-        return bits == GLM_SCALE_BITS
-    if not math.isfinite(spec.scale) or spec.scale <= 0:
-        return False
-    f32 = struct.unpack("<f", struct.pack("<f", spec.scale))[0]
-    return math.isfinite(f32) and f32 > 0
+        return bool(np.isfinite(f32)) and int(f32.view(np.uint32)) == GLM_SCALE_BITS
+    return bool(np.isfinite(f32)) and float(f32) > 0
 
 
 def validate(spec: Spec, query_counts, max_per_seq=MAX_DECODE_QUERIES):
@@ -211,7 +212,8 @@ def validate(spec: Spec, query_counts, max_per_seq=MAX_DECODE_QUERIES):
         _check("kv_len", spec.kv_len, [sequences], I32, "packed", launching),
     ]
     outputs = [
-        _check("out", spec.out, [tokens, heads, V_WIDTH], BF16, "padded", launching),
+        _check("out", spec.out, [tokens, heads, V_WIDTH], F32 if spec.out.dtype == F32 else BF16,
+               "padded", launching),
         _check("lse", spec.lse, [tokens, heads], F32, "packed", launching),
     ]
     if len(query_counts) != sequences:

@@ -167,16 +167,20 @@ def paged_attention(q, pool_rows, page_table, seq_id, q_pos, kv_len, *, scale, v
 
 
 def combine_partials(partial_out, partial_lse):
-    """Log-sum-exp merge of split results: ``partial_out [k,H,Dv]``, ``partial_lse [k,H]``.
+    """Log-sum-exp merge of split results along axis 0.
 
-    An all ``-inf`` column yields zeros and ``-inf`` with no NaN.
+    ``partial_out [k, ..., Dv]`` holds outputs normalised over each part and ``partial_lse
+    [k, ...]`` their natural-log lse. A row whose parts are all ``-inf`` yields zeros and
+    ``-inf`` with no NaN.
     """
     m = partial_lse.max(axis=0)
     finite = np.isfinite(m)
     safe_m = np.where(finite, m, 0.0)
-    w = np.where(np.isfinite(partial_lse), np.exp(partial_lse - safe_m), 0.0)
+    with np.errstate(invalid="ignore", over="ignore"):
+        w = np.where(np.isfinite(partial_lse), np.exp(partial_lse - safe_m), 0.0)
     total = w.sum(axis=0)
-    out = np.where(total[:, None] > 0, (w[:, :, None] * partial_out).sum(0) /
-                   np.where(total > 0, total, 1.0)[:, None], 0.0)
-    lse = np.where(total > 0, safe_m + np.log(np.where(total > 0, total, 1.0)), -np.inf)
+    denom = np.where(total > 0, total, 1.0)
+    out = np.where((total > 0)[..., None], (w[..., None] * partial_out).sum(0) / denom[..., None],
+                   0.0)
+    lse = np.where(total > 0, safe_m + np.log(denom), -np.inf)
     return out, lse
