@@ -62,6 +62,9 @@ struct Meta {
 
 struct MainArgs {
   Meta meta;
+  const char* q;
+  long long q_stride_t;
+  long long q_stride_h;
   const int* page_table;
   const int* seq_id;
   long long slots;
@@ -295,8 +298,7 @@ struct Waiter {
 
 template <bool kRope>
 __global__ void __launch_bounds__(kThreads, 1)
-    mla_paged_kernel(const __grid_constant__ CUtensorMap tm_q,
-                     const __grid_constant__ CUtensorMap tm_q_rope,
+    mla_paged_kernel(const __grid_constant__ CUtensorMap tm_q_rope,
                      const __grid_constant__ CUtensorMap tm_kv,
                      const __grid_constant__ CUtensorMap tm_kv_rope, const MainArgs a) {
   extern __shared__ uint8_t smem_raw[];
@@ -317,40 +319,37 @@ __global__ void __launch_bounds__(kThreads, 1)
       ptx::mbar_init(bar(kBarKvFull + s), 1);
       ptx::mbar_init(bar(kBarKvEmpty + s), 1);
     }
-    ptx::mbar_init(bar(kBarQFull), 1);
+    ptx::mbar_init(bar(kBarQRopeFull), 1);
+    ptx::mbar_init(bar(kBarQTmemFull), 4);
     ptx::mbar_init(bar(kBarQEmpty), 1);
     for (int b = 0; b < 2; ++b) {
       ptx::mbar_init(bar(kBarSFull + b), 1);
-      ptx::mbar_init(bar(kBarSFree + b), kSoftmaxWarps);
       ptx::mbar_init(bar(kBarPFull + b), kSoftmaxWarps);
       ptx::mbar_init(bar(kBarPvDone + b), 1);
+      ptx::mbar_init(bar(kBarXbFull + b), 1);
+      ptx::mbar_init(bar(kBarXbFree + b), kSoftmaxWarps);
+      ptx::mbar_init(bar(kBarRowMax + b), kSoftmaxWarps);
     }
     ptx::mbar_init(bar(kBarOFull), 1);
     ptx::mbar_init(bar(kBarOFree), kSoftmaxWarps);
-    ptx::mbar_init(bar(kBarXbFull), kSoftmaxWarps);
-    ptx::mbar_init(bar(kBarXbFree), kSoftmaxWarps);
+    ptx::mbar_init(bar(kBarRowSum), kSoftmaxWarps);
     ptx::mbar_init(bar(kBarDrain), 1);
+    // The receive tiles of pages 0 and 1 expect the peer's 32 KB each.
+    ptx::mbar_expect_tx(bar(kBarXbFull + 0), kTileBytes);
+    ptx::mbar_expect_tx(bar(kBarXbFull + 1), kTileBytes);
     *abort_flag = 0;
     ptx::fence_mbar_init_cluster();
-    ptx::tma_prefetch_desc(&tm_q);
     ptx::tma_prefetch_desc(&tm_kv);
     if (kRope) {
       ptx::tma_prefetch_desc(&tm_q_rope);
       ptx::tma_prefetch_desc(&tm_kv_rope);
     }
   }
-  // Query rows past the head count stay zero for the whole kernel (TMA writes rows < heads).
-  if (a.heads < kHeadsTile) {
-    const int rows = kHeadsTile - a.heads;
-    const int main_words = rows * 128 / 16, rope_words = rows * 64 / 16;
-    for (int i = threadIdx.x; i < 4 * main_words; i += kThreads) {
-      const int chunk = i / main_words, w = i % main_words;
-      reinterpret_cast<uint4*>(sm + kSmQMain + chunk * kQChunkBytes + a.heads * 128)[w] =
-          make_uint4(0, 0, 0, 0);
-    }
-    if (kRope)
-      for (int i = threadIdx.x; i < rope_words; i += kThreads)
-        reinterpret_cast<uint4*>(sm + kSmQRope + a.heads * 64)[i] = make_uint4(0, 0, 0, 0);
+  // RoPE query rows past the head count stay zero for the whole kernel (TMA writes rows < heads).
+  if (kRope && a.heads < kHeadsTile) {
+    const int words = (kHeadsTile - a.heads) * 64 / 16;
+    for (int i = threadIdx.x; i < words; i += kThreads)
+      reinterpret_cast<uint4*>(sm + kSmQRope + a.heads * 64)[i] = make_uint4(0, 0, 0, 0);
     ptx::fence_proxy_async_smem();
   }
   if (warp == 1) {
@@ -372,20 +371,17 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0) {
     // ------------------------------------------------------------------ TMA producer
     if (lane == 0) {
-      const uint32_t q_bytes = uint32_t(a.heads) * (kRope ? (256 + 32) * 2 : 256 * 2);
       const uint32_t stage_bytes = kRope ? kStageBytes : 4 * kKvChunkBytes;
       uint32_t it = 0, useq = 0;
       Seg s;
       bool ok = true;
       while (ok && walker.next(meta, s)) {
         wt.where = (1 << 24) | int(it & 0xFFFFFF);
-        if (!wt.wait<false>(bar(kBarQEmpty), (useq & 1u) ^ 1u)) break;
-        ptx::mbar_expect_tx(bar(kBarQFull), q_bytes);
-        for (int k = 0; k < 4; ++k)
-          ptx::tma_load_3d(base + kSmQMain + k * kQChunkBytes, &tm_q, bar(kBarQFull),
-                           k_main0 + 64 * k, 0, s.u);
-        if (kRope)
-          ptx::tma_load_3d(base + kSmQRope, &tm_q_rope, bar(kBarQFull), k_rope0, 0, s.u);
+        if (kRope) {
+          if (!wt.wait<false>(bar(kBarQEmpty), (useq & 1u) ^ 1u)) break;
+          ptx::mbar_expect_tx(bar(kBarQRopeFull), uint32_t(a.heads) * 64);
+          ptx::tma_load_3d(base + kSmQRope, &tm_q_rope, bar(kBarQRopeFull), k_rope0, 0, s.u);
+        }
         ++useq;
         const int* pt = a.page_table + (long long)a.seq_id[s.u] * a.slots;
         for (int j = 0; j < s.np; ++j, ++it) {
@@ -416,10 +412,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t last = it - 1 - ((it - 1 - st) % kStages);
         wt.drain(bar(kBarKvFull + st), (last / kStages) & 1u);
       }
-      if (useq) wt.drain(bar(kBarQFull), (useq - 1) & 1u);
+      if (kRope && useq) wt.drain(bar(kBarQRopeFull), (useq - 1) & 1u);
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer
+    // QK^T: S[128 x 64] = Q_slice (TMEM, 16 steps of K=16) x K_page^T (SMEM), then the RoPE
+    // slice from SMEM. PV: O_half[128 x 256] += P (TMEM, aliased over the scores) x V_half.
+    // S buffer j%2 is rewritten by QK(j+2) only after PV(j) was issued: the tensor pipe
+    // executes in issue order, so P(j) is consumed before it is overwritten.
     constexpr uint32_t idesc_qk = ptx::idesc_bf16(128, 64, 0);
     constexpr uint32_t idesc_pv = ptx::idesc_bf16(128, 256, 1);
     uint32_t it = 0, useq = 0;
@@ -427,7 +427,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool ok = true;
     while (ok && walker.next(meta, s)) {
       const int n = meta.unit_n[s.u];
-      if (!wt.wait<false>(bar(kBarQFull), useq & 1u)) break;
+      wt.where = (2 << 24) | int(it & 0xFFFFFF);
+      if (!wt.wait<false>(bar(kBarQTmemFull), useq & 1u)) break;
+      if (kRope && !wt.wait<false>(bar(kBarQRopeFull), useq & 1u)) break;
+      ptx::tc_fence_after();
       const uint32_t it0 = it;
       for (int j = 0; j <= s.np && ok; ++j) {
         wt.where = (2 << 24) | int((it0 + j) & 0xFFFFFF);
@@ -451,18 +454,14 @@ __global__ void __launch_bounds__(kThreads, 1)
             ptx::fence_proxy_async_smem();
             __syncwarp();
           }
-          if (!wt.wait<false>(bar(kBarSFree + sb), ((itq >> 1) & 1u) ^ 1u)) { ok = false; break; }
           ptx::tc_fence_after();
           if (lane == 0) {
             const uint32_t d = tmem + kTmemS + sb * 64;
-            for (int k = 0; k < 4; ++k)
-              for (int kk = 0; kk < 4; ++kk) {
-                const uint64_t ad = ptx::smem_desc(base + kSmQMain + k * kQChunkBytes + kk * 32,
-                                                   16, 1024, 2);
-                const uint64_t bd =
-                    ptx::smem_desc(stage_base + k * kKvChunkBytes + kk * 32, 16, 1024, 2);
-                ptx::mma_ss(d, ad, bd, idesc_qk, (k | kk) != 0);
-              }
+            for (int kk = 0; kk < 16; ++kk) {
+              const uint64_t bd = ptx::smem_desc(
+                  stage_base + (kk >> 2) * kKvChunkBytes + (kk & 3) * 32, 16, 1024, 2);
+              ptx::mma_ts(d, tmem + kTmemQ + kk * 8, bd, idesc_qk, kk != 0);
+            }
             if (kRope)
               for (int kk = 0; kk < 2; ++kk) {
                 const uint64_t ad = ptx::smem_desc(base + kSmQRope + kk * 32, 16, 512, 4);
@@ -485,7 +484,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int kk = 0; kk < 4; ++kk) {
               // V as B, MN-major: 64-dim chunks 8 KB apart (LBO), 8-key groups 1 KB apart (SBO).
               const uint64_t bd = ptx::smem_desc(stage_base + kk * 2048, kKvChunkBytes, 1024, 2);
-              ptx::mma_ts(tmem + kTmemO, tmem + kTmemP + pb * 32 + kk * 8, bd, idesc_pv,
+              ptx::mma_ts(tmem + kTmemO, tmem + kTmemS + pb * 64 + kk * 8, bd, idesc_pv,
                           (j > 1 || kk > 0) ? 1u : 0u);
             }
             ptx::mma_commit(bar(kBarKvEmpty + stage));
@@ -503,71 +502,111 @@ __global__ void __launch_bounds__(kThreads, 1)
     wt.drain(bar(kBarDrain), 0);
   } else {
     // ------------------------------------------------------------------ softmax + epilogue
-    // One thread per head row h (its TMEM lane). Per page: read this CTA's partial scores, send
-    // them to the peer, add the peer's partial scores, then an online softmax whose running
-    // maximum is raised only when it grows by more than 2^8 (exact after the final
-    // normalisation). Both CTAs compute identical statistics and probabilities.
-    const int qd = warp & 3;
+    // Group g (two warpgroups) handles keys [32 g, 32 g + 32) of each page; within a group one
+    // thread per head row h (its TMEM lane). Per page: read this CTA's partial scores, send them
+    // to the peer, add the peer's partial scores, combine the row maximum across the two groups,
+    // then an online softmax whose running maximum is raised only when it grows by more than
+    // 2^8 (exact after the final normalisation). Both CTAs compute identical statistics.
+    const int sw = warp - 2;                 // softmax warp index 0..7
+    const int g = sw >> 2;                   // key group
+    const int qd = warp & 3;                 // TMEM lane quarter
     const int h = 32 * qd + lane;
     const uint32_t lane_base = uint32_t(32 * qd) << 16;
-    const uint32_t swz = uint32_t(h & 7);
-    const uint32_t xb_row = uint32_t(h) * kXRowBytes;
-    const uint32_t xb_remote = ptx::map_peer(base + kSmXbuf + xb_row, peer);
-    const uint32_t xb_full_r = ptx::map_peer(bar(kBarXbFull), peer);
-    const uint32_t xb_free_r = ptx::map_peer(bar(kBarXbFree), peer);
-    const float4* xb_local = reinterpret_cast<const float4*>(sm + kSmXbuf + xb_row);
+    const uint32_t tile_off = uint32_t(g) * kGroupTileBytes + uint32_t(qd) * kWarpTileBytes +
+                              uint32_t(lane) * 16;
+    const uint32_t xb_remote = ptx::map_peer(base + kSmXbuf, peer) + tile_off;
+    const uint32_t xb_full_r0 = ptx::map_peer(bar(kBarXbFull), peer);
+    const uint32_t xb_free_r0 = ptx::map_peer(bar(kBarXbFree), peer);
+    float* row_max = reinterpret_cast<float*>(sm + kSmRowMax);
+    float* row_sum = reinterpret_cast<float*>(sm + kSmRowSum);
     const float c2 = a.scale_log2;
     uint32_t it = 0, useq = 0;
     Seg s;
     bool ok = true;
     while (ok && walker.next(meta, s)) {
       const int n = meta.unit_n[s.u];
-      float m_used = -INFINITY, l = 0.f;
-      for (int j = 0; j < s.np; ++j) {
-        const uint32_t itq = it + j, sb = itq & 1u;
-        const int valid = min(kPageRows, n - (s.p0 + j) * kPageRows);
-        wt.where = (3 << 24) | int(itq & 0xFFFFFF);
-        if (!wt.wait<false>(bar(kBarSFull + sb), (itq >> 1) & 1u)) { ok = false; break; }
+      // Group 0 writes this token's latent query slice into TMEM once the previous segment's
+      // QK MMAs have read the old one.
+      if (g == 0) {
+        wt.where = (6 << 24) | int(useq & 0xFFFFFF);
+        if (!wt.wait<false>(bar(kBarQEmpty), (useq & 1u) ^ 1u)) break;
         __syncwarp();
         ptx::tc_fence_after();
-        uint32_t sr[64];
-        {
-          const uint32_t t = tmem + lane_base + kTmemS + sb * 64;
-          ptx::tmem_ld16(t, *reinterpret_cast<uint32_t(*)[16]>(&sr[0]));
-          ptx::tmem_ld16(t + 16, *reinterpret_cast<uint32_t(*)[16]>(&sr[16]));
-          ptx::tmem_ld16(t + 32, *reinterpret_cast<uint32_t(*)[16]>(&sr[32]));
-          ptx::tmem_ld16(t + 48, *reinterpret_cast<uint32_t(*)[16]>(&sr[48]));
-          ptx::tmem_wait_ld();
+        const uint4* src = reinterpret_cast<const uint4*>(
+            a.q + s.u * a.q_stride_t + h * a.q_stride_h + (long long)k_main0 * 2);
+        for (int c = 0; c < 128; c += 16) {
+          uint32_t v[16];
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const uint4 x = h < a.heads ? src[c / 4 + k] : make_uint4(0, 0, 0, 0);
+            v[4 * k] = x.x; v[4 * k + 1] = x.y; v[4 * k + 2] = x.z; v[4 * k + 3] = x.w;
+          }
+          ptx::tmem_st16(tmem + lane_base + kTmemQ + c, v);
         }
+        ptx::tmem_wait_st();
         ptx::tc_fence_before();
         __syncwarp();
-        if (lane == 0) ptx::mbar_arrive(bar(kBarSFree + sb));
-        // Send this CTA's partial scores once the peer has read the previous page's.
-        if (!wt.wait<true>(bar(kBarXbFree), (itq & 1u) ^ 1u)) { ok = false; break; }
-#pragma unroll
-        for (int k = 0; k < 16; ++k)
-          ptx::st_cluster_v4(xb_remote + ((uint32_t(k) ^ swz) << 4), sr[4 * k], sr[4 * k + 1],
-                             sr[4 * k + 2], sr[4 * k + 3]);
+        if (lane == 0) ptx::mbar_arrive(bar(kBarQTmemFull));
+      }
+      float m_used = -INFINITY, l = 0.f;
+      for (int j = 0; j < s.np; ++j) {
+        const uint32_t itq = it + j, sb = itq & 1u, ph = (itq >> 1) & 1u;
+        const int valid = min(kPageRows, n - (s.p0 + j) * kPageRows) - kKeysPerGroup * g;
+        wt.where = (3 << 24) | int(itq & 0xFFFFFF);
+        if (!wt.wait<false>(bar(kBarSFull + sb), ph)) { ok = false; break; }
         __syncwarp();
-        if (lane == 0) ptx::mbar_arrive_cluster(xb_full_r);
-        if (!wt.wait<true>(bar(kBarXbFull), itq & 1u)) { ok = false; break; }
-        float sv[64];
+        ptx::tc_fence_after();
+        uint32_t sr[32];
+        {
+          const uint32_t t = tmem + lane_base + kTmemS + sb * 64 + kKeysPerGroup * g;
+          ptx::tmem_ld16(t, *reinterpret_cast<uint32_t(*)[16]>(&sr[0]));
+          ptx::tmem_ld16(t + 16, *reinterpret_cast<uint32_t(*)[16]>(&sr[16]));
+          ptx::tmem_wait_ld();
+        }
+        // Send this CTA's partial scores once the peer has read the tile of page itq-2.
+        if (!wt.wait<true>(bar(kBarXbFree + sb), ph ^ 1u)) { ok = false; break; }
+        {
+          const uint32_t dst = xb_remote + sb * kTileBytes;
+          const uint32_t rbar = xb_full_r0 + 8u * sb;
 #pragma unroll
-        for (int k = 0; k < 16; ++k) {
-          const float4 v = xb_local[k ^ int(swz)];
-          sv[4 * k] = __uint_as_float(sr[4 * k]) + v.x;
-          sv[4 * k + 1] = __uint_as_float(sr[4 * k + 1]) + v.y;
-          sv[4 * k + 2] = __uint_as_float(sr[4 * k + 2]) + v.z;
-          sv[4 * k + 3] = __uint_as_float(sr[4 * k + 3]) + v.w;
+          for (int k = 0; k < 8; ++k)
+            ptx::st_async_v4(dst + k * 512, sr[4 * k], sr[4 * k + 1], sr[4 * k + 2],
+                             sr[4 * k + 3], rbar);
+        }
+        // Receive the peer's partial scores for the same rows and keys.
+        if (!wt.wait<true>(bar(kBarXbFull + sb), ph)) { ok = false; break; }
+        if (sw == 0 && lane == 0) ptx::mbar_expect_tx(bar(kBarXbFull + sb), kTileBytes);
+        float sv[32];
+        {
+          const uint8_t* src = sm + kSmXbuf + sb * kTileBytes + tile_off;
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            const float4 v = *reinterpret_cast<const float4*>(src + k * 512);
+            sv[4 * k] = __uint_as_float(sr[4 * k]) + v.x;
+            sv[4 * k + 1] = __uint_as_float(sr[4 * k + 1]) + v.y;
+            sv[4 * k + 2] = __uint_as_float(sr[4 * k + 2]) + v.z;
+            sv[4 * k + 3] = __uint_as_float(sr[4 * k + 3]) + v.w;
+          }
         }
         __syncwarp();
-        if (lane == 0) ptx::mbar_arrive_cluster(xb_free_r);
+        if (lane == 0) ptx::mbar_arrive_cluster_relaxed(xb_free_r0 + 8u * sb);
         float mx = -INFINITY;
 #pragma unroll
-        for (int i = 0; i < 64; ++i) {
+        for (int i = 0; i < 32; ++i) {
           sv[i] = i < valid ? sv[i] * c2 : -INFINITY;
           mx = fmaxf(mx, sv[i]);
         }
+        // Row maximum over both key groups.
+        // This arrival also orders this warp's TMEM score loads before the other group's P
+        // stores into the same columns.
+        row_max[(sb * kSoftmaxGroups + g) * kHeadsTile + h] = mx;
+        ptx::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) ptx::mbar_arrive(bar(kBarRowMax + sb));
+        if (!wt.wait<false>(bar(kBarRowMax + sb), ph)) { ok = false; break; }
+        ptx::tc_fence_after();
+        mx = fmaxf(row_max[(sb * kSoftmaxGroups + 0) * kHeadsTile + h],
+                   row_max[(sb * kSoftmaxGroups + 1) * kHeadsTile + h]);
         float corr = 1.f;
         if (j == 0) {
           m_used = mx;
@@ -578,25 +617,26 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         // The row sum uses the f32 probabilities (softmax in f32); only the PV operand is
         // rounded to bf16 (docs/TEST-PLAN.md:61-63).
-        uint32_t pk[32];
+        uint32_t pk[16];
         float sum0 = 0.f, sum1 = 0.f;
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
+        for (int i = 0; i < 16; ++i) {
           const float p0 = ptx::ex2(sv[2 * i] - m_used), p1 = ptx::ex2(sv[2 * i + 1] - m_used);
           pk[i] = ptx::pack_bf16x2(p0, p1);
           sum0 += p0;
           sum1 += p1;
         }
         l += sum0 + sum1;
-        // The running maximum moved for some row of this warp: rescale those rows of O once
-        // PV(itq-1) has landed. The decision is per lane but tcgen05.ld/st are warp-collective,
-        // so the whole warp takes the branch (a factor of exactly 1 leaves a row unchanged).
+        // The running maximum moved for some row of this warp: rescale this group's columns of
+        // those rows of O once PV(itq-1) has landed. The decision is per lane but tcgen05.ld/st
+        // are warp-collective, so the whole warp takes the branch (a factor of exactly 1 leaves a
+        // row unchanged).
         if (__any_sync(0xFFFFFFFFu, j > 0 && corr != 1.f)) {
           const uint32_t prev = itq - 1;
           if (!wt.wait<false>(bar(kBarPvDone + (prev & 1u)), (prev >> 1) & 1u)) { ok = false; break; }
           __syncwarp();
           ptx::tc_fence_after();
-          for (int c = 0; c < kValueHalf; c += 16) {
+          for (int c = 128 * g; c < 128 * g + 128; c += 16) {
             uint32_t v[16];
             ptx::tmem_ld16(tmem + lane_base + kTmemO + c, v);
             ptx::tmem_wait_ld();
@@ -606,40 +646,38 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           ptx::tmem_wait_st();
         }
-        if (itq >= 2) {
-          const uint32_t prev = itq - 2;
-          if (!wt.wait<false>(bar(kBarPvDone + sb), (prev >> 1) & 1u)) { ok = false; break; }
-        }
+        // P overwrites the scores: both groups have read their scores (row maximum barrier).
         __syncwarp();
-        ptx::tc_fence_after();
-        {
-          const uint32_t t = tmem + lane_base + kTmemP + sb * 32;
-          ptx::tmem_st16(t, *reinterpret_cast<uint32_t(*)[16]>(&pk[0]));
-          ptx::tmem_st16(t + 16, *reinterpret_cast<uint32_t(*)[16]>(&pk[16]));
-          ptx::tmem_wait_st();
-        }
+        ptx::tmem_st16(tmem + lane_base + kTmemS + sb * 64 + 16 * g, pk);
+        ptx::tmem_wait_st();
         ptx::tc_fence_before();
         __syncwarp();
         if (lane == 0) ptx::mbar_arrive(bar(kBarPFull + sb));
       }
       if (!ok) break;
-      // Epilogue: normalise this CTA's half of O and write it.
+      // Epilogue: total row sum over both groups, then this group's 128 columns of O.
+      row_sum[g * kHeadsTile + h] = l;
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(bar(kBarRowSum));
       wt.where = (5 << 24) | int(useq & 0xFFFFFF);
+      if (!wt.wait<false>(bar(kBarRowSum), useq & 1u)) break;
+      l = row_sum[h] + row_sum[kHeadsTile + h];
       if (!wt.wait<false>(bar(kBarOFull), useq & 1u)) break;
       __syncwarp();
       ptx::tc_fence_after();
       const float inv_l = 1.f / l;
-      if (rank == 0 && h < a.heads) {
+      if (rank == 0 && g == 0 && h < a.heads) {
         const float lse = (m_used + log2f(l)) * kLn2;
         if (s.slot >= 0) meta.part_lse[(long long)s.slot * kHeadsTile + h] = lse;
         else a.lse[(long long)s.u * a.heads + h] = lse;
       }
-      const int col0 = kValueHalf * int(rank);
-      for (int c = 0; c < kValueHalf; c += 32) {
+      const int col0 = kValueHalf * int(rank) + 128 * g;
+      for (int c = 0; c < 128; c += 32) {
         uint32_t v[32];
         __syncwarp();  // TMEM loads are warp-collective; lanes past the head count rejoin here
-        ptx::tmem_ld16(tmem + lane_base + kTmemO + c, *reinterpret_cast<uint32_t(*)[16]>(&v[0]));
-        ptx::tmem_ld16(tmem + lane_base + kTmemO + c + 16,
+        ptx::tmem_ld16(tmem + lane_base + kTmemO + 128 * g + c,
+                       *reinterpret_cast<uint32_t(*)[16]>(&v[0]));
+        ptx::tmem_ld16(tmem + lane_base + kTmemO + 128 * g + c + 16,
                        *reinterpret_cast<uint32_t(*)[16]>(&v[16]));
         ptx::tmem_wait_ld();
         if (h >= a.heads) {
@@ -1042,11 +1080,10 @@ int32_t launch(const TqMlaParams* params, void* workspace, uint64_t workspace_by
                                       S, (long long)params->slots, (long long)params->pages,
                                       pairs);
   if (params->pages > 0) {
-    CUtensorMap tq_map, tq_rope, tkv, tkv_rope;
+    CUtensorMap tq_rope, tkv, tkv_rope;
     const uint64_t width = params->qk_width;
     const cuuint64_t qdims[3] = {width, params->heads, params->tokens};
     const cuuint64_t qstr[2] = {s.q.strides_bytes[1], s.q.strides_bytes[0]};
-    const cuuint32_t qbox[3] = {64, cuuint32_t(H), 1};
     const cuuint32_t qbox_r[3] = {32, cuuint32_t(H), 1};
     const cuuint64_t kdims[2] = {width, pool_rows};
     const cuuint64_t kstr[1] = {params->row_stride};
@@ -1054,19 +1091,21 @@ int32_t launch(const TqMlaParams* params, void* workspace, uint64_t workspace_by
     const cuuint32_t kbox_r[2] = {32, 64};
     const void* qa = reinterpret_cast<const void*>(s.q.device_address);
     const void* ka = reinterpret_cast<const void*>(s.kv.device_address);
-    if (!encode_bf16(&tq_map, qa, 3, qdims, qstr, qbox, CU_TENSOR_MAP_SWIZZLE_128B) ||
-        !encode_bf16(&tkv, ka, 2, kdims, kstr, kbox, CU_TENSOR_MAP_SWIZZLE_128B))
+    if (!encode_bf16(&tkv, ka, 2, kdims, kstr, kbox, CU_TENSOR_MAP_SWIZZLE_128B))
       return set_err(err, "tensor_map", TQ_ERR_CUDA);
     if (rope) {
       if (!encode_bf16(&tq_rope, qa, 3, qdims, qstr, qbox_r, CU_TENSOR_MAP_SWIZZLE_64B) ||
           !encode_bf16(&tkv_rope, ka, 2, kdims, kstr, kbox_r, CU_TENSOR_MAP_SWIZZLE_64B))
         return set_err(err, "tensor_map", TQ_ERR_CUDA);
     } else {
-      tq_rope = tq_map;
+      tq_rope = tkv;
       tkv_rope = tkv;
     }
     MainArgs a;
     a.meta = m;
+    a.q = reinterpret_cast<const char*>(s.q.device_address);
+    a.q_stride_t = (long long)s.q.strides_bytes[0];
+    a.q_stride_h = (long long)s.q.strides_bytes[1];
     a.page_table = reinterpret_cast<const int*>(s.page_table.device_address);
     a.seq_id = reinterpret_cast<const int*>(s.seq_id.device_address);
     a.slots = (long long)params->slots;
@@ -1092,10 +1131,8 @@ int32_t launch(const TqMlaParams* params, void* workspace, uint64_t workspace_by
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    cudaError_t e = rope ? cudaLaunchKernelEx(&cfg, mla_paged_kernel<true>, tq_map, tq_rope, tkv,
-                                              tkv_rope, a)
-                         : cudaLaunchKernelEx(&cfg, mla_paged_kernel<false>, tq_map, tq_rope, tkv,
-                                              tkv_rope, a);
+    cudaError_t e = rope ? cudaLaunchKernelEx(&cfg, mla_paged_kernel<true>, tq_rope, tkv, tkv_rope, a)
+                         : cudaLaunchKernelEx(&cfg, mla_paged_kernel<false>, tq_rope, tkv, tkv_rope, a);
     if (e != cudaSuccess) return set_err(err, "launch", TQ_ERR_CUDA);
   }
   combine_kernel<<<2 * pairs * kCombineBlocksPerJob, 256, 0, st>>>(

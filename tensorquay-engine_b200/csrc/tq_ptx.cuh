@@ -57,6 +57,15 @@ __device__ __forceinline__ void st_cluster_v2(uint32_t addr, uint32_t a, uint32_
                : "memory");
 }
 
+// Asynchronous 16-byte store into another CTA's shared memory; its bytes complete a transaction
+// on that CTA's mbarrier `remote_bar` (both addresses in the shared::cluster window).
+__device__ __forceinline__ void st_async_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c,
+                                            uint32_t d, uint32_t remote_bar) {
+  asm volatile(
+      "st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.b32 [%0], {%1, %2, %3, %4}, [%5];"
+      :: "r"(addr), "r"(a), "r"(b), "r"(c), "r"(d), "r"(remote_bar) : "memory");
+}
+
 // ---- mbarriers ------------------------------------------------------------------------------
 
 __device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
@@ -75,7 +84,6 @@ __device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" :: "r"(bar), "r"(bytes)
                : "memory");
 }
-
 // Arrive on a barrier in another CTA of the cluster, releasing this thread's prior writes
 // (including its st.shared::cluster stores) at cluster scope.
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t remote_bar) {
@@ -83,22 +91,31 @@ __device__ __forceinline__ void mbar_arrive_cluster(uint32_t remote_bar) {
                : "memory");
 }
 
+// Arrive on a barrier in another CTA without release semantics: only for signalling that loads
+// whose values this thread has already consumed are complete (a buffer may be overwritten).
+__device__ __forceinline__ void mbar_arrive_cluster_relaxed(uint32_t remote_bar) {
+  asm volatile("mbarrier.arrive.relaxed.cluster.shared::cluster.b64 _, [%0];" :: "r"(remote_bar)
+               : "memory");
+}
+
+// Non-blocking test of a phase (the callers spin with their own bounds): a suspended
+// try_wait can resume long after the phase completed.
 __device__ __forceinline__ bool mbar_test(uint32_t bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok) : "r"(bar), "r"(parity) : "memory");
   return ok != 0;
 }
 
-// Acquire at cluster scope: pairs with mbar_arrive_cluster from the peer CTA.
+// Acquire at cluster scope: pairs with arrivals and transactions from the peer CTA.
 __device__ __forceinline__ bool mbar_test_cluster(uint32_t bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.test_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok) : "r"(bar), "r"(parity) : "memory");
   return ok != 0;
