@@ -298,9 +298,11 @@ struct Waiter {
 
 template <bool kRope>
 __global__ void __launch_bounds__(kThreads, 1)
-    mla_paged_kernel(const __grid_constant__ CUtensorMap tm_q_rope,
-                     const __grid_constant__ CUtensorMap tm_kv,
-                     const __grid_constant__ CUtensorMap tm_kv_rope, const MainArgs a) {
+    mla_paged_kernel(const __grid_constant__ CUtensorMap tm_q,
+                     const __grid_constant__ CUtensorMap tm_kv, const MainArgs a) {
+  constexpr int kQkChunks = kRope ? 9 : 8;               // 64-dim chunks of the query width
+  constexpr int kQSmemChunks = kQkChunks - kQTmemDims / 64;
+  constexpr uint32_t kStageLoadBytes = (kQkChunks + 4) * kKvChunkBytes;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = ptx::smem_addr(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
@@ -319,37 +321,40 @@ __global__ void __launch_bounds__(kThreads, 1)
       ptx::mbar_init(bar(kBarKvFull + s), 1);
       ptx::mbar_init(bar(kBarKvEmpty + s), 1);
     }
-    ptx::mbar_init(bar(kBarQRopeFull), 1);
-    ptx::mbar_init(bar(kBarQTmemFull), 4);
+    ptx::mbar_init(bar(kBarQSmemFull), 1);
+    ptx::mbar_init(bar(kBarQTmemFull), kSoftmaxWarps);
     ptx::mbar_init(bar(kBarQEmpty), 1);
     for (int b = 0; b < 2; ++b) {
       ptx::mbar_init(bar(kBarSFull + b), 1);
       ptx::mbar_init(bar(kBarPFull + b), kSoftmaxWarps);
       ptx::mbar_init(bar(kBarPvDone + b), 1);
-      ptx::mbar_init(bar(kBarXbFull + b), 1);
-      ptx::mbar_init(bar(kBarXbFree + b), kSoftmaxWarps);
-      ptx::mbar_init(bar(kBarRowMax + b), kSoftmaxWarps);
     }
     ptx::mbar_init(bar(kBarOFull), 1);
     ptx::mbar_init(bar(kBarOFree), kSoftmaxWarps);
-    ptx::mbar_init(bar(kBarRowSum), kSoftmaxWarps);
+    for (int i = 0; i < 8; ++i) {
+      ptx::mbar_init(bar(kBarMsgFull + i), 1);
+      ptx::mbar_init(bar(kBarMsgFree + i), 1);
+      // Each receive buffer expects one peer warp's message; armed for pages 0 and 1.
+      ptx::mbar_expect_tx(bar(kBarMsgFull + i), kWarpMsgBytes);
+    }
+    for (int w = 0; w < 4; ++w) {
+      ptx::mbar_init(bar(kBarLsumFull + w), 1);
+      ptx::mbar_expect_tx(bar(kBarLsumFull + w), 32 * 4);
+    }
     ptx::mbar_init(bar(kBarDrain), 1);
-    // The receive tiles of pages 0 and 1 expect the peer's 32 KB each.
-    ptx::mbar_expect_tx(bar(kBarXbFull + 0), kTileBytes);
-    ptx::mbar_expect_tx(bar(kBarXbFull + 1), kTileBytes);
     *abort_flag = 0;
     ptx::fence_mbar_init_cluster();
+    ptx::tma_prefetch_desc(&tm_q);
     ptx::tma_prefetch_desc(&tm_kv);
-    if (kRope) {
-      ptx::tma_prefetch_desc(&tm_q_rope);
-      ptx::tma_prefetch_desc(&tm_kv_rope);
-    }
   }
-  // RoPE query rows past the head count stay zero for the whole kernel (TMA writes rows < heads).
-  if (kRope && a.heads < kHeadsTile) {
-    const int words = (kHeadsTile - a.heads) * 64 / 16;
-    for (int i = threadIdx.x; i < words; i += kThreads)
-      reinterpret_cast<uint4*>(sm + kSmQRope + a.heads * 64)[i] = make_uint4(0, 0, 0, 0);
+  // Query rows past the head count stay zero for the whole kernel (TMA writes rows < heads).
+  if (a.heads < kHeadsTile) {
+    const int words = (kHeadsTile - a.heads) * 128 / 16;
+    for (int i = threadIdx.x; i < kQSmemChunks * words; i += kThreads) {
+      const int chunk = i / words, w = i % words;
+      reinterpret_cast<uint4*>(sm + kSmQ + chunk * kQChunkBytes + a.heads * 128)[w] =
+          make_uint4(0, 0, 0, 0);
+    }
     ptx::fence_proxy_async_smem();
   }
   if (warp == 1) {
@@ -365,23 +370,22 @@ __global__ void __launch_bounds__(kThreads, 1)
   SegWalker walker;
   walker.init(a.meta, pair, a.tokens);
   const Meta& meta = a.meta;
-  const int k_main0 = 256 * int(rank);      // first latent dim of this CTA's slice
-  const int k_rope0 = 512 + 32 * int(rank); // first RoPE dim of this CTA's slice
+  const int key0 = kKeysPerCta * int(rank);  // this CTA's keys within a page
+  const int vdim0 = kValueHalf * int(rank);  // this CTA's value dims
 
   if (warp == 0) {
     // ------------------------------------------------------------------ TMA producer
     if (lane == 0) {
-      const uint32_t stage_bytes = kRope ? kStageBytes : 4 * kKvChunkBytes;
       uint32_t it = 0, useq = 0;
       Seg s;
       bool ok = true;
       while (ok && walker.next(meta, s)) {
         wt.where = (1 << 24) | int(it & 0xFFFFFF);
-        if (kRope) {
-          if (!wt.wait<false>(bar(kBarQEmpty), (useq & 1u) ^ 1u)) break;
-          ptx::mbar_expect_tx(bar(kBarQRopeFull), uint32_t(a.heads) * 64);
-          ptx::tma_load_3d(base + kSmQRope, &tm_q_rope, bar(kBarQRopeFull), k_rope0, 0, s.u);
-        }
+        if (!wt.wait<false>(bar(kBarQEmpty), (useq & 1u) ^ 1u)) break;
+        ptx::mbar_expect_tx(bar(kBarQSmemFull), uint32_t(a.heads) * 128 * kQSmemChunks);
+        for (int k = 0; k < kQSmemChunks; ++k)
+          ptx::tma_load_3d(base + kSmQ + k * kQChunkBytes, &tm_q, bar(kBarQSmemFull),
+                           kQTmemDims + 64 * k, 0, s.u);
         ++useq;
         const int* pt = a.page_table + (long long)a.seq_id[s.u] * a.slots;
         for (int j = 0; j < s.np; ++j, ++it) {
@@ -398,13 +402,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             row = a.pool_rows;  // a box entirely out of bounds: TMA fills zeros
           }
           const uint32_t dst = base + kSmKv + stage * kStageBytes;
-          ptx::mbar_expect_tx(bar(kBarKvFull + stage), stage_bytes);
-          for (int k = 0; k < 4; ++k)
-            ptx::tma_load_2d(dst + k * kKvChunkBytes, &tm_kv, bar(kBarKvFull + stage),
-                             k_main0 + 64 * k, int(row));
-          if (kRope)
-            ptx::tma_load_2d(dst + kKvRopeOffset, &tm_kv_rope, bar(kBarKvFull + stage), k_rope0,
-                             int(row));
+          const uint32_t fb = bar(kBarKvFull + stage);
+          ptx::mbar_expect_tx(fb, kStageLoadBytes);
+          for (int c = 0; c < kQkChunks; ++c)
+            ptx::tma_load_2d(dst + c * kKvChunkBytes, &tm_kv, fb, 64 * c, int(row) + key0);
+          for (int c = 0; c < 4; ++c)
+            ptx::tma_load_2d(dst + kPvxOffset + c * kKvChunkBytes, &tm_kv, fb, vdim0 + 64 * c,
+                             int(row) + kKeysPerCta - key0);
         }
       }
       // Drain: every issued copy has landed before the CTA may exit.
@@ -412,15 +416,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t last = it - 1 - ((it - 1 - st) % kStages);
         wt.drain(bar(kBarKvFull + st), (last / kStages) & 1u);
       }
-      if (kRope && useq) wt.drain(bar(kBarQRopeFull), (useq - 1) & 1u);
+      if (useq) wt.drain(bar(kBarQSmemFull), (useq - 1) & 1u);
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer
-    // QK^T: S[128 x 64] = Q_slice (TMEM, 16 steps of K=16) x K_page^T (SMEM), then the RoPE
-    // slice from SMEM. PV: O_half[128 x 256] += P (TMEM, aliased over the scores) x V_half.
+    // QK^T: S[128 x 32] = Q x K_own^T, 24 steps with the query from TMEM, then the remaining
+    // query chunks from shared memory. PV: O_half[128 x 256] += P[128 x 64] V[64 x 256]: the
+    // own keys' P from TMEM (aliased over the scores), the peer keys' P from shared memory.
     // S buffer j%2 is rewritten by QK(j+2) only after PV(j) was issued: the tensor pipe
     // executes in issue order, so P(j) is consumed before it is overwritten.
-    constexpr uint32_t idesc_qk = ptx::idesc_bf16(128, 64, 0);
+    constexpr uint32_t idesc_qk = ptx::idesc_bf16(128, 32, 0);
     constexpr uint32_t idesc_pv = ptx::idesc_bf16(128, 256, 1);
     uint32_t it = 0, useq = 0;
     Seg s;
@@ -429,7 +434,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int n = meta.unit_n[s.u];
       wt.where = (2 << 24) | int(it & 0xFFFFFF);
       if (!wt.wait<false>(bar(kBarQTmemFull), useq & 1u)) break;
-      if (kRope && !wt.wait<false>(bar(kBarQRopeFull), useq & 1u)) break;
+      if (!wt.wait<false>(bar(kBarQSmemFull), useq & 1u)) break;
       ptx::tc_fence_after();
       const uint32_t it0 = it;
       for (int j = 0; j <= s.np && ok; ++j) {
@@ -439,36 +444,44 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (!wt.wait<false>(bar(kBarKvFull + stage), (itq / kStages) & 1u)) { ok = false; break; }
           const uint32_t stage_base = base + kSmKv + stage * kStageBytes;
           const int valid = min(kPageRows, n - (s.p0 + j) * kPageRows);
-          if (valid < kPageRows) {
+          const int own_valid = max(0, min(kKeysPerCta, valid - key0));
+          const int peer_valid = max(0, min(kKeysPerCta, valid - (kKeysPerCta - key0)));
+          if (own_valid < kKeysPerCta || peer_valid < kKeysPerCta) {
+            // Rows past the cached length (NaN-poisoned slots) become zeros before any MMA.
             uint8_t* st_ptr = sm + kSmKv + stage * kStageBytes;
-            const int main_words = (kPageRows - valid) * 128 / 16;
-            for (int i = lane; i < 4 * main_words; i += 32) {
-              const int chunk = i / main_words, w = i % main_words;
-              reinterpret_cast<uint4*>(st_ptr + chunk * kKvChunkBytes + valid * 128)[w] =
+            const int own_words = (kKeysPerCta - own_valid) * 8;
+            const int peer_words = (kKeysPerCta - peer_valid) * 8;
+            for (int i = lane; i < kQkChunks * own_words; i += 32) {
+              const int c = i / own_words, w = i % own_words;
+              reinterpret_cast<uint4*>(st_ptr + c * kKvChunkBytes + own_valid * 128)[w] =
                   make_uint4(0, 0, 0, 0);
             }
-            if (kRope)
-              for (int i = lane; i < (kPageRows - valid) * 4; i += 32)
-                reinterpret_cast<uint4*>(st_ptr + kKvRopeOffset + valid * 64)[i] =
-                    make_uint4(0, 0, 0, 0);
+            for (int i = lane; i < 4 * peer_words; i += 32) {
+              const int c = i / peer_words, w = i % peer_words;
+              reinterpret_cast<uint4*>(st_ptr + kPvxOffset + c * kKvChunkBytes +
+                                       peer_valid * 128)[w] = make_uint4(0, 0, 0, 0);
+            }
             ptx::fence_proxy_async_smem();
             __syncwarp();
           }
           ptx::tc_fence_after();
           if (lane == 0) {
-            const uint32_t d = tmem + kTmemS + sb * 64;
-            for (int kk = 0; kk < 16; ++kk) {
-              const uint64_t bd = ptx::smem_desc(
-                  stage_base + (kk >> 2) * kKvChunkBytes + (kk & 3) * 32, 16, 1024, 2);
-              ptx::mma_ts(d, tmem + kTmemQ + kk * 8, bd, idesc_qk, kk != 0);
-            }
-            if (kRope)
-              for (int kk = 0; kk < 2; ++kk) {
-                const uint64_t ad = ptx::smem_desc(base + kSmQRope + kk * 32, 16, 512, 4);
-                const uint64_t bd =
-                    ptx::smem_desc(stage_base + kKvRopeOffset + kk * 32, 16, 512, 4);
-                ptx::mma_ss(d, ad, bd, idesc_qk, 1);
-              }
+            // Descriptors advance by compile-time offsets (start field = address >> 4; shared
+            // addresses stay below 256 KB, so the 14-bit field never carries).
+            const uint32_t d = tmem + kTmemS + sb * 32;
+            const uint64_t kd = ptx::smem_desc(stage_base, 16, 1024, 2);
+            const uint64_t qd = ptx::smem_desc(base + kSmQ, 16, 1024, 2);
+#pragma unroll
+            for (int kk = 0; kk < kQTmemDims / 16; ++kk)
+              ptx::mma_ts(d, tmem + kTmemQ + kk * 8,
+                          kd + uint64_t(((kk >> 2) * kKvChunkBytes + (kk & 3) * 32) >> 4),
+                          idesc_qk, kk != 0);
+#pragma unroll
+            for (int kk = 0; kk < kQSmemChunks * 4; ++kk)
+              ptx::mma_ss(d, qd + uint64_t(((kk >> 2) * kQChunkBytes + (kk & 3) * 32) >> 4),
+                          kd + uint64_t((((kQTmemDims / 64) + (kk >> 2)) * kKvChunkBytes +
+                                         (kk & 3) * 32) >> 4),
+                          idesc_qk, 1);
             ptx::mma_commit(bar(kBarSFull + sb));
             if (j == s.np - 1) ptx::mma_commit(bar(kBarQEmpty));
           }
@@ -481,12 +494,21 @@ __global__ void __launch_bounds__(kThreads, 1)
           ptx::tc_fence_after();
           if (lane == 0) {
             const uint32_t stage_base = base + kSmKv + stage * kStageBytes;
-            for (int kk = 0; kk < 4; ++kk) {
-              // V as B, MN-major: 64-dim chunks 8 KB apart (LBO), 8-key groups 1 KB apart (SBO).
-              const uint64_t bd = ptx::smem_desc(stage_base + kk * 2048, kKvChunkBytes, 1024, 2);
-              ptx::mma_ts(tmem + kTmemO, tmem + kTmemS + pb * 64 + kk * 8, bd, idesc_pv,
-                          (j > 1 || kk > 0) ? 1u : 0u);
-            }
+            // V as B, MN-major: 64-dim chunks 4 KB apart (LBO), 8-key groups 1 KB apart (SBO).
+            const uint64_t vd = ptx::smem_desc(stage_base + (vdim0 / 64) * kKvChunkBytes,
+                                               kKvChunkBytes, 1024, 2);
+            const uint64_t xd = ptx::smem_desc(stage_base + kPvxOffset, kKvChunkBytes, 1024, 2);
+            // Peer P, K-major without swizzle: 8-row groups 128 B apart (SBO), the two 8-key
+            // chunks of a step 2 KB apart (LBO).
+            const uint64_t pd = ptx::smem_desc(base + kSmPeer + pb * kPMsgBytes, kPChunkBytes, 128, 0);
+#pragma unroll
+            for (int kk = 0; kk < 2; ++kk)
+              ptx::mma_ts(tmem + kTmemO, tmem + kTmemS + pb * 32 + kk * 8,
+                          vd + uint64_t((kk * 2048) >> 4), idesc_pv, (j > 1 || kk > 0) ? 1u : 0u);
+#pragma unroll
+            for (int kk = 0; kk < 2; ++kk)
+              ptx::mma_ss(tmem + kTmemO, pd + uint64_t((kk * 2 * kPChunkBytes) >> 4),
+                          xd + uint64_t((kk * 2048) >> 4), idesc_pv, 1u);
             ptx::mma_commit(bar(kBarKvEmpty + stage));
             ptx::mma_commit(bar(kBarPvDone + pb));
             if (j == s.np) ptx::mma_commit(bar(kBarOFull));
@@ -502,39 +524,36 @@ __global__ void __launch_bounds__(kThreads, 1)
     wt.drain(bar(kBarDrain), 0);
   } else {
     // ------------------------------------------------------------------ softmax + epilogue
-    // Group g (two warpgroups) handles keys [32 g, 32 g + 32) of each page; within a group one
-    // thread per head row h (its TMEM lane). Per page: read this CTA's partial scores, send them
-    // to the peer, add the peer's partial scores, combine the row maximum across the two groups,
-    // then an online softmax whose running maximum is raised only when it grows by more than
-    // 2^8 (exact after the final normalisation). Both CTAs compute identical statistics.
-    const int sw = warp - 2;                 // softmax warp index 0..7
-    const int g = sw >> 2;                   // key group
-    const int qd = warp & 3;                 // TMEM lane quarter
+    // One thread per head row h (its TMEM lane), 32 own keys per page. Per page: scores to
+    // log2 units, a candidate reference maximum (the running one, or the page maximum when that
+    // grew by more than 2^8), probabilities against it, then one message to the peer: the bf16
+    // probabilities and the candidate. The new running maximum is the larger of the running one
+    // and both candidates; each CTA recomputes its own probabilities exactly against it and
+    // rescales the peer's (only when a maximum moved). Both CTAs derive identical statistics.
+    const int sw = warp - 2;                  // softmax warp index 0..3
+    const int qd = warp & 3;                  // TMEM lane quarter
     const int h = 32 * qd + lane;
     const uint32_t lane_base = uint32_t(32 * qd) << 16;
-    const uint32_t tile_off = uint32_t(g) * kGroupTileBytes + uint32_t(qd) * kWarpTileBytes +
-                              uint32_t(lane) * 16;
-    const uint32_t xb_remote = ptx::map_peer(base + kSmXbuf, peer) + tile_off;
-    const uint32_t xb_full_r0 = ptx::map_peer(bar(kBarXbFull), peer);
-    const uint32_t xb_free_r0 = ptx::map_peer(bar(kBarXbFree), peer);
-    float* row_max = reinterpret_cast<float*>(sm + kSmRowMax);
-    float* row_sum = reinterpret_cast<float*>(sm + kSmRowSum);
+    const uint32_t peer_base = ptx::map_peer(base + kSmPeer, peer);
+    const uint32_t lsum_remote = ptx::map_peer(base + kSmLsum, peer) + 4u * h;
+    const uint32_t msg_full_r = ptx::map_peer(bar(kBarMsgFull), peer);
+    const uint32_t msg_free_r = ptx::map_peer(bar(kBarMsgFree), peer);
+    const uint32_t lsum_full_r = ptx::map_peer(bar(kBarLsumFull), peer);
     const float c2 = a.scale_log2;
     uint32_t it = 0, useq = 0;
     Seg s;
     bool ok = true;
     while (ok && walker.next(meta, s)) {
       const int n = meta.unit_n[s.u];
-      // Group 0 writes this token's latent query slice into TMEM once the previous segment's
-      // QK MMAs have read the old one.
-      if (g == 0) {
+      // This token's query dims [0, 384) into TMEM once the previous segment's QK MMAs are done.
+      {
         wt.where = (6 << 24) | int(useq & 0xFFFFFF);
         if (!wt.wait<false>(bar(kBarQEmpty), (useq & 1u) ^ 1u)) break;
         __syncwarp();
         ptx::tc_fence_after();
-        const uint4* src = reinterpret_cast<const uint4*>(
-            a.q + s.u * a.q_stride_t + h * a.q_stride_h + (long long)k_main0 * 2);
-        for (int c = 0; c < 128; c += 16) {
+        const uint4* src = reinterpret_cast<const uint4*>(a.q + s.u * a.q_stride_t +
+                                                          h * a.q_stride_h);
+        for (int c = 0; c < kQTmemDims / 2; c += 16) {
           uint32_t v[16];
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
@@ -551,92 +570,103 @@ __global__ void __launch_bounds__(kThreads, 1)
       float m_used = -INFINITY, l = 0.f;
       for (int j = 0; j < s.np; ++j) {
         const uint32_t itq = it + j, sb = itq & 1u, ph = (itq >> 1) & 1u;
-        const int valid = min(kPageRows, n - (s.p0 + j) * kPageRows) - kKeysPerGroup * g;
+        const int own_valid = min(kPageRows, n - (s.p0 + j) * kPageRows) - key0;
         wt.where = (3 << 24) | int(itq & 0xFFFFFF);
         if (!wt.wait<false>(bar(kBarSFull + sb), ph)) { ok = false; break; }
         __syncwarp();
         ptx::tc_fence_after();
-        uint32_t sr[32];
+        float sv[32];
         {
-          const uint32_t t = tmem + lane_base + kTmemS + sb * 64 + kKeysPerGroup * g;
+          uint32_t sr[32];
+          const uint32_t t = tmem + lane_base + kTmemS + sb * 32;
           ptx::tmem_ld16(t, *reinterpret_cast<uint32_t(*)[16]>(&sr[0]));
           ptx::tmem_ld16(t + 16, *reinterpret_cast<uint32_t(*)[16]>(&sr[16]));
           ptx::tmem_wait_ld();
-        }
-        // Send this CTA's partial scores once the peer has read the tile of page itq-2.
-        if (!wt.wait<true>(bar(kBarXbFree + sb), ph ^ 1u)) { ok = false; break; }
-        {
-          const uint32_t dst = xb_remote + sb * kTileBytes;
-          const uint32_t rbar = xb_full_r0 + 8u * sb;
 #pragma unroll
-          for (int k = 0; k < 8; ++k)
-            ptx::st_async_v4(dst + k * 512, sr[4 * k], sr[4 * k + 1], sr[4 * k + 2],
-                             sr[4 * k + 3], rbar);
+          for (int i = 0; i < 32; ++i) sv[i] = i < own_valid ? __uint_as_float(sr[i]) * c2 : -INFINITY;
         }
-        // Receive the peer's partial scores for the same rows and keys.
-        if (!wt.wait<true>(bar(kBarXbFull + sb), ph)) { ok = false; break; }
-        if (sw == 0 && lane == 0) ptx::mbar_expect_tx(bar(kBarXbFull + sb), kTileBytes);
-        float sv[32];
-        {
-          const uint8_t* src = sm + kSmXbuf + sb * kTileBytes + tile_off;
-#pragma unroll
-          for (int k = 0; k < 8; ++k) {
-            const float4 v = *reinterpret_cast<const float4*>(src + k * 512);
-            sv[4 * k] = __uint_as_float(sr[4 * k]) + v.x;
-            sv[4 * k + 1] = __uint_as_float(sr[4 * k + 1]) + v.y;
-            sv[4 * k + 2] = __uint_as_float(sr[4 * k + 2]) + v.z;
-            sv[4 * k + 3] = __uint_as_float(sr[4 * k + 3]) + v.w;
-          }
-        }
-        __syncwarp();
-        if (lane == 0) ptx::mbar_arrive_cluster_relaxed(xb_free_r0 + 8u * sb);
         float mx = -INFINITY;
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          sv[i] = i < valid ? sv[i] * c2 : -INFINITY;
-          mx = fmaxf(mx, sv[i]);
-        }
-        // Row maximum over both key groups.
-        // This arrival also orders this warp's TMEM score loads before the other group's P
-        // stores into the same columns.
-        row_max[(sb * kSoftmaxGroups + g) * kHeadsTile + h] = mx;
-        ptx::tc_fence_before();
-        __syncwarp();
-        if (lane == 0) ptx::mbar_arrive(bar(kBarRowMax + sb));
-        if (!wt.wait<false>(bar(kBarRowMax + sb), ph)) { ok = false; break; }
-        ptx::tc_fence_after();
-        mx = fmaxf(row_max[(sb * kSoftmaxGroups + 0) * kHeadsTile + h],
-                   row_max[(sb * kSoftmaxGroups + 1) * kHeadsTile + h]);
-        float corr = 1.f;
-        if (j == 0) {
-          m_used = mx;
-        } else if (mx > m_used + kRescaleThreshold) {
-          corr = ptx::ex2(m_used - mx);
-          m_used = mx;
-          l *= corr;
-        }
-        // The row sum uses the f32 probabilities (softmax in f32); only the PV operand is
-        // rounded to bf16 (docs/TEST-PLAN.md:61-63).
+        for (int i = 0; i < 32; ++i) mx = fmaxf(mx, sv[i]);
+        const float m_cand = j == 0 ? mx : (mx > m_used + kRescaleThreshold ? mx : m_used);
         uint32_t pk[16];
-        float sum0 = 0.f, sum1 = 0.f;
+        float l_page = 0.f;
+        {
+          float s0 = 0.f, s1 = 0.f;
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const float p0 = ptx::ex2(sv[2 * i] - m_used), p1 = ptx::ex2(sv[2 * i + 1] - m_used);
-          pk[i] = ptx::pack_bf16x2(p0, p1);
-          sum0 += p0;
-          sum1 += p1;
+          for (int i = 0; i < 16; ++i) {
+            const float p0 = m_cand == -INFINITY ? 0.f : ptx::ex2(sv[2 * i] - m_cand);
+            const float p1 = m_cand == -INFINITY ? 0.f : ptx::ex2(sv[2 * i + 1] - m_cand);
+            pk[i] = ptx::pack_bf16x2(p0, p1);
+            s0 += p0;
+            s1 += p1;
+          }
+          l_page = s0 + s1;
         }
-        l += sum0 + sum1;
-        // The running maximum moved for some row of this warp: rescale this group's columns of
-        // those rows of O once PV(itq-1) has landed. The decision is per lane but tcgen05.ld/st
-        // are warp-collective, so the whole warp takes the branch (a factor of exactly 1 leaves a
-        // row unchanged).
-        if (__any_sync(0xFFFFFFFFu, j > 0 && corr != 1.f)) {
+        // Release the peer's buffer of page itq-2 (PV(itq-2) has consumed it), then send this
+        // page's probabilities and candidate once the peer has released ours.
+        if (itq >= 2) {
+          const uint32_t prev = itq - 2;
+          if (!wt.wait<false>(bar(kBarPvDone + sb), (prev >> 1) & 1u)) { ok = false; break; }
+          __syncwarp();
+          if (lane == 0) ptx::mbar_arrive_cluster_relaxed(msg_free_r + 8u * (sb * 4 + sw));
+        }
+        if (!wt.wait<true>(bar(kBarMsgFree + sb * 4 + sw), ph ^ 1u)) { ok = false; break; }
+        {
+          const uint32_t dst = peer_base + sb * kPMsgBytes + 16u * h;
+          const uint32_t rbar = msg_full_r + 8u * (sb * 4 + sw);
+#pragma unroll
+          for (int c = 0; c < 4; ++c)
+            ptx::st_async_v4(dst + c * kPChunkBytes, pk[4 * c], pk[4 * c + 1], pk[4 * c + 2],
+                             pk[4 * c + 3], rbar);
+          ptx::st_async_b32(peer_base + sb * kPMsgBytes + kPBytes + 4u * h,
+                            __float_as_uint(m_cand), rbar);
+        }
+        if (!wt.wait<true>(bar(kBarMsgFull + sb * 4 + sw), ph)) { ok = false; break; }
+        if (lane == 0) ptx::mbar_expect_tx(bar(kBarMsgFull + sb * 4 + sw), kWarpMsgBytes);
+        const uint8_t* msg = sm + kSmPeer + sb * kPMsgBytes;
+        const float m_peer = *reinterpret_cast<const float*>(msg + kPBytes + 4 * h);
+        const float m_new = fmaxf(m_used, fmaxf(m_cand, m_peer));
+        if (m_new != m_cand && m_cand != -INFINITY) {
+          // Own probabilities against the new maximum, exactly (rare after the first page).
+          float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const float p0 = ptx::ex2(sv[2 * i] - m_new), p1 = ptx::ex2(sv[2 * i + 1] - m_new);
+            pk[i] = ptx::pack_bf16x2(p0, p1);
+            s0 += p0;
+            s1 += p1;
+          }
+          l_page = s0 + s1;
+        }
+        if (m_new != m_peer && m_peer != -INFINITY) {
+          // The peer's probabilities were against a smaller maximum: rescale them in place.
+          const float f = ptx::ex2(m_peer - m_new);
+          uint8_t* prow = sm + kSmPeer + sb * kPMsgBytes + 16 * h;
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            uint4 v = *reinterpret_cast<uint4*>(prow + c * kPChunkBytes);
+            v.x = ptx::pack_bf16x2(ptx::bf16_lo(v.x) * f, ptx::bf16_hi(v.x) * f);
+            v.y = ptx::pack_bf16x2(ptx::bf16_lo(v.y) * f, ptx::bf16_hi(v.y) * f);
+            v.z = ptx::pack_bf16x2(ptx::bf16_lo(v.z) * f, ptx::bf16_hi(v.z) * f);
+            v.w = ptx::pack_bf16x2(ptx::bf16_lo(v.w) * f, ptx::bf16_hi(v.w) * f);
+            *reinterpret_cast<uint4*>(prow + c * kPChunkBytes) = v;
+          }
+        }
+        ptx::fence_proxy_async_smem();  // the peer's P (as received or rescaled) feeds the MMA
+        float corr = 1.f;
+        if (j > 0 && m_new > m_used) corr = ptx::ex2(m_used - m_new);
+        l = l * corr + l_page;
+        m_used = m_new;
+        // The running maximum moved for some row of this warp: rescale those rows of O once
+        // PV(itq-1) has landed. The decision is per lane but tcgen05.ld/st are warp-collective,
+        // so the whole warp takes the branch (a factor of exactly 1 leaves a row unchanged).
+        if (__any_sync(0xFFFFFFFFu, corr != 1.f)) {
           const uint32_t prev = itq - 1;
           if (!wt.wait<false>(bar(kBarPvDone + (prev & 1u)), (prev >> 1) & 1u)) { ok = false; break; }
           __syncwarp();
           ptx::tc_fence_after();
-          for (int c = 128 * g; c < 128 * g + 128; c += 16) {
+          for (int c = 0; c < kValueHalf; c += 16) {
             uint32_t v[16];
             ptx::tmem_ld16(tmem + lane_base + kTmemO + c, v);
             ptx::tmem_wait_ld();
@@ -646,38 +676,37 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           ptx::tmem_wait_st();
         }
-        // P overwrites the scores: both groups have read their scores (row maximum barrier).
+        // Own P over the scores of this buffer (this thread read them above).
         __syncwarp();
-        ptx::tmem_st16(tmem + lane_base + kTmemS + sb * 64 + 16 * g, pk);
+        ptx::tmem_st16(tmem + lane_base + kTmemS + sb * 32, pk);
         ptx::tmem_wait_st();
         ptx::tc_fence_before();
         __syncwarp();
         if (lane == 0) ptx::mbar_arrive(bar(kBarPFull + sb));
       }
       if (!ok) break;
-      // Epilogue: total row sum over both groups, then this group's 128 columns of O.
-      row_sum[g * kHeadsTile + h] = l;
-      __syncwarp();
-      if (lane == 0) ptx::mbar_arrive(bar(kBarRowSum));
+      // Epilogue: the row sum over both CTAs' keys, then this CTA's 256 columns of O.
       wt.where = (5 << 24) | int(useq & 0xFFFFFF);
-      if (!wt.wait<false>(bar(kBarRowSum), useq & 1u)) break;
-      l = row_sum[h] + row_sum[kHeadsTile + h];
+      ptx::st_async_b32(lsum_remote, __float_as_uint(l), lsum_full_r + 8u * sw);
+      if (!wt.wait<true>(bar(kBarLsumFull + sw), useq & 1u)) break;
+      const float l_peer = *reinterpret_cast<const float*>(sm + kSmLsum + 4 * h);
+      __syncwarp();
+      if (lane == 0) ptx::mbar_expect_tx(bar(kBarLsumFull + sw), 32 * 4);
+      const float l_tot = rank == 0 ? l + l_peer : l_peer + l;
       if (!wt.wait<false>(bar(kBarOFull), useq & 1u)) break;
       __syncwarp();
       ptx::tc_fence_after();
-      const float inv_l = 1.f / l;
-      if (rank == 0 && g == 0 && h < a.heads) {
-        const float lse = (m_used + log2f(l)) * kLn2;
+      const float inv_l = 1.f / l_tot;
+      if (rank == 0 && h < a.heads) {
+        const float lse = (m_used + log2f(l_tot)) * kLn2;
         if (s.slot >= 0) meta.part_lse[(long long)s.slot * kHeadsTile + h] = lse;
         else a.lse[(long long)s.u * a.heads + h] = lse;
       }
-      const int col0 = kValueHalf * int(rank) + 128 * g;
-      for (int c = 0; c < 128; c += 32) {
+      for (int c = 0; c < kValueHalf; c += 32) {
         uint32_t v[32];
         __syncwarp();  // TMEM loads are warp-collective; lanes past the head count rejoin here
-        ptx::tmem_ld16(tmem + lane_base + kTmemO + 128 * g + c,
-                       *reinterpret_cast<uint32_t(*)[16]>(&v[0]));
-        ptx::tmem_ld16(tmem + lane_base + kTmemO + 128 * g + c + 16,
+        ptx::tmem_ld16(tmem + lane_base + kTmemO + c, *reinterpret_cast<uint32_t(*)[16]>(&v[0]));
+        ptx::tmem_ld16(tmem + lane_base + kTmemO + c + 16,
                        *reinterpret_cast<uint32_t(*)[16]>(&v[16]));
         ptx::tmem_wait_ld();
         if (h >= a.heads) {
@@ -687,9 +716,9 @@ __global__ void __launch_bounds__(kThreads, 1)
               s.slot >= 0
                   ? reinterpret_cast<float4*>(meta.part_out +
                                               ((long long)s.slot * kHeadsTile + h) * kValueDim +
-                                              col0 + c)
+                                              vdim0 + c)
                   : reinterpret_cast<float4*>(a.out + s.u * a.out_stride_t + h * a.out_stride_h +
-                                              (long long)(col0 + c) * 4);
+                                              (long long)(vdim0 + c) * 4);
 #pragma unroll
           for (int k = 0; k < 8; ++k)
             dst[k] = make_float4(__uint_as_float(v[4 * k]) * inv_l,
@@ -703,7 +732,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             pkd[k] = ptx::pack_bf16x2(__uint_as_float(v[2 * k]) * inv_l,
                                       __uint_as_float(v[2 * k + 1]) * inv_l);
           uint4* dst = reinterpret_cast<uint4*>(a.out + s.u * a.out_stride_t +
-                                                h * a.out_stride_h + (long long)(col0 + c) * 2);
+                                                h * a.out_stride_h + (long long)(vdim0 + c) * 2);
 #pragma unroll
           for (int k = 0; k < 4; ++k)
             dst[k] = make_uint4(pkd[4 * k], pkd[4 * k + 1], pkd[4 * k + 2], pkd[4 * k + 3]);
@@ -1080,27 +1109,19 @@ int32_t launch(const TqMlaParams* params, void* workspace, uint64_t workspace_by
                                       S, (long long)params->slots, (long long)params->pages,
                                       pairs);
   if (params->pages > 0) {
-    CUtensorMap tq_rope, tkv, tkv_rope;
+    CUtensorMap tq_map, tkv;
     const uint64_t width = params->qk_width;
     const cuuint64_t qdims[3] = {width, params->heads, params->tokens};
     const cuuint64_t qstr[2] = {s.q.strides_bytes[1], s.q.strides_bytes[0]};
-    const cuuint32_t qbox_r[3] = {32, cuuint32_t(H), 1};
+    const cuuint32_t qbox[3] = {64, cuuint32_t(H), 1};
     const cuuint64_t kdims[2] = {width, pool_rows};
     const cuuint64_t kstr[1] = {params->row_stride};
-    const cuuint32_t kbox[2] = {64, 64};
-    const cuuint32_t kbox_r[2] = {32, 64};
+    const cuuint32_t kbox[2] = {64, uint32_t(kKeysPerCta)};
     const void* qa = reinterpret_cast<const void*>(s.q.device_address);
     const void* ka = reinterpret_cast<const void*>(s.kv.device_address);
-    if (!encode_bf16(&tkv, ka, 2, kdims, kstr, kbox, CU_TENSOR_MAP_SWIZZLE_128B))
+    if (!encode_bf16(&tq_map, qa, 3, qdims, qstr, qbox, CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !encode_bf16(&tkv, ka, 2, kdims, kstr, kbox, CU_TENSOR_MAP_SWIZZLE_128B))
       return set_err(err, "tensor_map", TQ_ERR_CUDA);
-    if (rope) {
-      if (!encode_bf16(&tq_rope, qa, 3, qdims, qstr, qbox_r, CU_TENSOR_MAP_SWIZZLE_64B) ||
-          !encode_bf16(&tkv_rope, ka, 2, kdims, kstr, kbox_r, CU_TENSOR_MAP_SWIZZLE_64B))
-        return set_err(err, "tensor_map", TQ_ERR_CUDA);
-    } else {
-      tq_rope = tkv;
-      tkv_rope = tkv;
-    }
     MainArgs a;
     a.meta = m;
     a.q = reinterpret_cast<const char*>(s.q.device_address);
@@ -1131,8 +1152,8 @@ int32_t launch(const TqMlaParams* params, void* workspace, uint64_t workspace_by
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    cudaError_t e = rope ? cudaLaunchKernelEx(&cfg, mla_paged_kernel<true>, tq_rope, tkv, tkv_rope, a)
-                         : cudaLaunchKernelEx(&cfg, mla_paged_kernel<false>, tq_rope, tkv, tkv_rope, a);
+    cudaError_t e = rope ? cudaLaunchKernelEx(&cfg, mla_paged_kernel<true>, tq_map, tkv, a)
+                         : cudaLaunchKernelEx(&cfg, mla_paged_kernel<false>, tq_map, tkv, a);
     if (e != cudaSuccess) return set_err(err, "launch", TQ_ERR_CUDA);
   }
   combine_kernel<<<2 * pairs * kCombineBlocksPerJob, 256, 0, st>>>(

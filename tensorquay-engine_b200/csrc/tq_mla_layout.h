@@ -2,13 +2,15 @@
 //
 // One CTA pair (a cluster of two, one CTA per SM) processes one query token at a time against a
 // range of 64-row KV pages. CTA rank r owns
-//   - the K-slice of QK^T: dims [256r, 256r+256) of the latent part (query slice held in TMEM),
-//     plus dims [512+32r, +32) of the RoPE part for 576-wide rows (query slice in shared memory);
-//   - the V-slice of PV and of the output: dims [256r, 256r+256).
-// Each CTA sends its partial score tile (all 128 heads) to the peer with asynchronous remote
-// stores that complete on the peer's mbarrier, and adds the peer's tile to its own. f32 addition is commutative, so both CTAs hold
-// bit-identical scores and compute bit-identical softmax statistics and probabilities; each then
-// runs PV for its half of the value dimension. Two softmax warpgroups split each page's 64 keys.
+//   - the keys [32r, 32r + 32) of every page for QK^T and the softmax: S_r = Q K_r^T over the
+//     full query width (M = 128 heads, N = 32 keys), with the query's first 384 dims in TMEM
+//     and the rest in shared memory;
+//   - the value dims [256r, 256r + 256) for PV and the output: O_r += P V[:, 256r:256r+256]
+//     over all 64 keys, its own keys' P from TMEM and the peer's P from shared memory.
+// Per page the CTAs exchange only bf16 probabilities and one f32 reference maximum per head
+// row (8.5 KB each way), pushed with asynchronous remote stores that complete on the receiver's
+// mbarrier. Both CTAs derive the same running maximum, so the two halves of O share one
+// normalisation.
 #pragma once
 
 #include <cstdint>
@@ -17,70 +19,75 @@ namespace tq {
 namespace mla {
 
 constexpr int kPageRows = 64;
+constexpr int kKeysPerCta = 32;
 constexpr int kHeadsTile = 128;  // UMMA M
 constexpr int kValueDim = 512;
 constexpr int kValueHalf = 256;  // per CTA
 constexpr int kStages = 3;
-constexpr int kSoftmaxGroups = 2;  // warpgroups splitting the 64 keys of a page
-constexpr int kSoftmaxWarps = 4 * kSoftmaxGroups;
+constexpr int kSoftmaxWarps = 4;
 constexpr int kSoftmaxThreads = 32 * kSoftmaxWarps;
-constexpr int kThreads = 64 + kSoftmaxThreads;  // warp 0 TMA, warp 1 MMA, then softmax
-constexpr int kKeysPerGroup = kPageRows / kSoftmaxGroups;  // 32
+constexpr int kThreads = 64 + kSoftmaxThreads;  // warp 0 TMA, warp 1 MMA, warps 2-5 softmax
+constexpr int kQTmemDims = 384;                 // query dims held in TMEM (A operand)
 
 // Shared memory (byte offsets from a 1024-aligned base).
-constexpr uint32_t kSmQRope = 0;             // [128 rows x 64 B], 64B swizzle
-constexpr uint32_t kSmKv = 8192;             // kStages x stage
-constexpr uint32_t kKvChunkBytes = 8192;     // [64 rows x 128 B], 128B swizzle
-constexpr uint32_t kKvRopeOffset = 32768;    // [64 rows x 64 B] inside a stage
-constexpr uint32_t kKvRopeBytes = 4096;
-constexpr uint32_t kStageBytes = 36864;
-// Partial-score tiles received from the peer, f32, double-buffered by page parity. A tile is
-// [group][lane quarter][8 chunks][32 lanes][16 B]: each softmax warp owns one 4 KB block holding
-// its 32 rows x 32 keys, chunk-major, so that a warp's store or load of one chunk touches 512
-// contiguous bytes.
-constexpr uint32_t kTileBytes = 32768;
-constexpr uint32_t kGroupTileBytes = kTileBytes / kSoftmaxGroups;
-constexpr uint32_t kWarpTileBytes = kGroupTileBytes / 4;
-constexpr uint32_t kSmXbuf = kSmKv + kStages * kStageBytes;  // [2] tiles
-constexpr uint32_t kSmRowMax = kSmXbuf + 2 * kTileBytes;      // f32 [2 parity][groups][128]
-constexpr uint32_t kSmRowSum = kSmRowMax + 2 * kSoftmaxGroups * kHeadsTile * 4;  // f32 [groups][128]
-constexpr uint32_t kSmBars = kSmRowSum + kSoftmaxGroups * kHeadsTile * 4;
-constexpr int kNumBars = 25;
+// Query dims [384, width): up to 3 chunks of [128 rows x 64 dims] bf16, 128B swizzle.
+constexpr uint32_t kSmQ = 0;
+constexpr uint32_t kQChunkBytes = 16384;
+constexpr uint32_t kSmKv = 3 * kQChunkBytes;
+// A stage holds one page: this CTA's 32 keys x all 64-dim chunks (up to 9), then the peer's 32
+// keys x this CTA's 4 value chunks. Each chunk is [32 rows x 128 B], 128B swizzle.
+constexpr uint32_t kKvChunkBytes = 4096;
+constexpr int kQkChunksMax = 9;
+constexpr uint32_t kPvxOffset = kQkChunksMax * kKvChunkBytes;
+constexpr uint32_t kStageBytes = kPvxOffset + 4 * kKvChunkBytes;
+// Peer probabilities, double-buffered by page parity: bf16 [4 key chunks][128 rows][8 keys]
+// (no-swizzle K-major UMMA layout: 8-row groups 128 B apart, key chunks 2 KB apart), then the
+// peer's f32 reference maximum per row.
+constexpr uint32_t kPChunkBytes = 2048;
+constexpr uint32_t kPBytes = 4 * kPChunkBytes;
+constexpr uint32_t kPMsgBytes = kPBytes + kHeadsTile * 4;
+constexpr uint32_t kSmPeer = kSmKv + kStages * kStageBytes;
+constexpr uint32_t kSmLsum = kSmPeer + 2 * kPMsgBytes;  // peer's f32 row sums
+constexpr uint32_t kSmBars = kSmLsum + kHeadsTile * 4;
+constexpr int kNumBars = 46;
 constexpr uint32_t kSmMisc = kSmBars + kNumBars * 8;  // tmem base holder, abort flag
 constexpr uint32_t kSmUsed = kSmMisc + 16;
 constexpr uint32_t kSmBytes = kSmUsed + 1024;          // slack for 1024-byte alignment
 
+// Bytes one softmax warp receives per page (its 32 rows of P and of the reference maximum).
+constexpr uint32_t kWarpMsgBytes = 32 * 64 + 32 * 4;
+
 static_assert(kSmKv % 1024 == 0 && kStageBytes % 1024 == 0, "swizzle alignment");
-static_assert(kSmXbuf % 1024 == 0, "tile alignment");
+static_assert(kSmPeer % 128 == 0, "operand alignment");
 static_assert(kSmBars % 8 == 0, "mbarrier alignment");
 static_assert(kSmBytes <= 232448, "shared memory per CTA");
 
 // Barrier indices.
 enum Bar : int {
-  kBarKvFull = 0,                      // [kStages] TMA transaction barriers
-  kBarKvEmpty = kBarKvFull + kStages,  // [kStages] PV done with the stage
-  kBarQRopeFull = kBarKvEmpty + kStages,  // TMA of the RoPE query slice
-  kBarQTmemFull,                       // latent query slice written to TMEM (one per group-0 warp)
-  kBarQEmpty,                          // all QK MMAs of the segment done
-  kBarSFull,                           // [2]
-  kBarPFull = kBarSFull + 2,           // [2], one arrival per softmax warp
-  kBarPvDone = kBarPFull + 2,          // [2]
+  kBarKvFull = 0,                       // [kStages] TMA transaction barriers
+  kBarKvEmpty = kBarKvFull + kStages,   // [kStages] PV done with the stage
+  kBarQSmemFull = kBarKvEmpty + kStages,  // TMA of the shared-memory query dims
+  kBarQTmemFull,                        // TMEM query dims written (one arrival per softmax warp)
+  kBarQEmpty,                           // all QK MMAs of the segment done
+  kBarSFull,                            // [2]
+  kBarPFull = kBarSFull + 2,            // [2] both halves of P ready (one arrival per warp)
+  kBarPvDone = kBarPFull + 2,           // [2]
   kBarOFull = kBarPvDone + 2,
-  kBarOFree,                           // one arrival per softmax warp
-  kBarXbFull,                          // [2] peer tile landed: armed locally with 32 KB expected
-  kBarXbFree = kBarXbFull + 2,         // [2] peer consumed my tile: one remote arrival per peer warp
-  kBarRowMax = kBarXbFree + 2,         // [2] both groups' partial row maxima written (per warp)
-  kBarRowSum = kBarRowMax + 2,         // both groups' partial row sums written (per warp)
-  kBarDrain,
+  kBarOFree,                            // one arrival per softmax warp
+  kBarMsgFull,                          // [2][4] peer warp's P rows + maxima landed (tx bytes)
+  kBarMsgFree = kBarMsgFull + 8,        // [2][4] peer warp may overwrite (one remote arrival)
+  kBarLsumFull = kBarMsgFree + 8,       // [4] peer warp's row sums landed (tx bytes)
+  kBarSpare = kBarLsumFull + 4,         // [8] unused
+  kBarDrain = kBarSpare + 8,
   kBarCount
 };
 static_assert(kBarCount == kNumBars, "barrier count");
 
 // TMEM columns (512 allocated).
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kTmemS = 0;     // [2] x 64 columns: f32 scores, then bf16 P in the first 32
-constexpr uint32_t kTmemQ = 128;   // 128 columns: latent query slice, bf16 pairs (A operand)
-constexpr uint32_t kTmemO = 256;   // 256 columns of f32 output half
+constexpr uint32_t kTmemS = 0;    // [2] x 32 columns: f32 scores, then bf16 P in the first 16
+constexpr uint32_t kTmemQ = 64;   // 192 columns: query dims [0, 384) as bf16 pairs (A operand)
+constexpr uint32_t kTmemO = 256;  // 256 columns of f32 output half
 
 // Workspace header words.
 enum Header : int {

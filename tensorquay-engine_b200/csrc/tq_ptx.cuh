@@ -66,6 +66,11 @@ __device__ __forceinline__ void st_async_v4(uint32_t addr, uint32_t a, uint32_t 
       :: "r"(addr), "r"(a), "r"(b), "r"(c), "r"(d), "r"(remote_bar) : "memory");
 }
 
+__device__ __forceinline__ void st_async_b32(uint32_t addr, uint32_t a, uint32_t remote_bar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.b32 [%0], %1, [%2];"
+               :: "r"(addr), "r"(a), "r"(remote_bar) : "memory");
+}
+
 // ---- mbarriers ------------------------------------------------------------------------------
 
 __device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
