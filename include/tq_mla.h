@@ -153,6 +153,12 @@ int32_t tq_mla_combine(const TqCombineParams* params, void* stream);
 /* Device error flag of the last launch that used `workspace` (synchronises `stream`). */
 int32_t tq_mla_read_device_error(const void* workspace, void* stream, int32_t* flags);
 
+/* Measurement hook, no reference counterpart. Makes later tq_mla_decode / tq_mla_prefill calls
+ * on the calling thread record `begin_event` right before and `end_event` right after the
+ * attention kernel, on the launch stream (both are cudaEvent_t created by the caller). Pass two
+ * nulls to switch it off; exactly one null is TQ_ERR_INVALID_ARGUMENT. */
+int32_t tq_mla_set_kernel_timer(void* begin_event, void* end_event);
+
 /* Philox4x32-10 test stream (host). tq_philox_words fills out[count]; an overflowing range
  * returns TQ_ERR_RANGE and leaves `out` untouched. */
 void tq_philox_block(const uint32_t counter[4], const uint32_t key[2], uint32_t out[4]);
@@ -160,7 +166,7 @@ int32_t tq_philox_words(uint64_t seed, uint64_t stream_id, uint64_t start, uint3
                         uint64_t count);
 float tq_philox_uniform_f32(uint32_t word);
 
-/* Seeded synthetic inputs on the device (Box-Muller normals rounded to bf16; see DESIGN).
+/* Seeded synthetic inputs on the device (Box-Muller normals rounded to bf16).
  *   tq_gen_normal_bf16: dst[i] = normal(seed, stream_id, start + i) for i < count.
  *   tq_gen_kv_pool: fills every row of the pool with NaN, then writes normal rows for each
  *   sequence's cached positions through the page table (normal index (tok_off[b]+p)*width+d). */

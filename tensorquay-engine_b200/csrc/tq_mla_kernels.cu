@@ -299,7 +299,8 @@ struct Waiter {
 template <bool kRope>
 __global__ void __launch_bounds__(kThreads, 1)
     mla_paged_kernel(const __grid_constant__ CUtensorMap tm_q,
-                     const __grid_constant__ CUtensorMap tm_kv, const MainArgs a) {
+                     const __grid_constant__ CUtensorMap tm_kv,
+                     const __grid_constant__ CUtensorMap tm_v, const MainArgs a) {
   constexpr int kQkChunks = kRope ? 9 : 8;               // 64-dim chunks of the query width
   constexpr int kQSmemChunks = kQkChunks - kQTmemDims / 64;
   constexpr uint32_t kStageLoadBytes = (kQkChunks + 4) * kKvChunkBytes;
@@ -346,6 +347,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     ptx::fence_mbar_init_cluster();
     ptx::tma_prefetch_desc(&tm_q);
     ptx::tma_prefetch_desc(&tm_kv);
+    ptx::tma_prefetch_desc(&tm_v);
   }
   // Query rows past the head count stay zero for the whole kernel (TMA writes rows < heads).
   if (a.heads < kHeadsTile) {
@@ -403,12 +405,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           const uint32_t dst = base + kSmKv + stage * kStageBytes;
           const uint32_t fb = bar(kBarKvFull + stage);
+          // Two requests per stage (the TMA unit's cost is largely per request): this CTA's keys
+          // across every 64-dim chunk, then the peer's keys across this CTA's value chunks. The
+          // map's axes are {64 dims, pool row, chunk}, so a box lands as [chunk][key][128 B].
           ptx::mbar_expect_tx(fb, kStageLoadBytes);
-          for (int c = 0; c < kQkChunks; ++c)
-            ptx::tma_load_2d(dst + c * kKvChunkBytes, &tm_kv, fb, 64 * c, int(row) + key0);
-          for (int c = 0; c < 4; ++c)
-            ptx::tma_load_2d(dst + kPvxOffset + c * kKvChunkBytes, &tm_kv, fb, vdim0 + 64 * c,
-                             int(row) + kKeysPerCta - key0);
+          ptx::tma_load_3d(dst, &tm_kv, fb, 0, int(row) + key0, 0);
+          ptx::tma_load_3d(dst + kPvxOffset, &tm_v, fb, 0, int(row) + kKeysPerCta - key0,
+                           vdim0 / 64);
         }
       }
       // Drain: every issued copy has landed before the CTA may exit.
@@ -1068,6 +1071,11 @@ int32_t set_err(TqContractError* err, const char* field, int32_t kind) {
   return kind;
 }
 
+// Optional events recorded on the launch stream right before and right after the attention
+// kernel (per calling thread; both null = off). Instrumentation for measuring the kernel alone.
+thread_local cudaEvent_t t_timer_begin = nullptr;
+thread_local cudaEvent_t t_timer_end = nullptr;
+
 int32_t launch(const TqMlaParams* params, void* workspace, uint64_t workspace_bytes, void* stream,
                TqContractError* err) {
   if (!params_intact(params)) return set_err(err, "params", TQ_ERR_PARAMS);
@@ -1109,18 +1117,22 @@ int32_t launch(const TqMlaParams* params, void* workspace, uint64_t workspace_by
                                       S, (long long)params->slots, (long long)params->pages,
                                       pairs);
   if (params->pages > 0) {
-    CUtensorMap tq_map, tkv;
+    CUtensorMap tq_map, tkv, tv;
     const uint64_t width = params->qk_width;
     const cuuint64_t qdims[3] = {width, params->heads, params->tokens};
     const cuuint64_t qstr[2] = {s.q.strides_bytes[1], s.q.strides_bytes[0]};
     const cuuint32_t qbox[3] = {64, cuuint32_t(H), 1};
-    const cuuint64_t kdims[2] = {width, pool_rows};
-    const cuuint64_t kstr[1] = {params->row_stride};
-    const cuuint32_t kbox[2] = {64, uint32_t(kKeysPerCta)};
+    // Pool rows seen as {64 dims, row, 64-dim chunk}: strides row_stride and 128 B, so one box
+    // covers several chunks of a run of rows and lands chunk-major in shared memory.
+    const cuuint64_t kdims[3] = {64, pool_rows, width / 64};
+    const cuuint64_t kstr[2] = {params->row_stride, 128};
+    const cuuint32_t kbox[3] = {64, uint32_t(kKeysPerCta), uint32_t(width / 64)};
+    const cuuint32_t vbox[3] = {64, uint32_t(kKeysPerCta), uint32_t(kValueHalf / 64)};
     const void* qa = reinterpret_cast<const void*>(s.q.device_address);
     const void* ka = reinterpret_cast<const void*>(s.kv.device_address);
     if (!encode_bf16(&tq_map, qa, 3, qdims, qstr, qbox, CU_TENSOR_MAP_SWIZZLE_128B) ||
-        !encode_bf16(&tkv, ka, 2, kdims, kstr, kbox, CU_TENSOR_MAP_SWIZZLE_128B))
+        !encode_bf16(&tkv, ka, 3, kdims, kstr, kbox, CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !encode_bf16(&tv, ka, 3, kdims, kstr, vbox, CU_TENSOR_MAP_SWIZZLE_128B))
       return set_err(err, "tensor_map", TQ_ERR_CUDA);
     MainArgs a;
     a.meta = m;
@@ -1152,9 +1164,13 @@ int32_t launch(const TqMlaParams* params, void* workspace, uint64_t workspace_by
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    cudaError_t e = rope ? cudaLaunchKernelEx(&cfg, mla_paged_kernel<true>, tq_map, tkv, a)
-                         : cudaLaunchKernelEx(&cfg, mla_paged_kernel<false>, tq_map, tkv, a);
+    if (t_timer_begin && cudaEventRecord(t_timer_begin, st) != cudaSuccess)
+      return set_err(err, "timer", TQ_ERR_CUDA);
+    cudaError_t e = rope ? cudaLaunchKernelEx(&cfg, mla_paged_kernel<true>, tq_map, tkv, tv, a)
+                         : cudaLaunchKernelEx(&cfg, mla_paged_kernel<false>, tq_map, tkv, tv, a);
     if (e != cudaSuccess) return set_err(err, "launch", TQ_ERR_CUDA);
+    if (t_timer_end && cudaEventRecord(t_timer_end, st) != cudaSuccess)
+      return set_err(err, "timer", TQ_ERR_CUDA);
   }
   combine_kernel<<<2 * pairs * kCombineBlocksPerJob, 256, 0, st>>>(
       m, reinterpret_cast<char*>(s.out.device_address), (long long)s.out.strides_bytes[0],
@@ -1216,6 +1232,13 @@ int32_t tq_mla_combine(const TqCombineParams* p, void* stream) {
       (long long)p->out_stride_head, p->out_dtype == TQ_DTYPE_F32,
       reinterpret_cast<float*>(p->lse));
   return cudaGetLastError() == cudaSuccess ? TQ_OK : TQ_ERR_CUDA;
+}
+
+int32_t tq_mla_set_kernel_timer(void* begin_event, void* end_event) {
+  if ((begin_event == nullptr) != (end_event == nullptr)) return TQ_ERR_INVALID_ARGUMENT;
+  t_timer_begin = static_cast<cudaEvent_t>(begin_event);
+  t_timer_end = static_cast<cudaEvent_t>(end_event);
+  return TQ_OK;
 }
 
 int32_t tq_mla_read_device_error(const void* workspace, void* stream, int32_t* flags) {

@@ -154,6 +154,17 @@ class MlaLaunch:
         return flags.value
 
 
+def set_kernel_timer(begin=None, end=None):
+    """Record ``begin``/``end`` (``torch.cuda.Event``, already recorded once so that they exist)
+    around the attention kernel of later launches from this thread; no arguments switches it off.
+    """
+    if (begin is None) != (end is None):
+        raise ValueError("set_kernel_timer needs both events or neither")
+    b = ctypes.c_void_p(begin.cuda_event) if begin is not None else None
+    e = ctypes.c_void_p(end.cuda_event) if end is not None else None
+    raise_for(lib.tq_mla_set_kernel_timer(b, e))
+
+
 def mla_decode(q, kv, page_table, seq_id, q_pos, kv_len, *, scale, query_counts=None, out=None,
                lse=None, out_dtype=torch.bfloat16, prefill=False, kv_format=None, stream=None):
     """Dense paged absorbed-MLA attention: returns ``(out [T,H,512], lse [T,H])``.
