@@ -153,6 +153,20 @@ int32_t tq_mla_combine(const TqCombineParams* params, void* stream);
 /* Device error flag of the last launch that used `workspace` (synchronises `stream`). */
 int32_t tq_mla_read_device_error(const void* workspace, void* stream, int32_t* flags);
 
+/* Decode without any device allocation. No counterpart in the reference: it exists for callers
+ * that cannot allocate device memory at launch time, such as an engine that hands all GPU memory
+ * to its own pool up front, or code running where cudaMalloc is not allowed.
+ * Same plan, inputs, outputs and results as tq_mla_decode, but the workspace is a fixed array
+ * inside this library of TQ_MLA_NO_ALLOC_WORKSPACE_BYTES (42 MiB), which every GPU that loads the
+ * library keeps until the process exits. A plan whose tq_mla_workspace_bytes exceeds that size
+ * returns TQ_ERR_WORKSPACE with field "no_alloc_workspace" (on a B200 that means more than about
+ * 160 000 query tokens). The first call on each device looks up the array's device address, so
+ * make it before capturing any stream. All calls share the one array: calls that may overlap on
+ * the GPU (other streams, other threads) race and must be serialised by the caller. Device error
+ * flags of these calls cannot be read back (tq_mla_read_device_error needs the workspace). */
+#define TQ_MLA_NO_ALLOC_WORKSPACE_BYTES (42ull << 20)
+int32_t tq_mla_decode_no_alloc(const TqMlaParams* params, void* stream, TqContractError* err);
+
 /* Measurement hook, no reference counterpart. Makes later tq_mla_decode / tq_mla_prefill calls
  * on the calling thread record `begin_event` right before and `end_event` right after the
  * attention kernel, on the launch stream (both are cudaEvent_t created by the caller). Pass two

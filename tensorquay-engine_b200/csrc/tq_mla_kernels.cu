@@ -1180,6 +1180,30 @@ int32_t launch(const TqMlaParams* params, void* workspace, uint64_t workspace_by
   return TQ_OK;
 }
 
+// ---------------------------------------------------------------------------------------------
+// Fixed scratch for callers that cannot allocate device memory (see tq_mla_decode_no_alloc).
+// Every GPU that loads this library holds these TQ_MLA_NO_ALLOC_WORKSPACE_BYTES until exit.
+
+static __device__ __align__(256) uint8_t g_no_alloc_workspace[TQ_MLA_NO_ALLOC_WORKSPACE_BYTES];
+
+// Device address of g_no_alloc_workspace on `device`, looked up once per device with that
+// device current (in host code the array's name is only a host-side stand-in).
+void* no_alloc_workspace(int device) {
+  static std::mutex mu;
+  static void* cache[128] = {nullptr};
+  std::lock_guard<std::mutex> lock(mu);
+  if (device < 0 || device >= 128) return nullptr;
+  if (!cache[device]) {
+    void* ptr = nullptr;
+    if (cudaGetSymbolAddress(&ptr, g_no_alloc_workspace) != cudaSuccess) {
+      cudaGetLastError();
+      return nullptr;
+    }
+    cache[device] = ptr;
+  }
+  return cache[device];
+}
+
 }  // namespace mla
 }  // namespace tq
 
@@ -1211,6 +1235,25 @@ int32_t tq_mla_decode(const TqMlaParams* params, void* workspace, uint64_t works
   if (params && tq::params_intact(params) && params->max_queries_per_sequence == 0)
     return set_err(err, "params", TQ_ERR_PARAMS);  // a prefill plan
   return launch(params, workspace, workspace_bytes, stream, err);
+}
+
+int32_t tq_mla_decode_no_alloc(const TqMlaParams* params, void* stream, TqContractError* err) {
+  if (!params || !tq::params_intact(params)) return set_err(err, "params", TQ_ERR_PARAMS);
+  if (params->max_queries_per_sequence == 0) return set_err(err, "params", TQ_ERR_PARAMS);
+  if (!params->should_launch) return set_err(err, nullptr, TQ_OK);
+  int device = 0;
+  if (cudaGetDevice(&device) != cudaSuccess) return set_err(err, "device", TQ_ERR_CUDA);
+  const int pairs = pairs_for_device(device);
+  if (pairs <= 0) return set_err(err, "device", TQ_ERR_CUDA);
+  TqWorkspaceLayout L;
+  layout_for(params->tokens, pairs, &L);
+  if (L.total_bytes > TQ_MLA_NO_ALLOC_WORKSPACE_BYTES)
+    return set_err(err, "no_alloc_workspace", TQ_ERR_WORKSPACE);
+  void* ws = no_alloc_workspace(device);
+  if (!ws) return set_err(err, "no_alloc_workspace", TQ_ERR_CUDA);
+  // The scheduler kernel rewrites every workspace word the later kernels read, so the previous
+  // call's contents need no clearing.
+  return launch(params, ws, TQ_MLA_NO_ALLOC_WORKSPACE_BYTES, stream, err);
 }
 
 int32_t tq_mla_prefill(const TqMlaParams* params, void* workspace, uint64_t workspace_bytes,

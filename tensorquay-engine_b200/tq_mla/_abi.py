@@ -93,6 +93,7 @@ PROTOTYPES = {
     "tq_mla_combine": (_I32, [_P(TqCombineParams), _VP]),
     "tq_mla_read_device_error": (_I32, [_VP, _VP, _P(_I32)]),
     "tq_mla_set_kernel_timer": (_I32, [_VP, _VP]),
+    "tq_mla_decode_no_alloc": (_I32, [_P(TqMlaParams), _VP, _P(TqContractError)]),
     "tq_philox_block": (None, [_P(ctypes.c_uint32), _P(ctypes.c_uint32), _P(ctypes.c_uint32)]),
     "tq_philox_words": (_I32, [_U64, _U64, _U64, _P(ctypes.c_uint32), _U64]),
     "tq_philox_uniform_f32": (ctypes.c_float, [ctypes.c_uint32]),
