@@ -240,6 +240,8 @@ def traffic_from_profiles(workload_name):
     if not p.exists():
         return None
     for line in p.read_text().splitlines():
+        if line.lstrip().startswith("#"):
+            continue
         kv = dict(x.split("=", 1) for x in line.split() if "=" in x)
         if kv.get("workload") == workload_name and "dram_bytes_per_launch" in kv:
             return float(kv["dram_bytes_per_launch"])
