@@ -382,6 +382,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       Seg s;
       bool ok = true;
       while (ok && walker.next(meta, s)) {
+        // Page-table entries are read three pages ahead of their loads: a dependent global read
+        // at load time would add its latency to every page's arrival.
+        const int* pt = a.page_table + (long long)a.seq_id[s.u] * a.slots;
+        int pf0 = s.np > 0 ? pt[s.p0] : 0;
+        int pf1 = s.np > 1 ? pt[s.p0 + 1] : 0;
+        int pf2 = s.np > 2 ? pt[s.p0 + 2] : 0;
         wt.where = (1 << 24) | int(it & 0xFFFFFF);
         if (!wt.wait<false>(bar(kBarQEmpty), (useq & 1u) ^ 1u)) break;
         ptx::mbar_expect_tx(bar(kBarQSmemFull), uint32_t(a.heads) * 128 * kQSmemChunks);
@@ -389,15 +395,17 @@ __global__ void __launch_bounds__(kThreads, 1)
           ptx::tma_load_3d(base + kSmQ + k * kQChunkBytes, &tm_q, bar(kBarQSmemFull),
                            kQTmemDims + 64 * k, 0, s.u);
         ++useq;
-        const int* pt = a.page_table + (long long)a.seq_id[s.u] * a.slots;
         for (int j = 0; j < s.np; ++j, ++it) {
           const uint32_t stage = it % kStages;
+          const int page = pf0;
+          pf0 = pf1;
+          pf1 = pf2;
+          pf2 = j + 3 < s.np ? pt[s.p0 + j + 3] : 0;
           wt.where = (1 << 24) | int(it & 0xFFFFFF);
           if (!wt.wait<false>(bar(kBarKvEmpty + stage), ((it / kStages) & 1u) ^ 1u)) {
             ok = false;
             break;
           }
-          const int page = pt[s.p0 + j];
           long long row = (long long)page * kPageRows;
           if (page < 0 || row >= a.pool_rows) {
             atomicOr(a.meta.header + kHdrError, TQ_DEV_PAGE_RANGE);
@@ -426,99 +434,127 @@ __global__ void __launch_bounds__(kThreads, 1)
     // QK^T: S[128 x 32] = Q x K_own^T, 24 steps with the query from TMEM, then the remaining
     // query chunks from shared memory. PV: O_half[128 x 256] += P[128 x 64] V[64 x 256]: the
     // own keys' P from TMEM (aliased over the scores), the peer keys' P from shared memory.
-    // S buffer j%2 is rewritten by QK(j+2) only after PV(j) was issued: the tensor pipe
-    // executes in issue order, so P(j) is consumed before it is overwritten.
+    // Issue order per step j: QK(j) is already queued; wait for P(j-1) and for page j+1's data;
+    // commit S(j); PV(j-1); QK(j+1). Every wait of a step comes before its commits: a barrier
+    // test issued behind a pending tcgen05.commit stalls until that commit's MMAs have finished,
+    // which would let the tensor pipe run dry between QK^T and PV. S buffer j%2 is rewritten by
+    // QK(j+2) only after PV(j) was issued: the pipe executes in issue order, so P(j) is read
+    // before it is overwritten.
+    // The whole warp runs this loop converged: waits are made warp-uniform, and each MMA and
+    // commit is issued by one lane elected inside the instruction sequence.
     constexpr uint32_t idesc_qk = ptx::idesc_bf16(128, 32, 0);
     constexpr uint32_t idesc_pv = ptx::idesc_bf16(128, 256, 1);
     uint32_t it = 0, useq = 0;
     Seg s;
     bool ok = true;
+    auto wait_all = [&](uint32_t b, uint32_t parity) -> bool {
+      const bool r = wt.wait<false>(b, parity);
+      return __all_sync(0xFFFFFFFFu, r);
+    };
+    // Waits for page itq (page `p` of its sequence, `n` visible keys) and zeroes its rows past
+    // the cached length (NaN-poisoned slots) before any MMA reads them.
+    auto prepare = [&](uint32_t itq, int p, int n) -> bool {
+      const uint32_t stage = itq % kStages;
+      if (!wait_all(bar(kBarKvFull + stage), (itq / kStages) & 1u)) return false;
+      const int valid = min(kPageRows, n - p * kPageRows);
+      const int own_valid = max(0, min(kKeysPerCta, valid - key0));
+      const int peer_valid = max(0, min(kKeysPerCta, valid - (kKeysPerCta - key0)));
+      if (own_valid < kKeysPerCta || peer_valid < kKeysPerCta) {
+        uint8_t* st_ptr = sm + kSmKv + stage * kStageBytes;
+        const int own_words = (kKeysPerCta - own_valid) * 8;
+        const int peer_words = (kKeysPerCta - peer_valid) * 8;
+        for (int i = lane; i < kQkChunks * own_words; i += 32) {
+          const int c = i / own_words, w = i % own_words;
+          reinterpret_cast<uint4*>(st_ptr + c * kKvChunkBytes + own_valid * 128)[w] =
+              make_uint4(0, 0, 0, 0);
+        }
+        for (int i = lane; i < 4 * peer_words; i += 32) {
+          const int c = i / peer_words, w = i % peer_words;
+          reinterpret_cast<uint4*>(st_ptr + kPvxOffset + c * kKvChunkBytes + peer_valid * 128)[w] =
+              make_uint4(0, 0, 0, 0);
+        }
+        ptx::fence_proxy_async_smem();
+        __syncwarp();
+      }
+      return true;
+    };
+    // Descriptors advance by compile-time offsets (start field = address >> 4; shared addresses
+    // stay below 256 KB, so the 14-bit field never carries).
+    auto issue_qk = [&](uint32_t itq) {
+      const uint32_t stage_base = base + kSmKv + (itq % kStages) * kStageBytes;
+      const uint32_t d = tmem + kTmemS + (itq & 1u) * 32;
+      const uint64_t kd = ptx::smem_desc(stage_base, 16, 1024, 2);
+      const uint64_t qd = ptx::smem_desc(base + kSmQ, 16, 1024, 2);
+#pragma unroll
+      for (int kk = 0; kk < kQTmemDims / 16; ++kk)
+        ptx::mma_ts_warp(d, tmem + kTmemQ + kk * 8,
+                         kd + uint64_t(((kk >> 2) * kKvChunkBytes + (kk & 3) * 32) >> 4),
+                         idesc_qk, kk != 0);
+#pragma unroll
+      for (int kk = 0; kk < kQSmemChunks * 4; ++kk)
+        ptx::mma_ss_warp(d, qd + uint64_t(((kk >> 2) * kQChunkBytes + (kk & 3) * 32) >> 4),
+                         kd + uint64_t((((kQTmemDims / 64) + (kk >> 2)) * kKvChunkBytes +
+                                        (kk & 3) * 32) >> 4),
+                         idesc_qk, 1);
+    };
+    auto issue_pv = [&](uint32_t itp, bool first) {
+      const uint32_t stage = itp % kStages, pb = itp & 1u;
+      const uint32_t stage_base = base + kSmKv + stage * kStageBytes;
+      // V as B, MN-major: 64-dim chunks 4 KB apart (LBO), 8-key groups 1 KB apart (SBO).
+      const uint64_t vd =
+          ptx::smem_desc(stage_base + (vdim0 / 64) * kKvChunkBytes, kKvChunkBytes, 1024, 2);
+      const uint64_t xd = ptx::smem_desc(stage_base + kPvxOffset, kKvChunkBytes, 1024, 2);
+      // Peer P, K-major without swizzle: 8-row groups 128 B apart (SBO), the two 8-key chunks of
+      // a step 2 KB apart (LBO).
+      const uint64_t pd = ptx::smem_desc(base + kSmPeer + pb * kPMsgBytes, kPChunkBytes, 128, 0);
+#pragma unroll
+      for (int kk = 0; kk < 2; ++kk)
+        ptx::mma_ts_warp(tmem + kTmemO, tmem + kTmemS + pb * 32 + kk * 8,
+                         vd + uint64_t((kk * 2048) >> 4), idesc_pv, (!first || kk > 0) ? 1u : 0u);
+#pragma unroll
+      for (int kk = 0; kk < 2; ++kk)
+        ptx::mma_ss_warp(tmem + kTmemO, pd + uint64_t((kk * 2 * kPChunkBytes) >> 4),
+                         xd + uint64_t((kk * 2048) >> 4), idesc_pv, 1u);
+      ptx::mma_commit_warp(bar(kBarKvEmpty + stage));
+      ptx::mma_commit_warp(bar(kBarPvDone + pb));
+    };
     while (ok && walker.next(meta, s)) {
       const int n = meta.unit_n[s.u];
-      wt.where = (2 << 24) | int(it & 0xFFFFFF);
-      if (!wt.wait<false>(bar(kBarQTmemFull), useq & 1u)) break;
-      if (!wt.wait<false>(bar(kBarQSmemFull), useq & 1u)) break;
-      ptx::tc_fence_after();
       const uint32_t it0 = it;
-      for (int j = 0; j <= s.np && ok; ++j) {
-        wt.where = (2 << 24) | int((it0 + j) & 0xFFFFFF);
-        if (j < s.np) {
-          const uint32_t itq = it0 + j, stage = itq % kStages, sb = itq & 1u;
-          if (!wt.wait<false>(bar(kBarKvFull + stage), (itq / kStages) & 1u)) { ok = false; break; }
-          const uint32_t stage_base = base + kSmKv + stage * kStageBytes;
-          const int valid = min(kPageRows, n - (s.p0 + j) * kPageRows);
-          const int own_valid = max(0, min(kKeysPerCta, valid - key0));
-          const int peer_valid = max(0, min(kKeysPerCta, valid - (kKeysPerCta - key0)));
-          if (own_valid < kKeysPerCta || peer_valid < kKeysPerCta) {
-            // Rows past the cached length (NaN-poisoned slots) become zeros before any MMA.
-            uint8_t* st_ptr = sm + kSmKv + stage * kStageBytes;
-            const int own_words = (kKeysPerCta - own_valid) * 8;
-            const int peer_words = (kKeysPerCta - peer_valid) * 8;
-            for (int i = lane; i < kQkChunks * own_words; i += 32) {
-              const int c = i / own_words, w = i % own_words;
-              reinterpret_cast<uint4*>(st_ptr + c * kKvChunkBytes + own_valid * 128)[w] =
-                  make_uint4(0, 0, 0, 0);
-            }
-            for (int i = lane; i < 4 * peer_words; i += 32) {
-              const int c = i / peer_words, w = i % peer_words;
-              reinterpret_cast<uint4*>(st_ptr + kPvxOffset + c * kKvChunkBytes +
-                                       peer_valid * 128)[w] = make_uint4(0, 0, 0, 0);
-            }
-            ptx::fence_proxy_async_smem();
-            __syncwarp();
-          }
-          ptx::tc_fence_after();
-          if (lane == 0) {
-            // Descriptors advance by compile-time offsets (start field = address >> 4; shared
-            // addresses stay below 256 KB, so the 14-bit field never carries).
-            const uint32_t d = tmem + kTmemS + sb * 32;
-            const uint64_t kd = ptx::smem_desc(stage_base, 16, 1024, 2);
-            const uint64_t qd = ptx::smem_desc(base + kSmQ, 16, 1024, 2);
-#pragma unroll
-            for (int kk = 0; kk < kQTmemDims / 16; ++kk)
-              ptx::mma_ts(d, tmem + kTmemQ + kk * 8,
-                          kd + uint64_t(((kk >> 2) * kKvChunkBytes + (kk & 3) * 32) >> 4),
-                          idesc_qk, kk != 0);
-#pragma unroll
-            for (int kk = 0; kk < kQSmemChunks * 4; ++kk)
-              ptx::mma_ss(d, qd + uint64_t(((kk >> 2) * kQChunkBytes + (kk & 3) * 32) >> 4),
-                          kd + uint64_t((((kQTmemDims / 64) + (kk >> 2)) * kKvChunkBytes +
-                                         (kk & 3) * 32) >> 4),
-                          idesc_qk, 1);
-            ptx::mma_commit(bar(kBarSFull + sb));
-            if (j == s.np - 1) ptx::mma_commit(bar(kBarQEmpty));
-          }
-          __syncwarp();
+      wt.where = (2 << 24) | int(it0 & 0xFFFFFF);
+      if (!wait_all(bar(kBarQTmemFull), useq & 1u)) break;
+      if (!wait_all(bar(kBarQSmemFull), useq & 1u)) break;
+      if (!prepare(it0, s.p0, n)) break;
+      ptx::tc_fence_after();
+      issue_qk(it0);
+      __syncwarp();
+      for (int j = 0; j < s.np; ++j) {
+        const uint32_t itq = it0 + j;
+        const bool has_next = j + 1 < s.np;
+        wt.where = (2 << 24) | int(itq & 0xFFFFFF);
+        if (j >= 1) {
+          const uint32_t itp = itq - 1;
+          if (j == 1 && !wait_all(bar(kBarOFree), (useq & 1u) ^ 1u)) { ok = false; break; }
+          if (!wait_all(bar(kBarPFull + (itp & 1u)), (itp >> 1) & 1u)) { ok = false; break; }
         }
-        if (j > 0) {
-          const uint32_t itp = it0 + j - 1, stage = itp % kStages, pb = itp & 1u;
-          if (j == 1 && !wt.wait<false>(bar(kBarOFree), (useq & 1u) ^ 1u)) { ok = false; break; }
-          if (!wt.wait<false>(bar(kBarPFull + pb), (itp >> 1) & 1u)) { ok = false; break; }
-          ptx::tc_fence_after();
-          if (lane == 0) {
-            const uint32_t stage_base = base + kSmKv + stage * kStageBytes;
-            // V as B, MN-major: 64-dim chunks 4 KB apart (LBO), 8-key groups 1 KB apart (SBO).
-            const uint64_t vd = ptx::smem_desc(stage_base + (vdim0 / 64) * kKvChunkBytes,
-                                               kKvChunkBytes, 1024, 2);
-            const uint64_t xd = ptx::smem_desc(stage_base + kPvxOffset, kKvChunkBytes, 1024, 2);
-            // Peer P, K-major without swizzle: 8-row groups 128 B apart (SBO), the two 8-key
-            // chunks of a step 2 KB apart (LBO).
-            const uint64_t pd = ptx::smem_desc(base + kSmPeer + pb * kPMsgBytes, kPChunkBytes, 128, 0);
-#pragma unroll
-            for (int kk = 0; kk < 2; ++kk)
-              ptx::mma_ts(tmem + kTmemO, tmem + kTmemS + pb * 32 + kk * 8,
-                          vd + uint64_t((kk * 2048) >> 4), idesc_pv, (j > 1 || kk > 0) ? 1u : 0u);
-#pragma unroll
-            for (int kk = 0; kk < 2; ++kk)
-              ptx::mma_ss(tmem + kTmemO, pd + uint64_t((kk * 2 * kPChunkBytes) >> 4),
-                          xd + uint64_t((kk * 2048) >> 4), idesc_pv, 1u);
-            ptx::mma_commit(bar(kBarKvEmpty + stage));
-            ptx::mma_commit(bar(kBarPvDone + pb));
-            if (j == s.np) ptx::mma_commit(bar(kBarOFull));
-          }
-          __syncwarp();
-        }
+        if (has_next && !prepare(itq + 1, s.p0 + j + 1, n)) { ok = false; break; }
+        ptx::tc_fence_after();
+        ptx::mma_commit_warp(bar(kBarSFull + (itq & 1u)));
+        if (!has_next) ptx::mma_commit_warp(bar(kBarQEmpty));
+        if (j >= 1) issue_pv(itq - 1, j == 1);
+        if (has_next) issue_qk(itq + 1);
+        __syncwarp();
       }
+      if (!ok) break;
+      // PV of the segment's last page completes this token's output.
+      const uint32_t itp = it0 + s.np - 1;
+      wt.where = (2 << 24) | int(itp & 0xFFFFFF);
+      if (s.np == 1 && !wait_all(bar(kBarOFree), (useq & 1u) ^ 1u)) { ok = false; break; }
+      if (!wait_all(bar(kBarPFull + (itp & 1u)), (itp >> 1) & 1u)) { ok = false; break; }
+      ptx::tc_fence_after();
+      issue_pv(itp, s.np == 1);
+      ptx::mma_commit_warp(bar(kBarOFull));
+      __syncwarp();
       it = it0 + s.np;
       ++useq;
     }
