@@ -434,12 +434,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     // QK^T: S[128 x 32] = Q x K_own^T, 24 steps with the query from TMEM, then the remaining
     // query chunks from shared memory. PV: O_half[128 x 256] += P[128 x 64] V[64 x 256]: the
     // own keys' P from TMEM (aliased over the scores), the peer keys' P from shared memory.
-    // Issue order per step j: QK(j) is already queued; wait for P(j-1) and for page j+1's data;
-    // commit S(j); PV(j-1); QK(j+1). Every wait of a step comes before its commits: a barrier
-    // test issued behind a pending tcgen05.commit stalls until that commit's MMAs have finished,
-    // which would let the tensor pipe run dry between QK^T and PV. S buffer j%2 is rewritten by
-    // QK(j+2) only after PV(j) was issued: the pipe executes in issue order, so P(j) is read
-    // before it is overwritten.
+    // Issue order per step j (QK(j) already issued and its S(j) committed, so the softmax of
+    // page j runs while the pipe works): wait for P(j-1); PV(j-1) and its commits; wait for page
+    // j+1's data; QK(j+1) and the commit of S(j+1). A barrier test issued behind a pending
+    // tcgen05.commit stalls until that commit's MMAs have finished: the P wait overlaps QK(j),
+    // and the data wait makes PV(j-1) finish (freeing its KV stage) before QK(j+1) starts.
+    // S buffer j%2 is rewritten by QK(j+2) only after PV(j) was issued: the pipe executes in
+    // issue order, so P(j) is read before it is overwritten.
     // The whole warp runs this loop converged: waits are made warp-uniform, and each MMA and
     // commit is issued by one lane elected inside the instruction sequence.
     constexpr uint32_t idesc_qk = ptx::idesc_bf16(128, 32, 0);
@@ -527,22 +528,28 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!prepare(it0, s.p0, n)) break;
       ptx::tc_fence_after();
       issue_qk(it0);
-      __syncwarp();
+      ptx::mma_commit_warp(bar(kBarSFull + (it0 & 1u)));
+      if (s.np == 1) ptx::mma_commit_warp(bar(kBarQEmpty));
       for (int j = 0; j < s.np; ++j) {
-        const uint32_t itq = it0 + j;
+        const uint32_t itq = it0 + j;  // QK(itq) is issued and committed
         const bool has_next = j + 1 < s.np;
         wt.where = (2 << 24) | int(itq & 0xFFFFFF);
         if (j >= 1) {
           const uint32_t itp = itq - 1;
           if (j == 1 && !wait_all(bar(kBarOFree), (useq & 1u) ^ 1u)) { ok = false; break; }
           if (!wait_all(bar(kBarPFull + (itp & 1u)), (itp >> 1) & 1u)) { ok = false; break; }
+          ptx::tc_fence_after();
+          issue_pv(itp, j == 1);
         }
+        // Behind PV's commits this wait also holds QK(j+1) back until PV(j-1) has finished, so
+        // the pipe does not interleave the two and the KV stage is released as early as possible.
         if (has_next && !prepare(itq + 1, s.p0 + j + 1, n)) { ok = false; break; }
         ptx::tc_fence_after();
-        ptx::mma_commit_warp(bar(kBarSFull + (itq & 1u)));
-        if (!has_next) ptx::mma_commit_warp(bar(kBarQEmpty));
-        if (j >= 1) issue_pv(itq - 1, j == 1);
-        if (has_next) issue_qk(itq + 1);
+        if (has_next) {
+          issue_qk(itq + 1);
+          ptx::mma_commit_warp(bar(kBarSFull + ((itq + 1) & 1u)));
+          if (j + 2 == s.np) ptx::mma_commit_warp(bar(kBarQEmpty));
+        }
         __syncwarp();
       }
       if (!ok) break;
