@@ -304,6 +304,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr int kQkChunks = kRope ? 9 : 8;               // 64-dim chunks of the query width
   constexpr int kQSmemChunks = kQkChunks - kQTmemDims / 64;
   constexpr uint32_t kStageLoadBytes = (kQkChunks + 4) * kKvChunkBytes;
+  constexpr uint32_t kOwnGroupBytes = kQkChunks * kAtomBytes;  // 8 own keys x all chunks
+  constexpr uint32_t kPeerGroupBytes = 4 * kAtomBytes;         // 8 peer keys x value chunks
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = ptx::smem_addr(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
@@ -415,11 +417,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t fb = bar(kBarKvFull + stage);
           // Two requests per stage (the TMA unit's cost is largely per request): this CTA's keys
           // across every 64-dim chunk, then the peer's keys across this CTA's value chunks. The
-          // map's axes are {64 dims, pool row, chunk}, so a box lands as [chunk][key][128 B].
+          // map's axes are {64 dims, key in group, chunk, 8-key group}: a box reads each 8-row
+          // group's contiguous bytes in one go and lands as [group][chunk][8 keys x 128 B].
           ptx::mbar_expect_tx(fb, kStageLoadBytes);
-          ptx::tma_load_3d(dst, &tm_kv, fb, 0, int(row) + key0, 0);
-          ptx::tma_load_3d(dst + kPvxOffset, &tm_v, fb, 0, int(row) + kKeysPerCta - key0,
-                           vdim0 / 64);
+          ptx::tma_load_4d(dst, &tm_kv, fb, 0, 0, 0, int((row + key0) / 8));
+          ptx::tma_load_4d(dst + kPvxOffset, &tm_v, fb, 0, 0, vdim0 / 64,
+                           int((row + kKeysPerCta - key0) / 8));
         }
       }
       // Drain: every issued copy has landed before the CTA may exit.
@@ -464,15 +467,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint8_t* st_ptr = sm + kSmKv + stage * kStageBytes;
         const int own_words = (kKeysPerCta - own_valid) * 8;
         const int peer_words = (kKeysPerCta - peer_valid) * 8;
+        // Key r of chunk c sits at (r / 8) * group bytes + c * 1 KB + (r % 8) * 128 B.
         for (int i = lane; i < kQkChunks * own_words; i += 32) {
-          const int c = i / own_words, w = i % own_words;
-          reinterpret_cast<uint4*>(st_ptr + c * kKvChunkBytes + own_valid * 128)[w] =
-              make_uint4(0, 0, 0, 0);
+          const int c = i / own_words, r = own_valid + (i % own_words) / 8, w = i % 8;
+          reinterpret_cast<uint4*>(st_ptr + (r >> 3) * kOwnGroupBytes + c * kAtomBytes +
+                                   (r & 7) * 128)[w] = make_uint4(0, 0, 0, 0);
         }
         for (int i = lane; i < 4 * peer_words; i += 32) {
-          const int c = i / peer_words, w = i % peer_words;
-          reinterpret_cast<uint4*>(st_ptr + kPvxOffset + c * kKvChunkBytes + peer_valid * 128)[w] =
-              make_uint4(0, 0, 0, 0);
+          const int c = i / peer_words, r = peer_valid + (i % peer_words) / 8, w = i % 8;
+          reinterpret_cast<uint4*>(st_ptr + kPvxOffset + (r >> 3) * kPeerGroupBytes +
+                                   c * kAtomBytes + (r & 7) * 128)[w] = make_uint4(0, 0, 0, 0);
         }
         ptx::fence_proxy_async_smem();
         __syncwarp();
@@ -484,38 +488,41 @@ __global__ void __launch_bounds__(kThreads, 1)
     auto issue_qk = [&](uint32_t itq) {
       const uint32_t stage_base = base + kSmKv + (itq % kStages) * kStageBytes;
       const uint32_t d = tmem + kTmemS + (itq & 1u) * 32;
-      const uint64_t kd = ptx::smem_desc(stage_base, 16, 1024, 2);
+      // K-major, 128B swizzle: 8-key groups kOwnGroupBytes apart, chunks 1 KB apart.
+      const uint64_t kd = ptx::smem_desc(stage_base, 16, kOwnGroupBytes, 2);
       const uint64_t qd = ptx::smem_desc(base + kSmQ, 16, 1024, 2);
 #pragma unroll
       for (int kk = 0; kk < kQTmemDims / 16; ++kk)
         ptx::mma_ts_warp(d, tmem + kTmemQ + kk * 8,
-                         kd + uint64_t(((kk >> 2) * kKvChunkBytes + (kk & 3) * 32) >> 4),
+                         kd + uint64_t(((kk >> 2) * kAtomBytes + (kk & 3) * 32) >> 4),
                          idesc_qk, kk != 0);
 #pragma unroll
       for (int kk = 0; kk < kQSmemChunks * 4; ++kk)
         ptx::mma_ss_warp(d, qd + uint64_t(((kk >> 2) * kQChunkBytes + (kk & 3) * 32) >> 4),
-                         kd + uint64_t((((kQTmemDims / 64) + (kk >> 2)) * kKvChunkBytes +
+                         kd + uint64_t((((kQTmemDims / 64) + (kk >> 2)) * kAtomBytes +
                                         (kk & 3) * 32) >> 4),
                          idesc_qk, 1);
     };
     auto issue_pv = [&](uint32_t itp, bool first) {
       const uint32_t stage = itp % kStages, pb = itp & 1u;
       const uint32_t stage_base = base + kSmKv + stage * kStageBytes;
-      // V as B, MN-major: 64-dim chunks 4 KB apart (LBO), 8-key groups 1 KB apart (SBO).
+      // V as B, MN-major: 64-dim chunks 1 KB apart (LBO), 8-key groups one group apart (SBO).
       const uint64_t vd =
-          ptx::smem_desc(stage_base + (vdim0 / 64) * kKvChunkBytes, kKvChunkBytes, 1024, 2);
-      const uint64_t xd = ptx::smem_desc(stage_base + kPvxOffset, kKvChunkBytes, 1024, 2);
+          ptx::smem_desc(stage_base + (vdim0 / 64) * kAtomBytes, kAtomBytes, kOwnGroupBytes, 2);
+      const uint64_t xd =
+          ptx::smem_desc(stage_base + kPvxOffset, kAtomBytes, kPeerGroupBytes, 2);
       // Peer P, K-major without swizzle: 8-row groups 128 B apart (SBO), the two 8-key chunks of
       // a step 2 KB apart (LBO).
       const uint64_t pd = ptx::smem_desc(base + kSmPeer + pb * kPMsgBytes, kPChunkBytes, 128, 0);
 #pragma unroll
       for (int kk = 0; kk < 2; ++kk)
         ptx::mma_ts_warp(tmem + kTmemO, tmem + kTmemS + pb * 32 + kk * 8,
-                         vd + uint64_t((kk * 2048) >> 4), idesc_pv, (!first || kk > 0) ? 1u : 0u);
+                         vd + uint64_t((kk * 2 * kOwnGroupBytes) >> 4), idesc_pv,
+                         (!first || kk > 0) ? 1u : 0u);
 #pragma unroll
       for (int kk = 0; kk < 2; ++kk)
         ptx::mma_ss_warp(tmem + kTmemO, pd + uint64_t((kk * 2 * kPChunkBytes) >> 4),
-                         xd + uint64_t((kk * 2048) >> 4), idesc_pv, 1u);
+                         xd + uint64_t((kk * 2 * kPeerGroupBytes) >> 4), idesc_pv, 1u);
       ptx::mma_commit_warp(bar(kBarKvEmpty + stage));
       ptx::mma_commit_warp(bar(kBarPvDone + pb));
     };
@@ -1016,7 +1023,7 @@ bool encode_bf16(CUtensorMap* map, const void* addr, int rank, const cuuint64_t*
                  const cuuint64_t* strides, const cuuint32_t* box, CUtensorMapSwizzle swz) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return false;
-  cuuint32_t elem_strides[3] = {1, 1, 1};
+  cuuint32_t elem_strides[5] = {1, 1, 1, 1, 1};
   return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, cuuint32_t(rank), const_cast<void*>(addr), dims,
             strides, box, elem_strides, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
@@ -1165,17 +1172,18 @@ int32_t launch(const TqMlaParams* params, void* workspace, uint64_t workspace_by
     const cuuint64_t qdims[3] = {width, params->heads, params->tokens};
     const cuuint64_t qstr[2] = {s.q.strides_bytes[1], s.q.strides_bytes[0]};
     const cuuint32_t qbox[3] = {64, cuuint32_t(H), 1};
-    // Pool rows seen as {64 dims, row, 64-dim chunk}: strides row_stride and 128 B, so one box
-    // covers several chunks of a run of rows and lands chunk-major in shared memory.
-    const cuuint64_t kdims[3] = {64, pool_rows, width / 64};
-    const cuuint64_t kstr[2] = {params->row_stride, 128};
-    const cuuint32_t kbox[3] = {64, uint32_t(kKeysPerCta), uint32_t(width / 64)};
-    const cuuint32_t vbox[3] = {64, uint32_t(kKeysPerCta), uint32_t(kValueHalf / 64)};
+    // Pool rows seen as {64 dims, row in an 8-row group, 64-dim chunk, 8-row group}: strides
+    // row_stride, 128 B and 8 rows. A box reads whole 8-row groups (contiguous bytes) at a time
+    // and lands as [group][chunk][8 rows x 128 B], a 128B-swizzled UMMA operand layout.
+    const cuuint64_t kdims[4] = {64, 8, width / 64, pool_rows / 8};
+    const cuuint64_t kstr[3] = {params->row_stride, 128, 8 * params->row_stride};
+    const cuuint32_t kbox[4] = {64, 8, uint32_t(width / 64), uint32_t(kKeysPerCta / 8)};
+    const cuuint32_t vbox[4] = {64, 8, uint32_t(kValueHalf / 64), uint32_t(kKeysPerCta / 8)};
     const void* qa = reinterpret_cast<const void*>(s.q.device_address);
     const void* ka = reinterpret_cast<const void*>(s.kv.device_address);
     if (!encode_bf16(&tq_map, qa, 3, qdims, qstr, qbox, CU_TENSOR_MAP_SWIZZLE_128B) ||
-        !encode_bf16(&tkv, ka, 3, kdims, kstr, kbox, CU_TENSOR_MAP_SWIZZLE_128B) ||
-        !encode_bf16(&tv, ka, 3, kdims, kstr, vbox, CU_TENSOR_MAP_SWIZZLE_128B))
+        !encode_bf16(&tkv, ka, 4, kdims, kstr, kbox, CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !encode_bf16(&tv, ka, 4, kdims, kstr, vbox, CU_TENSOR_MAP_SWIZZLE_128B))
       return set_err(err, "tensor_map", TQ_ERR_CUDA);
     MainArgs a;
     a.meta = m;

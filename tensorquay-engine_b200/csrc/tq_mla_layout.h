@@ -35,8 +35,10 @@ constexpr uint32_t kSmQ = 0;
 constexpr uint32_t kQChunkBytes = 16384;
 constexpr uint32_t kSmKv = 3 * kQChunkBytes;
 // A stage holds one page: this CTA's 32 keys x all 64-dim chunks (up to 9), then the peer's 32
-// keys x this CTA's 4 value chunks. Each chunk is [32 rows x 128 B], 128B swizzle.
-constexpr uint32_t kKvChunkBytes = 4096;
+// keys x this CTA's 4 value chunks, both as [8-key group][chunk][8 keys x 128 B] (128B swizzle):
+// 1 KB atoms, chunks 1 KB apart, key groups (chunks x 1 KB) apart.
+constexpr uint32_t kAtomBytes = 1024;
+constexpr uint32_t kKvChunkBytes = 4096;  // one chunk of 32 keys
 constexpr int kQkChunksMax = 9;
 constexpr uint32_t kPvxOffset = kQkChunksMax * kKvChunkBytes;
 constexpr uint32_t kStageBytes = kPvxOffset + 4 * kKvChunkBytes;

@@ -152,6 +152,14 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const void* tmap, uint
       :: "r"(dst), "l"(tmap), "r"(bar), "r"(x), "r"(y), "r"(z) : "memory");
 }
 
+__device__ __forceinline__ void tma_load_4d(uint32_t dst, const void* tmap, uint32_t bar, int x,
+                                            int y, int z, int w) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6}], [%2];"
+      :: "r"(dst), "l"(tmap), "r"(bar), "r"(x), "r"(y), "r"(z), "r"(w) : "memory");
+}
+
 // ---- tcgen05 ---------------------------------------------------------------------------------
 
 __device__ __forceinline__ void tmem_alloc(uint32_t holder_smem, uint32_t ncols) {
