@@ -115,6 +115,7 @@ __global__ void __launch_bounds__(1024) schedule_kernel(Meta m, const int* __res
                                                         int pairs) {
   __shared__ long long sh[32];
   __shared__ int s_err;
+  ptx::grid_launch_dependents();  // the attention kernel may start its prologue meanwhile
   if (threadIdx.x == 0) s_err = 0;
   for (int c = threadIdx.x; c < pairs; c += blockDim.x) m.pair_begin[c] = -1;
   __syncthreads();
@@ -371,6 +372,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   ptx::tc_fence_after();
   const uint32_t tmem = *tmem_holder;
 
+  // Everything above overlaps the scheduler kernel; its outputs are read from here on. The
+  // combine grid may then launch early and wait for this grid in turn.
+  ptx::grid_dependency_wait();
+  ptx::grid_launch_dependents();
   SegWalker walker;
   walker.init(a.meta, pair, a.tokens);
   const Meta& meta = a.meta;
@@ -832,6 +837,7 @@ constexpr int kCombineBlocksPerJob = 8;
 __global__ void __launch_bounds__(256) combine_kernel(Meta m, char* out, long long st_t,
                                                       long long st_h, int out_f32, float* lse,
                                                       int heads) {
+  ptx::grid_dependency_wait();  // launched early; the attention kernel's results start here
   const int ncomb = m.header[kHdrNumCombine], nempty = m.header[kHdrNumEmpty];
   const int esize = out_f32 ? 4 : 2;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -1208,13 +1214,15 @@ int32_t launch(const TqMlaParams* params, void* workspace, uint64_t workspace_by
     cfg.blockDim = dim3(kThreads, 1, 1);
     cfg.dynamicSmemBytes = kSmBytes;
     cfg.stream = st;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = 2;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = 2;
     if (t_timer_begin && cudaEventRecord(t_timer_begin, st) != cudaSuccess)
       return set_err(err, "timer", TQ_ERR_CUDA);
     cudaError_t e = rope ? cudaLaunchKernelEx(&cfg, mla_paged_kernel<true>, tq_map, tkv, tv, a)
@@ -1223,10 +1231,24 @@ int32_t launch(const TqMlaParams* params, void* workspace, uint64_t workspace_by
     if (t_timer_end && cudaEventRecord(t_timer_end, st) != cudaSuccess)
       return set_err(err, "timer", TQ_ERR_CUDA);
   }
-  combine_kernel<<<2 * pairs * kCombineBlocksPerJob, 256, 0, st>>>(
-      m, reinterpret_cast<char*>(s.out.device_address), (long long)s.out.strides_bytes[0],
-      (long long)s.out.strides_bytes[1], s.out.dtype == TQ_DTYPE_F32,
-      reinterpret_cast<float*>(s.lse.device_address), H);
+  {
+    // Launched as a programmatic dependent of the attention kernel (or of the scheduler when
+    // there is no page): its blocks start early and wait inside the kernel.
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * pairs * kCombineBlocksPerJob, 1, 1);
+    cfg.blockDim = dim3(256, 1, 1);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaLaunchKernelEx(&cfg, combine_kernel, m, reinterpret_cast<char*>(s.out.device_address),
+                           (long long)s.out.strides_bytes[0], (long long)s.out.strides_bytes[1],
+                           int(s.out.dtype == TQ_DTYPE_F32),
+                           reinterpret_cast<float*>(s.lse.device_address), H) != cudaSuccess)
+      return set_err(err, "launch", TQ_ERR_CUDA);
+  }
   if (cudaGetLastError() != cudaSuccess) return set_err(err, "launch", TQ_ERR_CUDA);
   return TQ_OK;
 }

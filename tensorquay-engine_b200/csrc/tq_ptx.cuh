@@ -160,6 +160,16 @@ __device__ __forceinline__ void tma_load_4d(uint32_t dst, const void* tmap, uint
       :: "r"(dst), "l"(tmap), "r"(bar), "r"(x), "r"(y), "r"(z), "r"(w) : "memory");
 }
 
+// Programmatic dependent launch: the dependent grid may start early; it waits here until the
+// grids it depends on have completed and their memory is visible.
+__device__ __forceinline__ void grid_dependency_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+// Lets the grid that depends on this one start launching (its CTAs then wait as above).
+__device__ __forceinline__ void grid_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // ---- tcgen05 ---------------------------------------------------------------------------------
 
 __device__ __forceinline__ void tmem_alloc(uint32_t holder_smem, uint32_t ncols) {
