@@ -8,19 +8,22 @@
 // lse = -inf (mla_attention.py:147-148). The launch grid depends only on the device, never on the
 // data (docs/TEST-PLAN.md:205-206); split-KV partial results merge by log-sum-exp.
 //
-// Kernel structure (one CTA pair = cluster of 2, one CTA per SM):
-//   warp 0      TMA producer: Q slice per token, then 64-row KV pages through the page table
-//               (3-stage ring); pages outside the pool are fetched fully out of bounds (zeros)
-//               and flagged.
-//   warp 1      MMA issuer: S = Q_slice K_slice^T into TMEM (M=128 heads, N=64 keys), then
-//               O_half += P V_half with P read from TMEM (M=128, N=256, K=16 keys per step).
-//               It zeroes the rows of a partial last page before the MMAs read them, so the NaN
-//               poison of unused slots never reaches an accumulator.
-//   warps 2-5   softmax and epilogue: one thread per head row (its TMEM lane). Partial scores
-//               of the heads owned by the peer are sent to it through distributed shared memory;
-//               the owner adds both halves, applies the mask and an online softmax whose running
-//               maximum is only raised when it grows by more than 2^8 (exact after the final
-//               normalisation), and sends the bf16 probabilities back.
+// Kernel structure (one CTA pair = cluster of 2, one CTA per SM; rank r owns keys [32r, 32r+32)
+// of every page for QK^T and value dims [256r, 256r+256) for PV and the output):
+//   warp 0      TMA producer: the query's shared-memory slice per token, then per page this
+//               CTA's 32 keys across all chunks and the peer's 32 keys across this CTA's value
+//               chunks (3-stage ring, page-table entries read ahead); pages outside the pool are
+//               fetched fully out of bounds (zeros) and flagged.
+//   warp 1      MMA issuer (whole warp, one elected lane issues): S_r = Q K_r^T into TMEM
+//               (M=128 heads, N=32 keys), then O_r += P V_r (M=128, N=256, K=16 keys per step)
+//               with the own keys' P from TMEM and the peer keys' P from shared memory. It zeroes
+//               the rows of a partial last page before the MMAs read them, so the NaN poison of
+//               unused slots never reaches an accumulator.
+//   warps 2-5   softmax and epilogue: one thread per head row (its TMEM lane). Per page: scores
+//               to log2 units, mask, a candidate reference maximum (raised only when the page
+//               maximum grows by more than 2^8; exact after the final normalisation), bf16
+//               probabilities; the pair swaps probabilities and candidates through distributed
+//               shared memory so both derive the same running maximum for their halves of O.
 // Every wait is bounded (globaltimer); on timeout the CTA pair records TQ_DEV_WAIT_TIMEOUT,
 // drains its in-flight TMA and MMA work, frees TMEM and exits.
 
@@ -444,9 +447,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     // own keys' P from TMEM (aliased over the scores), the peer keys' P from shared memory.
     // Issue order per step j (QK(j) already issued and its S(j) committed, so the softmax of
     // page j runs while the pipe works): wait for P(j-1); PV(j-1) and its commits; wait for page
-    // j+1's data; QK(j+1) and the commit of S(j+1). A barrier test issued behind a pending
-    // tcgen05.commit stalls until that commit's MMAs have finished: the P wait overlaps QK(j),
-    // and the data wait makes PV(j-1) finish (freeing its KV stage) before QK(j+1) starts.
+    // j+1's data; QK(j+1) and the commit of S(j+1). Queued back to back, PV(j-1) and QK(j+1)
+    // interleave in the pipe and PV's stage release comes late (measured slower); with the data
+    // wait between them, PV(j-1) drains first and frees its KV stage for the producer sooner.
     // S buffer j%2 is rewritten by QK(j+2) only after PV(j) was issued: the pipe executes in
     // issue order, so P(j) is read before it is overwritten.
     // The whole warp runs this loop converged: waits are made warp-uniform, and each MMA and
@@ -553,8 +556,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           ptx::tc_fence_after();
           issue_pv(itp, j == 1);
         }
-        // Behind PV's commits this wait also holds QK(j+1) back until PV(j-1) has finished, so
-        // the pipe does not interleave the two and the KV stage is released as early as possible.
+        // Waiting here, after PV(j-1) was issued, keeps QK(j+1) out of the pipe until page j+1's
+        // data is in, which in practice lets PV(j-1) drain first and release its KV stage early.
         if (has_next && !prepare(itq + 1, s.p0 + j + 1, n)) { ok = false; break; }
         ptx::tc_fence_after();
         if (has_next) {
