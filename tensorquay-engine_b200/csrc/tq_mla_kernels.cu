@@ -391,10 +391,20 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t it = 0, useq = 0;
       Seg s;
       bool ok = true;
+      // A sequence with one query token has its KV rows read once per launch (by this pair,
+      // within a page's time): evict-first keeps them from displacing the page tables, queries
+      // and split partials in L2. Rows of a sequence with several query tokens (multi-token
+      // decode, prefill chunks; adjacent tokens) are read again and keep the normal priority.
+      const uint64_t policy_once = ptx::l2_policy_evict_first();
+      const uint64_t policy_reused = ptx::l2_policy_evict_normal();
       while (ok && walker.next(meta, s)) {
+        const int sq = a.seq_id[s.u];
+        const bool reused = (s.u > 0 && a.seq_id[s.u - 1] == sq) ||
+                            (s.u + 1 < a.tokens && a.seq_id[s.u + 1] == sq);
+        const uint64_t kv_policy = reused ? policy_reused : policy_once;
         // Page-table entries are read three pages ahead of their loads: a dependent global read
         // at load time would add its latency to every page's arrival.
-        const int* pt = a.page_table + (long long)a.seq_id[s.u] * a.slots;
+        const int* pt = a.page_table + (long long)sq * a.slots;
         int pf0 = s.np > 0 ? pt[s.p0] : 0;
         int pf1 = s.np > 1 ? pt[s.p0 + 1] : 0;
         int pf2 = s.np > 2 ? pt[s.p0 + 2] : 0;
@@ -428,9 +438,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           // map's axes are {64 dims, key in group, chunk, 8-key group}: a box reads each 8-row
           // group's contiguous bytes in one go and lands as [group][chunk][8 keys x 128 B].
           ptx::mbar_expect_tx(fb, kStageLoadBytes);
-          ptx::tma_load_4d(dst, &tm_kv, fb, 0, 0, 0, int((row + key0) / 8));
-          ptx::tma_load_4d(dst + kPvxOffset, &tm_v, fb, 0, 0, vdim0 / 64,
-                           int((row + kKeysPerCta - key0) / 8));
+          ptx::tma_load_4d_hint(dst, &tm_kv, fb, 0, 0, 0, int((row + key0) / 8), kv_policy);
+          ptx::tma_load_4d_hint(dst + kPvxOffset, &tm_v, fb, 0, 0, vdim0 / 64,
+                                int((row + kKeysPerCta - key0) / 8), kv_policy);
         }
       }
       // Drain: every issued copy has landed before the CTA may exit.
@@ -831,11 +841,11 @@ __device__ __forceinline__ void store8(char* base, int f32, const float (&v)[8])
   }
 }
 
-// Grid: kCombineBlocksPerJob blocks per possible split token (2 x pairs of them, an upper bound
-// that does not depend on the data). Block b merges heads [16 g, 16 g + 16), g = b % 8, of split
-// token b / 8: one warp per head row, 16 value dims per lane. Blocks without a split token
-// zero-fill the tokens that see no key.
-constexpr int kCombineBlocksPerJob = 8;
+// One thread per (split token, head, 8 value dims), grid-stride over a fixed grid. Each thread
+// merges its 8 dims over the token's partials four at a time: the loads of four partials are in
+// flight together, folded into a running maximum and sum of weights. Tokens that see no key are
+// zero-filled by the same grid.
+constexpr int kCombineBlocksPerPair = 16;
 
 __global__ void __launch_bounds__(256) combine_kernel(Meta m, char* out, long long st_t,
                                                       long long st_h, int out_f32, float* lse,
@@ -843,47 +853,56 @@ __global__ void __launch_bounds__(256) combine_kernel(Meta m, char* out, long lo
   ptx::grid_dependency_wait();  // launched early; the attention kernel's results start here
   const int ncomb = m.header[kHdrNumCombine], nempty = m.header[kHdrNumEmpty];
   const int esize = out_f32 ? 4 : 2;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int job = blockIdx.x / kCombineBlocksPerJob, group = blockIdx.x % kCombineBlocksPerJob;
-  if (job < ncomb) {
+  const long long items = (long long)ncomb * heads * 64;
+  for (long long t = blockIdx.x * 256ll + threadIdx.x; t < items; t += (long long)gridDim.x * 256) {
+    const int job = int(t / (heads * 64)), rem = int(t % (heads * 64));
+    const int h = rem >> 6, d0 = (rem & 63) * 8;
     const int u = m.combine_list[job];
     const int ns = m.unit_nsplit[u], off = m.unit_split_off[u];
-    for (int h = group * 16 + warp; h < min(heads, group * 16 + 16); h += 8) {
-      float mx = -INFINITY;
-      for (int i = 0; i < ns; ++i) mx = fmaxf(mx, m.part_lse[(long long)(off + i) * kHeadsTile + h]);
-      float acc[16];
+    float mx = -INFINITY, wsum = 0.f;
+    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    for (int i0 = 0; i0 < ns; i0 += 4) {
+      float li[4];
+      float4 x[4][2];
 #pragma unroll
-      for (int k = 0; k < 16; ++k) acc[k] = 0.f;
-      float wsum = 0.f;
-      for (int i = 0; i < ns; ++i) {
-        const float li = m.part_lse[(long long)(off + i) * kHeadsTile + h];
-        const float w = li == -INFINITY ? 0.f : expf(li - mx);
-        wsum += w;
-        const float4* src = reinterpret_cast<const float4*>(
-            m.part_out + ((long long)(off + i) * kHeadsTile + h) * kValueDim + lane * 16);
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const float4 x = src[k];
-          acc[4 * k] += w * x.x;
-          acc[4 * k + 1] += w * x.y;
-          acc[4 * k + 2] += w * x.z;
-          acc[4 * k + 3] += w * x.w;
+      for (int k = 0; k < 4; ++k) {
+        if (i0 + k < ns) {
+          const long long slot = off + i0 + k;
+          li[k] = __ldcg(m.part_lse + slot * kHeadsTile + h);
+          const float4* src =
+              reinterpret_cast<const float4*>(m.part_out + (slot * kHeadsTile + h) * kValueDim + d0);
+          x[k][0] = __ldcg(src);
+          x[k][1] = __ldcg(src + 1);
+        } else {
+          li[k] = -INFINITY;
+          x[k][0] = x[k][1] = make_float4(0.f, 0.f, 0.f, 0.f);
         }
       }
-      const float inv = wsum > 0.f ? 1.f / wsum : 0.f;
-      float lo[8], hi[8];
+      const float m4 = fmaxf(fmaxf(li[0], li[1]), fmaxf(li[2], li[3]));
+      if (m4 > mx) {
+        const float f = mx == -INFINITY ? 0.f : expf(mx - m4);
+        wsum *= f;
 #pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        lo[k] = acc[k] * inv;
-        hi[k] = acc[8 + k] * inv;
+        for (int k = 0; k < 8; ++k) acc[k] *= f;
+        mx = m4;
       }
-      char* dst = out + u * st_t + h * st_h + (long long)(lane * 16) * esize;
-      store8(dst, out_f32, lo);
-      store8(dst + 8 * esize, out_f32, hi);
-      if (lane == 0) lse[(long long)u * heads + h] = wsum > 0.f ? mx + logf(wsum) : -INFINITY;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float w = li[k] == -INFINITY ? 0.f : expf(li[k] - mx);
+        wsum += w;
+        acc[0] += w * x[k][0].x; acc[1] += w * x[k][0].y;
+        acc[2] += w * x[k][0].z; acc[3] += w * x[k][0].w;
+        acc[4] += w * x[k][1].x; acc[5] += w * x[k][1].y;
+        acc[6] += w * x[k][1].z; acc[7] += w * x[k][1].w;
+      }
     }
+    const float inv = wsum > 0.f ? 1.f / wsum : 0.f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) acc[k] *= inv;
+    store8(out + u * st_t + h * st_h + (long long)d0 * esize, out_f32, acc);
+    if (d0 == 0) lse[(long long)u * heads + h] = wsum > 0.f ? mx + logf(wsum) : -INFINITY;
   }
-  // Tokens with no visible key: zeros and lse = -inf, spread over every block.
+  // Tokens with no visible key: zeros and lse = -inf.
   const float z[8] = {0, 0, 0, 0, 0, 0, 0, 0};
   const long long tasks = (long long)nempty * heads * 64;
   for (long long t = blockIdx.x * 256ll + threadIdx.x; t < tasks; t += (long long)gridDim.x * 256) {
@@ -1238,7 +1257,7 @@ int32_t launch(const TqMlaParams* params, void* workspace, uint64_t workspace_by
     // Launched as a programmatic dependent of the attention kernel (or of the scheduler when
     // there is no page): its blocks start early and wait inside the kernel.
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(2 * pairs * kCombineBlocksPerJob, 1, 1);
+    cfg.gridDim = dim3(pairs * kCombineBlocksPerPair, 1, 1);
     cfg.blockDim = dim3(256, 1, 1);
     cfg.stream = st;
     cudaLaunchAttribute attr[1];

@@ -160,6 +160,30 @@ __device__ __forceinline__ void tma_load_4d(uint32_t dst, const void* tmap, uint
       :: "r"(dst), "l"(tmap), "r"(bar), "r"(x), "r"(y), "r"(z), "r"(w) : "memory");
 }
 
+// L2 policy for data read once: its lines are the first candidates for eviction, so a stream of
+// them does not push out lines that are read again soon (page tables, partial results).
+__device__ __forceinline__ uint64_t l2_policy_evict_first() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+
+// Default L2 priority, for data that is read again (by later tokens of the same sequence).
+__device__ __forceinline__ uint64_t l2_policy_evict_normal() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_normal.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+
+// tma_load_4d with an L2 cache policy (from l2_policy_evict_first or similar).
+__device__ __forceinline__ void tma_load_4d_hint(uint32_t dst, const void* tmap, uint32_t bar,
+                                                 int x, int y, int z, int w, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%3, %4, %5, %6}], [%2], %7;"
+      :: "r"(dst), "l"(tmap), "r"(bar), "r"(x), "r"(y), "r"(z), "r"(w), "l"(policy) : "memory");
+}
+
 // Programmatic dependent launch: the dependent grid may start early; it waits here until the
 // grids it depends on have completed and their memory is visible.
 __device__ __forceinline__ void grid_dependency_wait() {
