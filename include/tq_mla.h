@@ -123,7 +123,7 @@ typedef struct {
   uint64_t combine_list;  /* int32[T]                                                       */
   uint64_t empty_list;    /* int32[T]                                                       */
   uint64_t part_lse;      /* f32[2*pairs, 128]                                              */
-  uint64_t part_out;      /* f32[2*pairs, 128, 512]                                         */
+  uint64_t part_out;      /* f32[2*pairs, 128 column quads, 128 rows, 4]                    */
   int32_t pairs;          /* CTA pairs of the main kernel on this device                    */
 } TqWorkspaceLayout;
 

@@ -612,31 +612,46 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t lsum_full_r = ptx::map_peer(bar(kBarLsumFull), peer);
     const float c2 = a.scale_log2;
     uint32_t it = 0, useq = 0;
-    Seg s;
-    bool ok = true;
-    while (ok && walker.next(meta, s)) {
-      const int n = meta.unit_n[s.u];
-      // This token's query dims [0, 384) into TMEM once the previous segment's QK MMAs are done.
-      {
-        wt.where = (6 << 24) | int(useq & 0xFFFFFF);
-        if (!wt.wait<false>(bar(kBarQEmpty), (useq & 1u) ^ 1u)) break;
-        __syncwarp();
-        ptx::tc_fence_after();
-        const uint4* src = reinterpret_cast<const uint4*>(a.q + s.u * a.q_stride_t +
-                                                          h * a.q_stride_h);
-        for (int c = 0; c < kQTmemDims / 2; c += 16) {
+    // Segment `idx`'s query dims [0, 384) into TMEM once the previous segment's QK MMAs are done.
+    auto load_q = [&](const Seg& sq, uint32_t idx) -> bool {
+      wt.where = (6 << 24) | int(idx & 0xFFFFFF);
+      if (!wt.wait<false>(bar(kBarQEmpty), (idx & 1u) ^ 1u)) return false;
+      __syncwarp();
+      ptx::tc_fence_after();
+      const uint4* src = reinterpret_cast<const uint4*>(a.q + sq.u * a.q_stride_t +
+                                                        h * a.q_stride_h);
+      // 256 bytes of the row per batch: the loads of a batch are in flight together (the TMEM
+      // stores between batches are ordered with them).
+      for (int c = 0; c < kQTmemDims / 2; c += 64) {
+        uint4 x[16];
+#pragma unroll
+        for (int k = 0; k < 16; ++k) x[k] = h < a.heads ? src[c / 4 + k] : make_uint4(0, 0, 0, 0);
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
           uint32_t v[16];
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
-            const uint4 x = h < a.heads ? src[c / 4 + k] : make_uint4(0, 0, 0, 0);
-            v[4 * k] = x.x; v[4 * k + 1] = x.y; v[4 * k + 2] = x.z; v[4 * k + 3] = x.w;
+            v[4 * k] = x[4 * g + k].x; v[4 * k + 1] = x[4 * g + k].y;
+            v[4 * k + 2] = x[4 * g + k].z; v[4 * k + 3] = x[4 * g + k].w;
           }
-          ptx::tmem_st16(tmem + lane_base + kTmemQ + c, v);
+          ptx::tmem_st16(tmem + lane_base + kTmemQ + c + 16 * g, v);
         }
-        ptx::tmem_wait_st();
-        ptx::tc_fence_before();
-        __syncwarp();
-        if (lane == 0) ptx::mbar_arrive(bar(kBarQTmemFull));
+      }
+      ptx::tmem_wait_st();
+      ptx::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(bar(kBarQTmemFull));
+      return true;
+    };
+    Seg s, s_next;
+    bool ok = walker.next(meta, s) && load_q(s, 0);
+    while (ok) {
+      const int n = meta.unit_n[s.u];
+      // The next segment is usually the next token: its query row is pulled into L2 now, so the
+      // TMEM load before this segment's epilogue finds it there.
+      if (s.u + 1 < a.tokens && h < a.heads) {
+        const char* next_row = a.q + (s.u + 1) * a.q_stride_t + h * a.q_stride_h;
+        for (int k = 0; k <= kQTmemDims * 2; k += 128) ptx::prefetch_l2(next_row + k);
       }
       float m_used = -INFINITY, l = 0.f;
       for (int j = 0; j < s.np; ++j) {
@@ -756,6 +771,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) ptx::mbar_arrive(bar(kBarPFull + sb));
       }
       if (!ok) break;
+      // The next segment's query goes into TMEM before this epilogue, so its first QK MMAs
+      // overlap the epilogue.
+      const bool has_next = walker.next(meta, s_next);
+      if (has_next && !load_q(s_next, useq + 1)) break;
       // Epilogue: the row sum over both CTAs' keys, then this CTA's 256 columns of O.
       wt.where = (5 << 24) | int(useq & 0xFFFFFF);
       ptx::st_async_b32(lsum_remote, __float_as_uint(l), lsum_full_r + 8u * sw);
@@ -773,47 +792,66 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (s.slot >= 0) meta.part_lse[(long long)s.slot * kHeadsTile + h] = lse;
         else a.lse[(long long)s.u * a.heads + h] = lse;
       }
-      for (int c = 0; c < kValueHalf; c += 32) {
-        uint32_t v[32];
-        __syncwarp();  // TMEM loads are warp-collective; lanes past the head count rejoin here
-        ptx::tmem_ld16(tmem + lane_base + kTmemO + c, *reinterpret_cast<uint32_t(*)[16]>(&v[0]));
-        ptx::tmem_ld16(tmem + lane_base + kTmemO + c + 16,
-                       *reinterpret_cast<uint32_t(*)[16]>(&v[16]));
-        ptx::tmem_wait_ld();
+      // O leaves TMEM 32 columns at a time, the next chunk's load in flight while this one is
+      // stored. Split partials use the layout [slot][column quad][row] (float4), so each warp
+      // store writes 32 consecutive rows' quads: 512 contiguous bytes.
+      uint32_t v[2][32];
+      __syncwarp();
+      ptx::tmem_ld16(tmem + lane_base + kTmemO, *reinterpret_cast<uint32_t(*)[16]>(&v[0][0]));
+      ptx::tmem_ld16(tmem + lane_base + kTmemO + 16, *reinterpret_cast<uint32_t(*)[16]>(&v[0][16]));
+      ptx::tmem_wait_ld();
+#pragma unroll
+      for (int ci = 0; ci < kValueHalf / 32; ++ci) {
+        const int c = 32 * ci;
+        const uint32_t(&cur)[32] = v[ci & 1];
+        if (ci + 1 < kValueHalf / 32) {
+          __syncwarp();  // TMEM loads are warp-collective; lanes past the head count rejoin here
+          ptx::tmem_ld16(tmem + lane_base + kTmemO + c + 32,
+                         *reinterpret_cast<uint32_t(*)[16]>(&v[(ci + 1) & 1][0]));
+          ptx::tmem_ld16(tmem + lane_base + kTmemO + c + 48,
+                         *reinterpret_cast<uint32_t(*)[16]>(&v[(ci + 1) & 1][16]));
+        }
         if (h >= a.heads) {
           // padding row: nothing to store
-        } else if (s.slot >= 0 || a.out_f32) {
-          float4* dst =
-              s.slot >= 0
-                  ? reinterpret_cast<float4*>(meta.part_out +
-                                              ((long long)s.slot * kHeadsTile + h) * kValueDim +
-                                              vdim0 + c)
-                  : reinterpret_cast<float4*>(a.out + s.u * a.out_stride_t + h * a.out_stride_h +
-                                              (long long)(vdim0 + c) * 4);
+        } else if (s.slot >= 0) {
+          float4* dst = reinterpret_cast<float4*>(meta.part_out) +
+                        ((long long)s.slot * (kValueDim / 4) + (vdim0 + c) / 4) * kHeadsTile + h;
 #pragma unroll
           for (int k = 0; k < 8; ++k)
-            dst[k] = make_float4(__uint_as_float(v[4 * k]) * inv_l,
-                                 __uint_as_float(v[4 * k + 1]) * inv_l,
-                                 __uint_as_float(v[4 * k + 2]) * inv_l,
-                                 __uint_as_float(v[4 * k + 3]) * inv_l);
+            dst[k * kHeadsTile] = make_float4(__uint_as_float(cur[4 * k]) * inv_l,
+                                              __uint_as_float(cur[4 * k + 1]) * inv_l,
+                                              __uint_as_float(cur[4 * k + 2]) * inv_l,
+                                              __uint_as_float(cur[4 * k + 3]) * inv_l);
+        } else if (a.out_f32) {
+          float4* dst = reinterpret_cast<float4*>(a.out + s.u * a.out_stride_t +
+                                                  h * a.out_stride_h + (long long)(vdim0 + c) * 4);
+#pragma unroll
+          for (int k = 0; k < 8; ++k)
+            dst[k] = make_float4(__uint_as_float(cur[4 * k]) * inv_l,
+                                 __uint_as_float(cur[4 * k + 1]) * inv_l,
+                                 __uint_as_float(cur[4 * k + 2]) * inv_l,
+                                 __uint_as_float(cur[4 * k + 3]) * inv_l);
         } else {
           uint32_t pkd[16];
 #pragma unroll
           for (int k = 0; k < 16; ++k)
-            pkd[k] = ptx::pack_bf16x2(__uint_as_float(v[2 * k]) * inv_l,
-                                      __uint_as_float(v[2 * k + 1]) * inv_l);
+            pkd[k] = ptx::pack_bf16x2(__uint_as_float(cur[2 * k]) * inv_l,
+                                      __uint_as_float(cur[2 * k + 1]) * inv_l);
           uint4* dst = reinterpret_cast<uint4*>(a.out + s.u * a.out_stride_t +
                                                 h * a.out_stride_h + (long long)(vdim0 + c) * 2);
 #pragma unroll
           for (int k = 0; k < 4; ++k)
             dst[k] = make_uint4(pkd[4 * k], pkd[4 * k + 1], pkd[4 * k + 2], pkd[4 * k + 3]);
         }
+        if (ci + 1 < kValueHalf / 32) ptx::tmem_wait_ld();
       }
       ptx::tc_fence_before();
       __syncwarp();
       if (lane == 0) ptx::mbar_arrive(bar(kBarOFree));
       it += s.np;
       ++useq;
+      if (!has_next) break;
+      s = s_next;
     }
   }
 
@@ -855,8 +893,10 @@ __global__ void __launch_bounds__(256) combine_kernel(Meta m, char* out, long lo
   const int esize = out_f32 ? 4 : 2;
   const long long items = (long long)ncomb * heads * 64;
   for (long long t = blockIdx.x * 256ll + threadIdx.x; t < items; t += (long long)gridDim.x * 256) {
+    // Consecutive threads take consecutive rows of one 8-column group: the partials'
+    // [slot][column quad][row] layout makes their loads contiguous.
     const int job = int(t / (heads * 64)), rem = int(t % (heads * 64));
-    const int h = rem >> 6, d0 = (rem & 63) * 8;
+    const int h = rem % heads, d0 = (rem / heads) * 8;
     const int u = m.combine_list[job];
     const int ns = m.unit_nsplit[u], off = m.unit_split_off[u];
     float mx = -INFINITY, wsum = 0.f;
@@ -869,10 +909,10 @@ __global__ void __launch_bounds__(256) combine_kernel(Meta m, char* out, long lo
         if (i0 + k < ns) {
           const long long slot = off + i0 + k;
           li[k] = __ldcg(m.part_lse + slot * kHeadsTile + h);
-          const float4* src =
-              reinterpret_cast<const float4*>(m.part_out + (slot * kHeadsTile + h) * kValueDim + d0);
+          const float4* src = reinterpret_cast<const float4*>(m.part_out) +
+                              (slot * (kValueDim / 4) + d0 / 4) * kHeadsTile + h;
           x[k][0] = __ldcg(src);
-          x[k][1] = __ldcg(src + 1);
+          x[k][1] = __ldcg(src + kHeadsTile);
         } else {
           li[k] = -INFINITY;
           x[k][0] = x[k][1] = make_float4(0.f, 0.f, 0.f, 0.f);

@@ -184,6 +184,11 @@ __device__ __forceinline__ void tma_load_4d_hint(uint32_t dst, const void* tmap,
       :: "r"(dst), "l"(tmap), "r"(bar), "r"(x), "r"(y), "r"(z), "r"(w), "l"(policy) : "memory");
 }
 
+// Brings the line holding `p` into L2 (no register result, nothing to wait for).
+__device__ __forceinline__ void prefetch_l2(const void* p) {
+  asm volatile("prefetch.global.L2 [%0];" :: "l"(p));
+}
+
 // Programmatic dependent launch: the dependent grid may start early; it waits here until the
 // grids it depends on have completed and their memory is visible.
 __device__ __forceinline__ void grid_dependency_wait() {
