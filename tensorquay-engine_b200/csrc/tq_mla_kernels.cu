@@ -329,7 +329,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       ptx::mbar_init(bar(kBarKvEmpty + s), 1);
     }
     ptx::mbar_init(bar(kBarQSmemFull), 1);
-    ptx::mbar_init(bar(kBarQTmemFull), kSoftmaxWarps);
     ptx::mbar_init(bar(kBarQEmpty), 1);
     for (int b = 0; b < 2; ++b) {
       ptx::mbar_init(bar(kBarSFull + b), 1);
@@ -354,16 +353,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     ptx::tma_prefetch_desc(&tm_q);
     ptx::tma_prefetch_desc(&tm_kv);
     ptx::tma_prefetch_desc(&tm_v);
-  }
-  // Query rows past the head count stay zero for the whole kernel (TMA writes rows < heads).
-  if (a.heads < kHeadsTile) {
-    const int words = (kHeadsTile - a.heads) * 128 / 16;
-    for (int i = threadIdx.x; i < kQSmemChunks * words; i += kThreads) {
-      const int chunk = i / words, w = i % words;
-      reinterpret_cast<uint4*>(sm + kSmQ + chunk * kQChunkBytes + a.heads * 128)[w] =
-          make_uint4(0, 0, 0, 0);
-    }
-    ptx::fence_proxy_async_smem();
   }
   if (warp == 1) {
     ptx::tmem_alloc(base + kSmMisc, kTmemCols);
@@ -408,9 +397,26 @@ __global__ void __launch_bounds__(kThreads, 1)
         int pf0 = s.np > 0 ? pt[s.p0] : 0;
         int pf1 = s.np > 1 ? pt[s.p0 + 1] : 0;
         int pf2 = s.np > 2 ? pt[s.p0 + 2] : 0;
+        // Query dims [0, 384) pass through two ring slots, three 64-dim chunks each, on their way
+        // to TMEM (tcgen05.cp by the MMA warp). The query boxes are 128 rows high: rows past the
+        // head count lie outside the tensor and arrive as zeros.
+        for (int qp = 0; qp < 2; ++qp, ++it) {
+          const uint32_t stage = it % kStages;
+          wt.where = (1 << 24) | int(it & 0xFFFFFF);
+          if (!wt.wait<false>(bar(kBarKvEmpty + stage), ((it / kStages) & 1u) ^ 1u)) {
+            ok = false;
+            break;
+          }
+          const uint32_t fb = bar(kBarKvFull + stage);
+          ptx::mbar_expect_tx(fb, 3 * kQChunkBytes);
+          for (int k = 0; k < 3; ++k)
+            ptx::tma_load_3d(base + kSmKv + stage * kStageBytes + k * kQChunkBytes, &tm_q, fb,
+                             64 * (3 * qp + k), 0, s.u);
+        }
+        if (!ok) break;
         wt.where = (1 << 24) | int(it & 0xFFFFFF);
         if (!wt.wait<false>(bar(kBarQEmpty), (useq & 1u) ^ 1u)) break;
-        ptx::mbar_expect_tx(bar(kBarQSmemFull), uint32_t(a.heads) * 128 * kQSmemChunks);
+        ptx::mbar_expect_tx(bar(kBarQSmemFull), kQChunkBytes * kQSmemChunks);
         for (int k = 0; k < kQSmemChunks; ++k)
           ptx::tma_load_3d(base + kSmQ + k * kQChunkBytes, &tm_q, bar(kBarQSmemFull),
                            kQTmemDims + 64 * k, 0, s.u);
@@ -475,9 +481,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     };
     // Waits for page itq (page `p` of its sequence, `n` visible keys) and zeroes its rows past
     // the cached length (NaN-poisoned slots) before any MMA reads them.
-    auto prepare = [&](uint32_t itq, int p, int n) -> bool {
-      const uint32_t stage = itq % kStages;
-      if (!wait_all(bar(kBarKvFull + stage), (itq / kStages) & 1u)) return false;
+    auto prepare = [&](uint32_t rq, int p, int n) -> bool {
+      const uint32_t stage = rq % kStages;
+      if (!wait_all(bar(kBarKvFull + stage), (rq / kStages) & 1u)) return false;
       const int valid = min(kPageRows, n - p * kPageRows);
       const int own_valid = max(0, min(kKeysPerCta, valid - key0));
       const int peer_valid = max(0, min(kKeysPerCta, valid - (kKeysPerCta - key0)));
@@ -503,8 +509,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     };
     // Descriptors advance by compile-time offsets (start field = address >> 4; shared addresses
     // stay below 256 KB, so the 14-bit field never carries).
-    auto issue_qk = [&](uint32_t itq) {
-      const uint32_t stage_base = base + kSmKv + (itq % kStages) * kStageBytes;
+    auto issue_qk = [&](uint32_t itq, uint32_t rq) {
+      const uint32_t stage_base = base + kSmKv + (rq % kStages) * kStageBytes;
       const uint32_t d = tmem + kTmemS + (itq & 1u) * 32;
       // K-major, 128B swizzle: 8-key groups kOwnGroupBytes apart, chunks 1 KB apart.
       const uint64_t kd = ptx::smem_desc(stage_base, 16, kOwnGroupBytes, 2);
@@ -521,8 +527,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                                         (kk & 3) * 32) >> 4),
                          idesc_qk, 1);
     };
-    auto issue_pv = [&](uint32_t itp, bool first) {
-      const uint32_t stage = itp % kStages, pb = itp & 1u;
+    auto issue_pv = [&](uint32_t itp, uint32_t rp, bool first) {
+      const uint32_t stage = rp % kStages, pb = itp & 1u;
       const uint32_t stage_base = base + kSmKv + stage * kStageBytes;
       // V as B, MN-major: 64-dim chunks 1 KB apart (LBO), 8-key groups one group apart (SBO).
       const uint64_t vd =
@@ -544,15 +550,33 @@ __global__ void __launch_bounds__(kThreads, 1)
       ptx::mma_commit_warp(bar(kBarKvEmpty + stage));
       ptx::mma_commit_warp(bar(kBarPvDone + pb));
     };
+    uint32_t ring = 0;  // ring slots consumed: two query slots per segment, then its pages
     while (ok && walker.next(meta, s)) {
       const int n = meta.unit_n[s.u];
       const uint32_t it0 = it;
       wt.where = (2 << 24) | int(it0 & 0xFFFFFF);
-      if (!wait_all(bar(kBarQTmemFull), useq & 1u)) break;
+      // Query dims [0, 384) into TMEM from the two query slots, once the previous segment's QK
+      // MMAs (the readers of the old query) have completed. The copies and the MMAs after them
+      // run in issue order; each slot is released when its copies are done.
+      if (useq > 0 && !wait_all(bar(kBarQEmpty), (useq - 1) & 1u)) break;
+      for (int qp = 0; qp < 2 && ok; ++qp) {
+        const uint32_t rq = ring + qp, stage = rq % kStages;
+        if (!wait_all(bar(kBarKvFull + stage), (rq / kStages) & 1u)) { ok = false; break; }
+        ptx::tc_fence_after();
+        const uint32_t src = base + kSmKv + stage * kStageBytes;
+#pragma unroll
+        for (int c = 0; c < 12; ++c)
+          ptx::cp_smem_to_tmem_warp(
+              tmem + kTmemQ + (qp * 12 + c) * 8,
+              ptx::smem_desc(src + (c >> 2) * kQChunkBytes + (c & 3) * 32, 16, 1024, 2));
+        ptx::mma_commit_warp(bar(kBarKvEmpty + stage));
+      }
+      if (!ok) break;
+      const uint32_t r0 = ring + 2;  // ring slot of the segment's first page
       if (!wait_all(bar(kBarQSmemFull), useq & 1u)) break;
-      if (!prepare(it0, s.p0, n)) break;
+      if (!prepare(r0, s.p0, n)) break;
       ptx::tc_fence_after();
-      issue_qk(it0);
+      issue_qk(it0, r0);
       ptx::mma_commit_warp(bar(kBarSFull + (it0 & 1u)));
       if (s.np == 1) ptx::mma_commit_warp(bar(kBarQEmpty));
       for (int j = 0; j < s.np; ++j) {
@@ -564,14 +588,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (j == 1 && !wait_all(bar(kBarOFree), (useq & 1u) ^ 1u)) { ok = false; break; }
           if (!wait_all(bar(kBarPFull + (itp & 1u)), (itp >> 1) & 1u)) { ok = false; break; }
           ptx::tc_fence_after();
-          issue_pv(itp, j == 1);
+          issue_pv(itp, r0 + j - 1, j == 1);
         }
         // Waiting here, after PV(j-1) was issued, keeps QK(j+1) out of the pipe until page j+1's
         // data is in, which in practice lets PV(j-1) drain first and release its KV stage early.
-        if (has_next && !prepare(itq + 1, s.p0 + j + 1, n)) { ok = false; break; }
+        if (has_next && !prepare(r0 + j + 1, s.p0 + j + 1, n)) { ok = false; break; }
         ptx::tc_fence_after();
         if (has_next) {
-          issue_qk(itq + 1);
+          issue_qk(itq + 1, r0 + j + 1);
           ptx::mma_commit_warp(bar(kBarSFull + ((itq + 1) & 1u)));
           if (j + 2 == s.np) ptx::mma_commit_warp(bar(kBarQEmpty));
         }
@@ -584,10 +608,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (s.np == 1 && !wait_all(bar(kBarOFree), (useq & 1u) ^ 1u)) { ok = false; break; }
       if (!wait_all(bar(kBarPFull + (itp & 1u)), (itp >> 1) & 1u)) { ok = false; break; }
       ptx::tc_fence_after();
-      issue_pv(itp, s.np == 1);
+      issue_pv(itp, r0 + s.np - 1, s.np == 1);
       ptx::mma_commit_warp(bar(kBarOFull));
       __syncwarp();
       it = it0 + s.np;
+      ring = r0 + s.np;
       ++useq;
     }
     if (lane == 0) ptx::mma_commit(bar(kBarDrain));
@@ -612,47 +637,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t lsum_full_r = ptx::map_peer(bar(kBarLsumFull), peer);
     const float c2 = a.scale_log2;
     uint32_t it = 0, useq = 0;
-    // Segment `idx`'s query dims [0, 384) into TMEM once the previous segment's QK MMAs are done.
-    auto load_q = [&](const Seg& sq, uint32_t idx) -> bool {
-      wt.where = (6 << 24) | int(idx & 0xFFFFFF);
-      if (!wt.wait<false>(bar(kBarQEmpty), (idx & 1u) ^ 1u)) return false;
-      __syncwarp();
-      ptx::tc_fence_after();
-      const uint4* src = reinterpret_cast<const uint4*>(a.q + sq.u * a.q_stride_t +
-                                                        h * a.q_stride_h);
-      // 256 bytes of the row per batch: the loads of a batch are in flight together (the TMEM
-      // stores between batches are ordered with them).
-      for (int c = 0; c < kQTmemDims / 2; c += 64) {
-        uint4 x[16];
-#pragma unroll
-        for (int k = 0; k < 16; ++k) x[k] = h < a.heads ? src[c / 4 + k] : make_uint4(0, 0, 0, 0);
-#pragma unroll
-        for (int g = 0; g < 4; ++g) {
-          uint32_t v[16];
-#pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            v[4 * k] = x[4 * g + k].x; v[4 * k + 1] = x[4 * g + k].y;
-            v[4 * k + 2] = x[4 * g + k].z; v[4 * k + 3] = x[4 * g + k].w;
-          }
-          ptx::tmem_st16(tmem + lane_base + kTmemQ + c + 16 * g, v);
-        }
-      }
-      ptx::tmem_wait_st();
-      ptx::tc_fence_before();
-      __syncwarp();
-      if (lane == 0) ptx::mbar_arrive(bar(kBarQTmemFull));
-      return true;
-    };
-    Seg s, s_next;
-    bool ok = walker.next(meta, s) && load_q(s, 0);
-    while (ok) {
+    Seg s;
+    bool ok = true;
+    while (ok && walker.next(meta, s)) {
       const int n = meta.unit_n[s.u];
-      // The next segment is usually the next token: its query row is pulled into L2 now, so the
-      // TMEM load before this segment's epilogue finds it there.
-      if (s.u + 1 < a.tokens && h < a.heads) {
-        const char* next_row = a.q + (s.u + 1) * a.q_stride_t + h * a.q_stride_h;
-        for (int k = 0; k <= kQTmemDims * 2; k += 128) ptx::prefetch_l2(next_row + k);
-      }
       float m_used = -INFINITY, l = 0.f;
       for (int j = 0; j < s.np; ++j) {
         const uint32_t itq = it + j, sb = itq & 1u, ph = (itq >> 1) & 1u;
@@ -771,10 +759,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) ptx::mbar_arrive(bar(kBarPFull + sb));
       }
       if (!ok) break;
-      // The next segment's query goes into TMEM before this epilogue, so its first QK MMAs
-      // overlap the epilogue.
-      const bool has_next = walker.next(meta, s_next);
-      if (has_next && !load_q(s_next, useq + 1)) break;
       // Epilogue: the row sum over both CTAs' keys, then this CTA's 256 columns of O.
       wt.where = (5 << 24) | int(useq & 0xFFFFFF);
       ptx::st_async_b32(lsum_remote, __float_as_uint(l), lsum_full_r + 8u * sw);
@@ -850,8 +834,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (lane == 0) ptx::mbar_arrive(bar(kBarOFree));
       it += s.np;
       ++useq;
-      if (!has_next) break;
-      s = s_next;
     }
   }
 
@@ -1239,7 +1221,7 @@ int32_t launch(const TqMlaParams* params, void* workspace, uint64_t workspace_by
     const uint64_t width = params->qk_width;
     const cuuint64_t qdims[3] = {width, params->heads, params->tokens};
     const cuuint64_t qstr[2] = {s.q.strides_bytes[1], s.q.strides_bytes[0]};
-    const cuuint32_t qbox[3] = {64, cuuint32_t(H), 1};
+    const cuuint32_t qbox[3] = {64, cuuint32_t(kHeadsTile), 1};
     // Pool rows seen as {64 dims, row in an 8-row group, 64-dim chunk, 8-row group}: strides
     // row_stride, 128 B and 8 rows. A box reads whole 8-row groups (contiguous bytes) at a time
     // and lands as [group][chunk][8 rows x 128 B], a 128B-swizzled UMMA operand layout.

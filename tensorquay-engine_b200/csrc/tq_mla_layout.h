@@ -69,7 +69,6 @@ enum Bar : int {
   kBarKvFull = 0,                       // [kStages] TMA transaction barriers
   kBarKvEmpty = kBarKvFull + kStages,   // [kStages] PV done with the stage
   kBarQSmemFull = kBarKvEmpty + kStages,  // TMA of the shared-memory query dims
-  kBarQTmemFull,                        // TMEM query dims written (one arrival per softmax warp)
   kBarQEmpty,                           // all QK MMAs of the segment done
   kBarSFull,                            // [2]
   kBarPFull = kBarSFull + 2,            // [2] both halves of P ready (one arrival per warp)
@@ -79,8 +78,8 @@ enum Bar : int {
   kBarMsgFull,                          // [2][4] peer warp's P rows + maxima landed (tx bytes)
   kBarMsgFree = kBarMsgFull + 8,        // [2][4] peer warp may overwrite (one remote arrival)
   kBarLsumFull = kBarMsgFree + 8,       // [4] peer warp's row sums landed (tx bytes)
-  kBarSpare = kBarLsumFull + 4,         // [8] unused
-  kBarDrain = kBarSpare + 8,
+  kBarSpare = kBarLsumFull + 4,         // [9] unused
+  kBarDrain = kBarSpare + 9,
   kBarCount
 };
 static_assert(kBarCount == kNumBars, "barrier count");

@@ -266,6 +266,16 @@ __device__ __forceinline__ void mma_ts_warp(uint32_t d_tmem, uint32_t a_tmem, ui
       :: "r"(d_tmem), "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate) : "memory");
 }
 
+// Shared memory -> TMEM copy of a 128-row x 256-bit tile (one K=16 step of a bf16 operand), by
+// one lane elected inside the instruction sequence.
+__device__ __forceinline__ void cp_smem_to_tmem_warp(uint32_t taddr, uint64_t src_desc) {
+  asm volatile(
+      "{\n\t.reg .pred e;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "@e tcgen05.cp.cta_group::1.128x256b [%0], %1;\n\t}"
+      :: "r"(taddr), "l"(src_desc) : "memory");
+}
+
 __device__ __forceinline__ void mma_commit_warp(uint32_t bar) {
   asm volatile(
       "{\n\t.reg .pred e;\n\t"
