@@ -337,9 +337,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     ptx::mbar_init(bar(kBarOFull), 1);
     ptx::mbar_init(bar(kBarOFree), kSoftmaxWarps);
+    for (int i = 0; i < 2; ++i) ptx::mbar_init(bar(kBarMsgFree + i), 1);
     for (int i = 0; i < 8; ++i) {
       ptx::mbar_init(bar(kBarMsgFull + i), 1);
-      ptx::mbar_init(bar(kBarMsgFree + i), 1);
       // Each receive buffer expects one peer warp's message; armed for pages 0 and 1.
       ptx::mbar_expect_tx(bar(kBarMsgFull + i), kWarpMsgBytes);
     }
@@ -549,6 +549,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                          xd + uint64_t((kk * 2 * kPeerGroupBytes) >> 4), idesc_pv, 1u);
       ptx::mma_commit_warp(bar(kBarKvEmpty + stage));
       ptx::mma_commit_warp(bar(kBarPvDone + pb));
+      // The peer's message buffer pb in this CTA is consumed: the peer may write its next one.
+      ptx::mma_commit_multicast_warp(bar(kBarMsgFree + pb), uint16_t(1u << peer));
     };
     uint32_t ring = 0;  // ring slots consumed: two query slots per segment, then its pages
     while (ok && walker.next(meta, s)) {
@@ -633,7 +635,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t peer_base = ptx::map_peer(base + kSmPeer, peer);
     const uint32_t lsum_remote = ptx::map_peer(base + kSmLsum, peer) + 4u * h;
     const uint32_t msg_full_r = ptx::map_peer(bar(kBarMsgFull), peer);
-    const uint32_t msg_free_r = ptx::map_peer(bar(kBarMsgFree), peer);
     const uint32_t lsum_full_r = ptx::map_peer(bar(kBarLsumFull), peer);
     const float c2 = a.scale_log2;
     uint32_t it = 0, useq = 0;
@@ -677,15 +678,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           l_page = s0 + s1;
         }
-        // Release the peer's buffer of page itq-2 (PV(itq-2) has consumed it), then send this
-        // page's probabilities and candidate once the peer has released ours.
-        if (itq >= 2) {
-          const uint32_t prev = itq - 2;
-          if (!wt.wait<false>(bar(kBarPvDone + sb), (prev >> 1) & 1u)) { ok = false; break; }
-          __syncwarp();
-          if (lane == 0) ptx::mbar_arrive_cluster_relaxed(msg_free_r + 8u * (sb * 4 + sw));
-        }
-        if (!wt.wait<true>(bar(kBarMsgFree + sb * 4 + sw), ph ^ 1u)) { ok = false; break; }
+        // Send this page's probabilities and candidate once the peer's PV of page itq-2 has
+        // consumed our previous message in that buffer (its MMA warp's commit arrives here).
+        if (!wt.wait<true>(bar(kBarMsgFree + sb), ph ^ 1u)) { ok = false; break; }
         {
           const uint32_t dst = peer_base + sb * kPMsgBytes + 16u * h;
           const uint32_t rbar = msg_full_r + 8u * (sb * 4 + sw);
@@ -834,6 +829,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (lane == 0) ptx::mbar_arrive(bar(kBarOFree));
       it += s.np;
       ++useq;
+    }
+    // The peer's last releases of our message buffers arrive asynchronously (when its last PVs
+    // complete); both have landed before this CTA may exit.
+    for (uint32_t b = 0; b < 2 && b < it; ++b) {
+      const uint32_t uses = (it + 1 - b) / 2;
+      wt.wait<true>(bar(kBarMsgFree + b), (uses - 1) & 1u);
     }
   }
 

@@ -76,10 +76,11 @@ enum Bar : int {
   kBarOFull = kBarPvDone + 2,
   kBarOFree,                            // one arrival per softmax warp
   kBarMsgFull,                          // [2][4] peer warp's P rows + maxima landed (tx bytes)
-  kBarMsgFree = kBarMsgFull + 8,        // [2][4] peer warp may overwrite (one remote arrival)
-  kBarLsumFull = kBarMsgFree + 8,       // [4] peer warp's row sums landed (tx bytes)
-  kBarSpare = kBarLsumFull + 4,         // [9] unused
-  kBarDrain = kBarSpare + 9,
+  kBarMsgFree = kBarMsgFull + 8,        // [2] the peer's PV of the buffer's last page is done
+                                        //     (one arrival, the peer MMA warp's commit)
+  kBarLsumFull = kBarMsgFree + 2,       // [4] peer warp's row sums landed (tx bytes)
+  kBarSpare = kBarLsumFull + 4,         // [15] unused
+  kBarDrain = kBarSpare + 15,
   kBarCount
 };
 static_assert(kBarCount == kNumBars, "barrier count");

@@ -284,6 +284,16 @@ __device__ __forceinline__ void mma_commit_warp(uint32_t bar) {
       :: "r"(bar) : "memory");
 }
 
+// As mma_commit_warp, on the mbarrier at the same shared offset in each CTA of `cta_mask`.
+__device__ __forceinline__ void mma_commit_multicast_warp(uint32_t bar, uint16_t cta_mask) {
+  asm volatile(
+      "{\n\t.reg .pred e;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
+      " [%0], %1;\n\t}"
+      :: "r"(bar), "h"(cta_mask) : "memory");
+}
+
 // Arrive once on a local mbarrier when all prior tcgen05 ops of this thread have completed.
 __device__ __forceinline__ void mma_commit(uint32_t bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
