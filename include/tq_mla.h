@@ -112,10 +112,10 @@ typedef struct {
 /* Byte offsets of the scheduler metadata inside a workspace (for inspection and tests). */
 typedef struct {
   uint64_t total_bytes;
-  uint64_t header;        /* int32[16]: error, total pages, quota, n_combine, n_empty, pairs */
+  uint64_t header;        /* int32[16]: error, virtual pages, quota, n_combine, n_empty, pairs*/
   uint64_t unit_n;        /* int32[T]  visible keys per token                               */
   uint64_t unit_pages;    /* int32[T]                                                       */
-  uint64_t unit_gstart;   /* int32[T]  first global page                                    */
+  uint64_t unit_gstart;   /* int32[T]  virtual position of the first page                   */
   uint64_t unit_first;    /* int32[T]  first CTA pair touching the token (-1 if none)       */
   uint64_t unit_nsplit;   /* int32[T]                                                       */
   uint64_t unit_split_off;/* int32[T]                                                       */

@@ -125,7 +125,10 @@ __global__ void __launch_bounds__(1024) schedule_kernel(Meta m, const int* __res
   const int per = (T + 1023) / 1024;
   const int lo = min(T, int(threadIdx.x) * per), hi = min(T, lo + per);
 
-  long long my_pages = 0;
+  // Units are laid end to end in a virtual page space: a unit with pages occupies
+  // kSegmentCostPages (its start-up cost) followed by its pages; pair c takes the virtual range
+  // [c * quota, (c + 1) * quota).
+  long long my_vlen = 0;
   for (int u = lo; u < hi; ++u) {
     const int s = seq_id[u];
     long long n = 0;
@@ -144,10 +147,10 @@ __global__ void __launch_bounds__(1024) schedule_kernel(Meta m, const int* __res
     const int pages = int((n + kPageRows - 1) / kPageRows);
     m.unit_n[u] = int(n);
     m.unit_pages[u] = pages;
-    my_pages += pages;
+    my_vlen += pages > 0 ? pages + kSegmentCostPages : 0;
   }
   long long total = 0;
-  long long g = block_exclusive_scan(my_pages, &total, sh);
+  long long g = block_exclusive_scan(my_vlen, &total, sh);
   if (total >= (1ll << 31)) {
     if (threadIdx.x == 0) atomicOr(&s_err, TQ_DEV_WORK_OVERFLOW);
     total = 0;
@@ -156,18 +159,20 @@ __global__ void __launch_bounds__(1024) schedule_kernel(Meta m, const int* __res
   long long my_split = 0;
   for (int u = lo; u < hi; ++u) {
     const int pages = total ? m.unit_pages[u] : 0;
-    m.unit_gstart[u] = int(g);
+    const long long a = g + (pages > 0 ? kSegmentCostPages : 0);  // virtual start of the pages
+    m.unit_gstart[u] = int(a);
     int first = -1, ns = 0;
     if (pages > 0) {
-      first = int(g / quota);
-      ns = int((g + pages - 1) / quota) - first + 1;
-      const long long c_lo = (g + quota - 1) / quota, c_hi = (g + pages - 1) / quota;
+      first = int(a / quota);
+      ns = int((a + pages - 1) / quota) - first + 1;
+      // Pairs whose range starts inside this unit's virtual span begin with it.
+      const long long c_lo = (g + quota - 1) / quota, c_hi = (a + pages - 1) / quota;
       for (long long c = c_lo; c <= c_hi; ++c) m.pair_begin[c] = u;
     }
     m.unit_first[u] = first;
     m.unit_nsplit[u] = ns;
     my_split += ns >= 2 ? ns : 0;
-    g += pages;
+    g = a + pages;
   }
   long long tmp;
   long long off = block_exclusive_scan(my_split, &tmp, sh);
@@ -209,37 +214,41 @@ struct Seg {
 };
 
 struct SegWalker {
-  long long g, g_end;
-  int u, p, T, c;
+  long long g, g_end;  // virtual page positions
+  int u, T, c;
   __device__ void init(const Meta& m, int pair, int tokens) {
     const long long total = m.header[kHdrTotalPages], quota = m.header[kHdrQuota];
     c = pair;
     T = tokens;
     g = g_end = 0;
-    u = p = 0;
+    u = 0;
     if (quota == 0 || (long long)pair * quota >= total) return;
     u = m.pair_begin[pair];
-    if (u < 0 || u >= tokens) return;  // inconsistent metadata: process nothing
+    if (u < 0 || u >= tokens) return;  // no unit starts in this range, or bad metadata
     g = (long long)pair * quota;
     g_end = min(g + quota, total);
-    p = int(g - m.unit_gstart[u]);
   }
   __device__ bool next(const Meta& m, Seg& s) {
-    if (g >= g_end || u >= T) return false;
-    const int pages = m.unit_pages[u];
-    if (p < 0 || p >= pages) return false;
-    const int n = int(min((long long)(pages - p), g_end - g));
-    s.u = u;
-    s.p0 = p;
-    s.np = n;
-    const int ns = m.unit_nsplit[u];
-    s.slot = ns >= 2 ? m.unit_split_off[u] + c - m.unit_first[u] : -1;
-    g += n;
-    p = 0;
-    if (g < g_end) {
-      do { ++u; } while (u < T && m.unit_pages[u] == 0);
+    while (g < g_end && u < T) {
+      const int pages = m.unit_pages[u];
+      const long long a = m.unit_gstart[u], b = a + pages;
+      if (pages <= 0 || g >= b) {
+        ++u;
+        continue;
+      }
+      if (g < a) g = a;  // skip the unit's start-up cost
+      if (g >= g_end) return false;
+      const int n = int(min(b, g_end) - g);
+      s.u = u;
+      s.p0 = int(g - a);
+      s.np = n;
+      const int ns = m.unit_nsplit[u];
+      s.slot = ns >= 2 ? m.unit_split_off[u] + c - m.unit_first[u] : -1;
+      g += n;
+      ++u;
+      return true;
     }
-    return true;
+    return false;
   }
 };
 

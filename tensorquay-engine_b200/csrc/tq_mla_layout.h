@@ -24,6 +24,9 @@ constexpr int kHeadsTile = 128;  // UMMA M
 constexpr int kValueDim = 512;
 constexpr int kValueHalf = 256;  // per CTA
 constexpr int kStages = 3;
+// Scheduling cost of starting a segment (a token's page range on one CTA pair: query load,
+// pipeline refill, epilogue), in pages. The partition balances pages + this per segment.
+constexpr int kSegmentCostPages = 8;
 constexpr int kSoftmaxWarps = 4;
 constexpr int kSoftmaxThreads = 32 * kSoftmaxWarps;
 constexpr int kThreads = 64 + kSoftmaxThreads;  // warp 0 TMA, warp 1 MMA, warps 2-5 softmax
