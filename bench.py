@@ -307,27 +307,36 @@ def run_ours(args, world, rank, local_rank):
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     clock = ClockSampler(local_rank, str(ROOT / "gpurun_out" / f"clocks_rank{rank}.csv")) \
         if (ROOT / "gpurun_out").exists() else ClockSampler(local_rank, f"/tmp/clocks{rank}.csv")
-    # Events around the attention kernel of every timed step (recorded once so that they exist).
-    kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-           for _ in range(args.steps)]
-    for b, e in kev:
-        b.record(stream)
-        e.record(stream)
     barrier()
     torch.cuda.synchronize(dev)
     with clock:
         ev0.record(stream)
-        for b, e in kev:
-            ops.set_kernel_timer(b, e)
+        for _ in range(args.steps):
             launch(stream)
         ev1.record(stream)
         torch.cuda.synchronize(dev)
-    ops.set_kernel_timer()
     barrier()
     ms = ev0.elapsed_time(ev1)
     ms_max = max_over_ranks(ms)
     ms_step = ms_max / args.steps
-    kernel_ms = sum(b.elapsed_time(e) for b, e in kev) / args.steps
+
+    # ---- the attention kernel alone: a second pass with events recorded around it in every
+    # step (recorded once beforehand so that they exist). An event between two launches breaks
+    # their programmatic overlap, so this pass is not the one that gives the step time above, and
+    # each kernel interval also holds the kernel's own launch latency (conservative).
+    k_steps = min(args.steps, 300)
+    kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(k_steps)]
+    for b, e in kev:
+        b.record(stream)
+        e.record(stream)
+    torch.cuda.synchronize(dev)
+    for b, e in kev:
+        ops.set_kernel_timer(b, e)
+        launch(stream)
+    torch.cuda.synchronize(dev)
+    ops.set_kernel_timer()
+    kernel_ms = sum(b.elapsed_time(e) for b, e in kev) / k_steps
 
     # ---- end-to-end through the C ABI with host buffers, pipelined as a serving loop would be:
     # two sets of device buffers, each with its own validated launch; per step k (set k % 2) the
