@@ -849,7 +849,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   ptx::tc_fence_before();
   __syncthreads();
-  ptx::cluster_sync();
+  // Every message, row sum and buffer release between the pair has been awaited by its receiver,
+  // so the exit barrier need not wait for this CTA's output stores to drain. After a timeout a
+  // remote abort flag may still be in flight: then the full barrier orders it first.
+  if (*abort_flag) ptx::cluster_sync();
+  else ptx::cluster_sync_relaxed();
   if (warp == 1) {
     ptx::tc_fence_after();
     ptx::tmem_dealloc(tmem, kTmemCols);

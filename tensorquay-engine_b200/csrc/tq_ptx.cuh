@@ -35,6 +35,15 @@ __device__ __forceinline__ void cluster_sync() {
                ::: "memory");
 }
 
+// Cluster-wide execution barrier whose arrive has no release semantics, so it does not wait for
+// this thread's earlier stores (an epilogue's global stores take microseconds to drain). Only for
+// points where every shared-memory transfer between the CTAs has already been awaited by its
+// receiver.
+__device__ __forceinline__ void cluster_sync_relaxed() {
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;\n\tbarrier.cluster.wait.aligned;"
+               ::: "memory");
+}
+
 // Address of the same shared-memory offset in CTA `rank` of this cluster.
 __device__ __forceinline__ uint32_t map_peer(uint32_t local, uint32_t rank) {
   uint32_t r;
