@@ -80,6 +80,8 @@ struct MainArgs {
   int out_f32;
   float* lse;
   float scale_log2;
+  const uint8_t* kv;        // pool base (FP8 rows are read by the kernel's convert warps)
+  long long kv_row_stride;  // bytes
 };
 
 // ---------------------------------------------------------------------------------------------
@@ -309,11 +311,16 @@ struct Waiter {
 // ---------------------------------------------------------------------------------------------
 // Main kernel.
 
-template <bool kRope>
-__global__ void __launch_bounds__(kThreads, 1)
+// kFp8: FP8 E4M3 rows (512 codes, then 4 f32 scales, one per 128 values; no RoPE part). Four
+// more warps (6-9) read each page's rows with plain loads, dequantize them to bf16 and write the
+// same shared-memory operand layout the TMA gives bf16 rows, zeros past the cached length; the
+// MMA and softmax warps are unchanged.
+template <bool kRope, bool kFp8 = false>
+__global__ void __launch_bounds__(kFp8 ? kThreadsFp8 : kThreads, 1)
     mla_paged_kernel(const __grid_constant__ CUtensorMap tm_q,
                      const __grid_constant__ CUtensorMap tm_kv,
                      const __grid_constant__ CUtensorMap tm_v, const MainArgs a) {
+  static_assert(!(kRope && kFp8), "FP8 rows carry no RoPE part");
   constexpr int kQkChunks = kRope ? 9 : 8;               // 64-dim chunks of the query width
   constexpr int kQSmemChunks = kQkChunks - kQTmemDims / 64;
   constexpr uint32_t kStageLoadBytes = (kQkChunks + 4) * kKvChunkBytes;
@@ -334,8 +341,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
-      ptx::mbar_init(bar(kBarKvFull + s), 1);
+      // FP8: a page's stage is complete when the four convert warps have arrived; a query
+      // slot's TMA arrives once with its bytes plus three plain arrivals.
+      ptx::mbar_init(bar(kBarKvFull + s), kFp8 ? kConvertWarps : 1);
       ptx::mbar_init(bar(kBarKvEmpty + s), 1);
+      ptx::mbar_init(bar(kBarKvGrant + s), 1);
     }
     ptx::mbar_init(bar(kBarQSmemFull), 1);
     ptx::mbar_init(bar(kBarQEmpty), 1);
@@ -418,6 +428,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           const uint32_t fb = bar(kBarKvFull + stage);
           ptx::mbar_expect_tx(fb, 3 * kQChunkBytes);
+          if constexpr (kFp8) {
+            for (int k = 1; k < kConvertWarps; ++k) ptx::mbar_arrive(fb);
+          }
           for (int k = 0; k < 3; ++k)
             ptx::tma_load_3d(base + kSmKv + stage * kStageBytes + k * kQChunkBytes, &tm_q, fb,
                              64 * (3 * qp + k), 0, s.u);
@@ -430,16 +443,26 @@ __global__ void __launch_bounds__(kThreads, 1)
           ptx::tma_load_3d(base + kSmQ + k * kQChunkBytes, &tm_q, bar(kBarQSmemFull),
                            kQTmemDims + 64 * k, 0, s.u);
         ++useq;
+        // FP8: the convert warps fill the pages' stages; this loop waits for each page's slot
+        // to be free and grants it to them. This thread is the only waiter on kBarKvEmpty and
+        // waits on every slot in ring order: a parity wait tells completions apart only modulo
+        // 2, so a waiter that skipped slots could pass two phases early or block one phase late.
+        // A stage's grants are at most one ahead of the convert warps (the next grant on it
+        // needs the previous page's release), so their waits on kBarKvGrant are exact.
         for (int j = 0; j < s.np; ++j, ++it) {
           const uint32_t stage = it % kStages;
           const int page = pf0;
           pf0 = pf1;
           pf1 = pf2;
-          pf2 = j + 3 < s.np ? pt[s.p0 + j + 3] : 0;
+          pf2 = (!kFp8 && j + 3 < s.np) ? pt[s.p0 + j + 3] : 0;
           wt.where = (1 << 24) | int(it & 0xFFFFFF);
           if (!wt.wait<false>(bar(kBarKvEmpty + stage), ((it / kStages) & 1u) ^ 1u)) {
             ok = false;
             break;
+          }
+          if constexpr (kFp8) {
+            ptx::mbar_arrive(bar(kBarKvGrant + stage));
+            continue;
           }
           long long row = (long long)page * kPageRows;
           if (page < 0 || row >= a.pool_rows) {
@@ -496,7 +519,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int valid = min(kPageRows, n - p * kPageRows);
       const int own_valid = max(0, min(kKeysPerCta, valid - key0));
       const int peer_valid = max(0, min(kKeysPerCta, valid - (kKeysPerCta - key0)));
-      if (own_valid < kKeysPerCta || peer_valid < kKeysPerCta) {
+      // FP8: the convert warps already wrote zeros past the cached length.
+      if (!kFp8 && (own_valid < kKeysPerCta || peer_valid < kKeysPerCta)) {
         uint8_t* st_ptr = sm + kSmKv + stage * kStageBytes;
         const int own_words = (kKeysPerCta - own_valid) * 8;
         const int peer_words = (kKeysPerCta - peer_valid) * 8;
@@ -629,6 +653,94 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) ptx::mma_commit(bar(kBarDrain));
     __syncwarp();
     wt.drain(bar(kBarDrain), 0);
+  } else if (warp >= 6) {
+    // ------------------------------------------------------------------ FP8 convert warps
+    // Warp cw handles this CTA's keys key0 + 8 cw + [0, 8) across all 512 dims (lane: dims
+    // [16 lane, 16 lane + 16), one 16-byte load of codes) and the peer's keys
+    // (32 - key0) + 8 cw + [0, 8) across this CTA's 256 value dims (two keys per load, 16 lanes
+    // each). All loads of a page are in flight together; each 16-byte group of codes becomes two
+    // bf16 16-byte units written at their 128B-swizzled places (unit u of row r at u ^ (r % 8)).
+    // Keys past the cached length (and pages outside the pool) are written as zeros and their
+    // rows are never read.
+    if constexpr (kFp8) {
+      const int cw = warp - 6, hl = lane & 15;
+      uint32_t it = 0;
+      uint32_t grant_parity = 0;  // bit s: parity of the next grant phase of stage s
+      Seg s;
+      bool ok = true;
+      while (ok && walker.next(meta, s)) {
+        const int n = meta.unit_n[s.u];
+        const int* pt = a.page_table + (long long)a.seq_id[s.u] * a.slots;
+        it += 2;  // the segment's two query slots, filled by the TMA producer
+        for (int j = 0; j < s.np; ++j, ++it) {
+          const uint32_t stage = it % kStages;
+          const int page = pt[s.p0 + j];
+          const int valid = min(kPageRows, n - (s.p0 + j) * kPageRows);
+          const long long row0 = (long long)page * kPageRows;
+          const bool page_ok = page >= 0 && row0 < a.pool_rows;
+          if (!page_ok && cw == 0 && lane == 0) atomicOr(a.meta.header + kHdrError, TQ_DEV_PAGE_RANGE);
+          uint4 own[8], pr[4];
+          float own_sc[8], pr_sc[4];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const int key = key0 + 8 * cw + i;
+            own[i] = make_uint4(0, 0, 0, 0);
+            own_sc[i] = 0.f;
+            if (page_ok && key < valid) {
+              const uint8_t* rp = a.kv + (row0 + key) * a.kv_row_stride;
+              own[i] = __ldg(reinterpret_cast<const uint4*>(rp) + lane);
+              own_sc[i] = __ldg(reinterpret_cast<const float*>(rp + kFp8RowCodes) + (lane >> 3));
+            }
+          }
+#pragma unroll
+          for (int p = 0; p < 4; ++p) {
+            const int key = (kKeysPerCta - key0) + 8 * cw + 2 * p + (lane >> 4);
+            pr[p] = make_uint4(0, 0, 0, 0);
+            pr_sc[p] = 0.f;
+            if (page_ok && key < valid) {
+              const uint8_t* rp = a.kv + (row0 + key) * a.kv_row_stride;
+              pr[p] = __ldg(reinterpret_cast<const uint4*>(rp + vdim0) + hl);
+              pr_sc[p] = __ldg(reinterpret_cast<const float*>(rp + kFp8RowCodes) +
+                               ((vdim0 + 16 * hl) >> 7));
+            }
+          }
+          wt.where = (7 << 24) | int(it & 0xFFFFFF);
+          const bool got = wt.wait<false>(bar(kBarKvGrant + stage), (grant_parity >> stage) & 1u);
+          if (!__all_sync(0xFFFFFFFFu, got)) { ok = false; break; }
+          grant_parity ^= 1u << stage;
+          uint8_t* st_ptr = sm + kSmKv + stage * kStageBytes;
+          auto put16 = [&](uint8_t* rowp, int u0, int r8, const uint4& c, float sc) {
+            uint4 lo, hi;
+            lo.x = ptx::e4m3x2_scaled_bf16x2(c.x, sc);
+            lo.y = ptx::e4m3x2_scaled_bf16x2(c.x >> 16, sc);
+            lo.z = ptx::e4m3x2_scaled_bf16x2(c.y, sc);
+            lo.w = ptx::e4m3x2_scaled_bf16x2(c.y >> 16, sc);
+            hi.x = ptx::e4m3x2_scaled_bf16x2(c.z, sc);
+            hi.y = ptx::e4m3x2_scaled_bf16x2(c.z >> 16, sc);
+            hi.z = ptx::e4m3x2_scaled_bf16x2(c.w, sc);
+            hi.w = ptx::e4m3x2_scaled_bf16x2(c.w >> 16, sc);
+            *reinterpret_cast<uint4*>(rowp + ((u0 ^ r8) << 4)) = lo;
+            *reinterpret_cast<uint4*>(rowp + (((u0 + 1) ^ r8) << 4)) = hi;
+          };
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const int r = 8 * cw + i;
+            put16(st_ptr + (r >> 3) * kOwnGroupBytes + (lane >> 2) * kAtomBytes + (r & 7) * 128,
+                  2 * (lane & 3), r & 7, own[i], own_sc[i]);
+          }
+#pragma unroll
+          for (int p = 0; p < 4; ++p) {
+            const int r = 8 * cw + 2 * p + (lane >> 4);
+            put16(st_ptr + kPvxOffset + (r >> 3) * kPeerGroupBytes + (hl >> 2) * kAtomBytes +
+                      (r & 7) * 128,
+                  2 * (hl & 3), r & 7, pr[p], pr_sc[p]);
+          }
+          ptx::fence_proxy_async_smem();  // the MMAs read the stage through the async proxy
+          __syncwarp();
+          if (lane == 0) ptx::mbar_arrive(bar(kBarKvFull + stage));
+        }
+      }
+    }
   } else {
     // ------------------------------------------------------------------ softmax + epilogue
     // One thread per head row h (its TMEM lane), 32 own keys per page. Per page: scores to
@@ -852,8 +964,16 @@ __global__ void __launch_bounds__(kThreads, 1)
   // Every message, row sum and buffer release between the pair has been awaited by its receiver,
   // so the exit barrier need not wait for this CTA's output stores to drain. After a timeout a
   // remote abort flag may still be in flight: then the full barrier orders it first.
-  if (*abort_flag) ptx::cluster_sync();
-  else ptx::cluster_sync_relaxed();
+  if (*abort_flag) {
+    // After a timeout, copies and remote stores may still be in flight towards this CTA's
+    // shared memory: give them a bounded 20 ms to land before the CTA leaves.
+    const uint64_t t0 = ptx::global_timer_ns();
+    for (uint32_t i = 0; i < (1u << 16) && ptx::global_timer_ns() - t0 < 20000000ull; ++i)
+      __nanosleep(1000);
+    ptx::cluster_sync();
+  } else {
+    ptx::cluster_sync_relaxed();
+  }
   if (warp == 1) {
     ptx::tc_fence_after();
     ptx::tmem_dealloc(tmem, kTmemCols);
@@ -1093,10 +1213,10 @@ bool encode_bf16(CUtensorMap* map, const void* addr, int rank, const cuuint64_t*
             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <bool kRope>
+template <bool kRope, bool kFp8 = false>
 cudaError_t prepare_kernel() {
-  return cudaFuncSetAttribute(mla_paged_kernel<kRope>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                              int(kSmBytes));
+  return cudaFuncSetAttribute(mla_paged_kernel<kRope, kFp8>,
+                              cudaFuncAttributeMaxDynamicSharedMemorySize, int(kSmBytes));
 }
 
 // CTA pairs that are co-resident on `device` (the persistent grid size).
@@ -1112,7 +1232,8 @@ int pairs_for_device(int device) {
   int sms = 0;
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
   int clusters = 0;
-  if (prepare_kernel<true>() == cudaSuccess && prepare_kernel<false>() == cudaSuccess) {
+  if (prepare_kernel<true>() == cudaSuccess && prepare_kernel<false>() == cudaSuccess &&
+      prepare_kernel<false, true>() == cudaSuccess) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * (sms / 2), 1, 1);
     cfg.blockDim = dim3(kThreads, 1, 1);
@@ -1196,8 +1317,8 @@ int32_t launch(const TqMlaParams* params, void* workspace, uint64_t workspace_by
   set_err(err, nullptr, TQ_OK);
   if (!params->should_launch) return TQ_OK;
   const TqMlaSpec& s = params->spec;
-  if (s.kv_format == TQ_KV_FP8_E4M3) return set_err(err, "kv_format", TQ_ERR_UNSUPPORTED);
   const bool rope = s.kv_format == TQ_KV_BF16_ROPE576;
+  const bool fp8 = s.kv_format == TQ_KV_FP8_E4M3;
   int device = 0;
   if (cudaGetDevice(&device) != cudaSuccess) return set_err(err, "device", TQ_ERR_CUDA);
   const int pairs = pairs_for_device(device);
@@ -1245,10 +1366,15 @@ int32_t launch(const TqMlaParams* params, void* workspace, uint64_t workspace_by
     const cuuint32_t vbox[4] = {64, 8, uint32_t(kValueHalf / 64), uint32_t(kKeysPerCta / 8)};
     const void* qa = reinterpret_cast<const void*>(s.q.device_address);
     const void* ka = reinterpret_cast<const void*>(s.kv.device_address);
-    if (!encode_bf16(&tq_map, qa, 3, qdims, qstr, qbox, CU_TENSOR_MAP_SWIZZLE_128B) ||
-        !encode_bf16(&tkv, ka, 4, kdims, kstr, kbox, CU_TENSOR_MAP_SWIZZLE_128B) ||
-        !encode_bf16(&tv, ka, 4, kdims, kstr, vbox, CU_TENSOR_MAP_SWIZZLE_128B))
+    if (!encode_bf16(&tq_map, qa, 3, qdims, qstr, qbox, CU_TENSOR_MAP_SWIZZLE_128B))
       return set_err(err, "tensor_map", TQ_ERR_CUDA);
+    if (fp8) {
+      tkv = tq_map;  // FP8 rows are read with plain loads: the KV maps are not used
+      tv = tq_map;
+    } else if (!encode_bf16(&tkv, ka, 4, kdims, kstr, kbox, CU_TENSOR_MAP_SWIZZLE_128B) ||
+               !encode_bf16(&tv, ka, 4, kdims, kstr, vbox, CU_TENSOR_MAP_SWIZZLE_128B)) {
+      return set_err(err, "tensor_map", TQ_ERR_CUDA);
+    }
     MainArgs a;
     a.meta = m;
     a.q = reinterpret_cast<const char*>(s.q.device_address);
@@ -1266,10 +1392,12 @@ int32_t launch(const TqMlaParams* params, void* workspace, uint64_t workspace_by
     a.out_f32 = s.out.dtype == TQ_DTYPE_F32;
     a.lse = reinterpret_cast<float*>(s.lse.device_address);
     a.scale_log2 = s.softmax_scale * 1.4426950408889634f;
+    a.kv = reinterpret_cast<const uint8_t*>(s.kv.device_address);
+    a.kv_row_stride = (long long)params->row_stride;
 
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * pairs, 1, 1);
-    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.blockDim = dim3(fp8 ? kThreadsFp8 : kThreads, 1, 1);
     cfg.dynamicSmemBytes = kSmBytes;
     cfg.stream = st;
     cudaLaunchAttribute attr[2];
@@ -1283,8 +1411,10 @@ int32_t launch(const TqMlaParams* params, void* workspace, uint64_t workspace_by
     cfg.numAttrs = 2;
     if (t_timer_begin && cudaEventRecord(t_timer_begin, st) != cudaSuccess)
       return set_err(err, "timer", TQ_ERR_CUDA);
-    cudaError_t e = rope ? cudaLaunchKernelEx(&cfg, mla_paged_kernel<true>, tq_map, tkv, tv, a)
-                         : cudaLaunchKernelEx(&cfg, mla_paged_kernel<false>, tq_map, tkv, tv, a);
+    cudaError_t e =
+        rope  ? cudaLaunchKernelEx(&cfg, mla_paged_kernel<true>, tq_map, tkv, tv, a)
+        : fp8 ? cudaLaunchKernelEx(&cfg, mla_paged_kernel<false, true>, tq_map, tkv, tv, a)
+              : cudaLaunchKernelEx(&cfg, mla_paged_kernel<false>, tq_map, tkv, tv, a);
     if (e != cudaSuccess) return set_err(err, "launch", TQ_ERR_CUDA);
     if (t_timer_end && cudaEventRecord(t_timer_end, st) != cudaSuccess)
       return set_err(err, "timer", TQ_ERR_CUDA);

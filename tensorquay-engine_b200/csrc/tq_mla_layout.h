@@ -30,6 +30,9 @@ constexpr int kSegmentCostPages = 8;
 constexpr int kSoftmaxWarps = 4;
 constexpr int kSoftmaxThreads = 32 * kSoftmaxWarps;
 constexpr int kThreads = 64 + kSoftmaxThreads;  // warp 0 TMA, warp 1 MMA, warps 2-5 softmax
+constexpr int kConvertWarps = 4;                 // FP8 rows: warps 6-9 dequantize the pages
+constexpr int kThreadsFp8 = kThreads + 32 * kConvertWarps;
+constexpr int kFp8RowCodes = 512;                // E4M3 codes per row, then 4 f32 scales
 constexpr int kQTmemDims = 384;                 // query dims held in TMEM (A operand)
 
 // Shared memory (byte offsets from a 1024-aligned base).
@@ -82,8 +85,10 @@ enum Bar : int {
   kBarMsgFree = kBarMsgFull + 8,        // [2] the peer's PV of the buffer's last page is done
                                         //     (one arrival, the peer MMA warp's commit)
   kBarLsumFull = kBarMsgFree + 2,       // [4] peer warp's row sums landed (tx bytes)
-  kBarSpare = kBarLsumFull + 4,         // [15] unused
-  kBarDrain = kBarSpare + 15,
+  kBarKvGrant = kBarLsumFull + 4,       // [kStages] FP8: a page's stage is free (the producer,
+                                        //     the only waiter on kBarKvEmpty, passes it on)
+  kBarSpare = kBarKvGrant + kStages,    // [15 - kStages] unused
+  kBarDrain = kBarSpare + 15 - kStages,
   kBarCount
 };
 static_assert(kBarCount == kNumBars, "barrier count");

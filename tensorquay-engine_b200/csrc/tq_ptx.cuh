@@ -353,6 +353,18 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   return r;
 }
 
+// Two E4M3 codes (bits 0-7: first, bits 8-15: second) times `scale`, as packed bf16 (first in
+// the low half). The codes widen exactly to f16, then to f32; only the final bf16 rounds.
+__device__ __forceinline__ uint32_t e4m3x2_scaled_bf16x2(uint32_t codes, float scale) {
+  uint32_t h2;
+  asm("{\n\t.reg .b16 c;\n\tcvt.u16.u32 c, %1;\n\tcvt.rn.f16x2.e4m3x2 %0, c;\n\t}"
+      : "=r"(h2) : "r"(codes));
+  float lo, hi;
+  asm("{\n\t.reg .b16 l, h;\n\tmov.b32 {l, h}, %2;\n\tcvt.f32.f16 %0, l;\n\tcvt.f32.f16 %1, h;\n\t}"
+      : "=f"(lo), "=f"(hi) : "r"(h2));
+  return pack_bf16x2(lo * scale, hi * scale);
+}
+
 __device__ __forceinline__ float bf16_lo(uint32_t v) { return __uint_as_float(v << 16); }
 __device__ __forceinline__ float bf16_hi(uint32_t v) { return __uint_as_float(v & 0xFFFF0000u); }
 

@@ -120,7 +120,7 @@ class Workload:
 
     def bytes(self):
         """Algorithmic bytes: each cached row once, q, out, lse, block tables and lengths."""
-        rows = float(self.kv_len.sum()) * self.width * 2
+        rows = float(self.kv_len.sum()) * self.extra.get("kv_row_bytes", self.width * 2)
         pages = float(((self.kv_len + PAGE_ROWS - 1) // PAGE_ROWS).sum())
         t = self.tokens
         return rows + t * self.heads * (self.width * 2 + 1024 + 4) + 4 * pages + 4 * self.sequences
@@ -146,6 +146,16 @@ def config(name, *, batch=None):
         kv = np.array([17, 64, 200, 1000], dtype=np.int64)
         w = Workload("cpu_decode_h16", 0, 16, 576, kv, np.ones(4, np.int64), kv - 1, scale)
         return _finish(w, pool_pages=64)
+    if name == "decode_fp8":
+        # The decode batch with FP8 E4M3 rows (512 codes + 4 f32 scales; no RoPE part, q width
+        # 512, the format's fixed scale 1/16).
+        b = 64 if batch is None else batch
+        kv = uniform_lengths(1, b, 4096, 8192)
+        w = Workload("decode_fp8_b64_h128_ctx4k-8k", 1, 128, 512, kv, np.ones(b, np.int64),
+                     kv - 1, 0.0625)
+        w.extra["kv_format"] = "fp8_e4m3"
+        w.extra["kv_row_bytes"] = FP8_ROW_PAYLOAD
+        return _finish(w)
     if name == "decode":
         b = 64 if batch is None else batch
         kv = uniform_lengths(1, b, 4096, 8192)
@@ -204,17 +214,12 @@ class DeviceBatch:
     query_counts: list
 
 
-def materialize(w: Workload, device, *, row_stride=None, q_seed=None):
-    """Allocate and fill the device tensors of ``w`` with the seeded generator."""
+def _gen_q(w: Workload, dev, q_seed=None):
     import torch
 
-    dev = torch.device(device)
     stream = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
-    width = w.width
-    row_stride = row_stride or width * 2
-    t = w.tokens
-    q = torch.empty((t, w.heads, width), dtype=torch.bfloat16, device=dev)
-    per_tok = w.heads * width
+    q = torch.empty((w.tokens, w.heads, w.width), dtype=torch.bfloat16, device=dev)
+    per_tok = w.heads * w.width
     local = 0
     for b in range(w.sequences):
         n = int(w.q_per_seq[b]) * per_tok
@@ -223,6 +228,20 @@ def materialize(w: Workload, device, *, row_stride=None, q_seed=None):
                                              n, q_seed if q_seed is not None else w.seed,
                                              STREAM_Q, int(w.token_global[b]) * per_tok, stream))
         local += int(w.q_per_seq[b])
+    return q
+
+
+def materialize(w: Workload, device, *, row_stride=None, q_seed=None):
+    """Allocate and fill the device tensors of ``w`` with the seeded generator."""
+    import torch
+
+    if w.extra.get("kv_format") == "fp8_e4m3":
+        return materialize_fp8(w, device, row_stride=row_stride or 544, q_seed=q_seed)
+    dev = torch.device(device)
+    stream = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+    width = w.width
+    row_stride = row_stride or width * 2
+    q = _gen_q(w, dev, q_seed)
     pool_bytes = max(1, w.pool_pages) * PAGE_ROWS * row_stride
     kv_raw = torch.empty(pool_bytes, dtype=torch.uint8, device=dev)
     kv = kv_raw[: w.pool_pages * PAGE_ROWS * row_stride].view(w.pool_pages, PAGE_ROWS, row_stride)
@@ -241,5 +260,64 @@ def materialize(w: Workload, device, *, row_stride=None, q_seed=None):
         seq_id=torch.from_numpy(w.seq_id()).to(dev),
         q_pos=torch.from_numpy(w.q_pos()).to(dev),
         kv_len=kv_len,
+        query_counts=[int(c) for c in w.q_per_seq],
+    )
+
+
+FP8_ROW_PAYLOAD = 528
+
+
+def used_rows(w: Workload):
+    """Boolean ``[pool_pages * 64]``: pool rows that hold a cached position of some sequence."""
+    used = np.zeros(max(1, w.pool_pages) * PAGE_ROWS, dtype=bool)
+    table = w.extra["page_table"]
+    for b in range(w.sequences):
+        n = int(w.kv_len[b])
+        pos = np.arange(n)
+        used[table[b, pos // PAGE_ROWS].astype(np.int64) * PAGE_ROWS + pos % PAGE_ROWS] = True
+    return used
+
+
+def materialize_fp8(w: Workload, device, *, row_stride=544, q_seed=None, poison=True):
+    """Device tensors of ``w`` with FP8 E4M3 rows ``uint8 [P, 64, row_stride]``.
+
+    q is the seeded bf16 generator's (width 512). Each cached position's 512 latent values are
+    drawn N(0, 1) from a torch generator seeded with ``w.seed`` and quantized per 128-value tile
+    with scale = amax / 448 (round to nearest even, the format's largest finite magnitude is
+    448). With ``poison``, rows that hold no cached position carry NaN codes and NaN scales, so a
+    kernel that read them would produce NaN.
+    """
+    import torch
+
+    assert w.width == 512 and row_stride >= FP8_ROW_PAYLOAD and row_stride % 16 == 0
+    dev = torch.device(device)
+    q = _gen_q(w, dev, q_seed)
+    rows_total = max(1, w.pool_pages) * PAGE_ROWS
+    pool = torch.zeros((rows_total, row_stride), dtype=torch.uint8, device=dev)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(int(w.seed) * 7919 + 17)
+    chunk = 1 << 16
+    for r0 in range(0, rows_total, chunk):
+        r1 = min(rows_total, r0 + chunk)
+        x = torch.randn((r1 - r0, 4, 128), generator=gen, device=dev, dtype=torch.float32)
+        amax = x.abs().amax(dim=2, keepdim=True).clamp_min(1e-30)
+        scale = amax / 448.0
+        codes = (x / scale).clamp(-448.0, 448.0).to(torch.float8_e4m3fn).view(torch.uint8)
+        pool[r0:r1, :512] = codes.reshape(r1 - r0, 512)
+        pool[r0:r1, 512:528] = scale.reshape(r1 - r0, 4).contiguous().view(torch.uint8)
+    if poison:
+        unused = torch.from_numpy(~used_rows(w)).to(dev)
+        pool[unused, :512] = 0x7F
+        nan = torch.full((1, 4), float("nan"), dtype=torch.float32, device=dev).view(torch.uint8)
+        pool[unused, 512:528] = nan
+    kv = pool[: w.pool_pages * PAGE_ROWS].view(w.pool_pages, PAGE_ROWS, row_stride)
+    table = torch.from_numpy(w.extra["page_table"]).to(dev)
+    return DeviceBatch(
+        q=q,
+        kv=kv,
+        page_table=table,
+        seq_id=torch.from_numpy(w.seq_id()).to(dev),
+        q_pos=torch.from_numpy(w.q_pos()).to(dev),
+        kv_len=torch.from_numpy(w.kv_len.astype(np.int32)).to(dev),
         query_counts=[int(c) for c in w.q_per_seq],
     )
