@@ -1,13 +1,15 @@
 """Benchmark of the B200 paged-MLA attention path (one JSON line on rank 0).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--config decode|mtp|prefill|longctx|cpu] [--cpu-sample S]
+                    [--config decode|decode_fp8|mtp|prefill|longctx|cpu] [--cpu-sample S]
 
 A step is one launch of the attention path (scheduler, tcgen05 attention kernel, combine) over
 one batch of synthetic, seeded input already resident in HBM. The default workload is bf16 paged
 decode: 64 sequences x 1 query token, 128 heads, 576-wide latent+RoPE rows, 512-wide output,
 cached lengths uniform in [4096, 8192], 64-row pages from a permuted pool. The pool (~0.5 GB)
 exceeds L2 (126 MB), so every step reads its rows from HBM; no L2 flush is needed.
+``--config decode_fp8`` is the same batch with FP8 E4M3 rows (512 codes + 4 f32 scales, stored
+544 bytes apart; q 512 wide).
 
 With N ranks (torchrun, one GPU each) the job holds N x 64 sequences drawn from the same seeded
 stream and sharded by token count (weak scaling); there is no collective on the data path.
@@ -55,7 +57,8 @@ def workload_for(name, world, rank):
 
     if world == 1:
         return inputs.config(name)
-    base = {"decode": 64, "mtp": 512, "prefill": 8, "longctx": 4, "cpu": 4}[name]
+    base = {"decode": 64, "decode_fp8": 64, "mtp": 512, "prefill": 8, "longctx": 4,
+            "cpu": 4}[name]
     if name in ("cpu",):
         return inputs.config(name)
     full = inputs.config(name, batch=base * world)
@@ -128,7 +131,7 @@ def _cpu_worker(args):
     os.environ.setdefault("OMP_NUM_THREADS", "1")
     name, world, seqs = args
     sys.path.insert(0, str(ROOT))
-    from oracle import generate as ogen, mla as omla
+    from oracle import fp8 as ofp8, generate as ogen, mla as omla
     from tq_mla import inputs  # host metadata only (no device)
 
     w = workload_for(name, world, 0) if world > 1 else inputs.config(name)
@@ -139,13 +142,26 @@ def _cpu_worker(args):
     for b in seqs:
         n = int(w.kv_len[b])
         t = int(w.q_per_seq[b])
-        rows = ogen.bf16_to_f64(ogen.normal_bf16(w.seed, ogen.STREAM_KV, int(tok_off[b]) * w.width,
-                                                 n * w.width)).reshape(n, w.width)
+        fp8 = w.extra.get("kv_format") == "fp8_e4m3"
         pages = (n + 63) // 64
         perm = np.random.default_rng(b).permutation(pages)
-        pool = np.zeros((pages * 64, w.width))
         pos = np.arange(n)
-        pool[perm[pos // 64] * 64 + pos % 64] = rows
+        if fp8:
+            # FP8 rows: random finite codes and tile scales of the generator's magnitude; the
+            # timed part then also decodes the sequence's rows.
+            rng = np.random.default_rng(int(w.seed) * 1000 + b)
+            pool = np.zeros((pages * 64, 544), np.uint8)
+            codes = rng.integers(0, 0x7E, size=(n, 512), dtype=np.uint8)
+            codes |= (rng.integers(0, 2, size=(n, 512), dtype=np.uint8) << 7)
+            pool[perm[pos // 64] * 64 + pos % 64, :512] = codes
+            scales = np.full((n, 4), 4.0 / 448.0, np.float32)
+            pool[perm[pos // 64] * 64 + pos % 64, 512:528] = scales.view(np.uint8)
+        else:
+            rows = ogen.bf16_to_f64(ogen.normal_bf16(w.seed, ogen.STREAM_KV,
+                                                     int(tok_off[b]) * w.width,
+                                                     n * w.width)).reshape(n, w.width)
+            pool = np.zeros((pages * 64, w.width))
+            pool[perm[pos // 64] * 64 + pos % 64] = rows
         table = perm[None, :].astype(np.int32)
         q = ogen.bf16_to_f64(ogen.normal_bf16(w.seed, ogen.STREAM_Q,
                                               int(tok_global[b]) * w.heads * w.width,
@@ -153,10 +169,22 @@ def _cpu_worker(args):
         seq_id = np.zeros(t, np.int32)
         q_pos = (w.prefix[b] + np.arange(t)).astype(np.int32)
         t0 = time.perf_counter()
-        omla.paged_attention(q, pool, table, seq_id, q_pos, np.array([n]), scale=w.scale)
+        values = ofp8.dequant_rows(pool) if fp8 else pool
+        omla.paged_attention(q, values, table, seq_id, q_pos, np.array([n]), scale=w.scale,
+                             value_dim=512)
         elapsed += time.perf_counter() - t0
         tokens += t
     return tokens, elapsed
+
+
+def _fp8_note(w):
+    return " and FP8 E4M3 row decoding" if w.extra.get("kv_format") == "fp8_e4m3" else ""
+
+
+def kv_format_of(w):
+    from tq_mla import _abi
+
+    return _abi.KV_FP8_E4M3 if w.extra.get("kv_format") == "fp8_e4m3" else None
 
 
 def cpu_baseline(name, world, budget_seqs=None, cores=None):
@@ -179,7 +207,8 @@ def cpu_baseline(name, world, budget_seqs=None, cores=None):
         "kind": "port",
         "sample": f"{tokens} query tokens ({n_seq} of {w.sequences} sequences, spread over the "
                   f"batch) of {w.name}; float64 oracle restatement of mla_attention_core with "
-                  f"block-table gather; {len(chunks)} spawn processes x 1 BLAS thread; "
+                  f"block-table gather{_fp8_note(w)}; {len(chunks)} spawn processes x 1 BLAS "
+                  f"thread; "
                   f"throughput = tokens / slowest process",
         "seconds": wall,
     }
@@ -217,17 +246,18 @@ def run_reference(args, world, rank):
                 times.append(busy)
                 tokens.append(tok)
     value = sum(tokens) / sum(times)
+    dtype = "f64" + (" (FP8 E4M3 rows decoded to f64)" if _fp8_note(w) else "")
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT,
         "n_gpus": world, "steps": len(times), "steps_requested": args.steps, "warmup": warmup,
         "ms_per_step": 1e3 * float(np.mean(times)), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
+        "scaling": "weak", "vs_baseline": None, "dtype": dtype, "data": "synthetic",
         "config": {"workload": w.name, "heads": w.heads, "row_width": w.width,
                    "sequences_per_step": per_step},
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port",
                          "sample": f"{per_step} sequences of {w.name} per step, one per spawn "
                                    f"process (1 BLAS thread each); timed part = block-table "
-                                   f"gather + float64 attention per sequence"},
+                                   f"gather{_fp8_note(w)} + float64 attention per sequence"},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -261,7 +291,8 @@ def run_ours(args, world, rank, local_rank):
     lse = torch.empty((w.tokens, w.heads), dtype=torch.float32, device=dev)
     launch = ops.MlaLaunch(batch.q, batch.kv, batch.page_table, batch.seq_id, batch.q_pos,
                            batch.kv_len, out, lse, scale=w.scale,
-                           query_counts=batch.query_counts, prefill=args.config == "prefill")
+                           query_counts=batch.query_counts, prefill=args.config == "prefill",
+                           kv_format=kv_format_of(w))
     stream = torch.cuda.current_stream(dev)
 
     # Host copies for the end-to-end leg (pinned). The four int32 metadata arrays travel as one
@@ -355,7 +386,7 @@ def run_ours(args, world, rank, local_rank):
         lse_d = torch.empty_like(lse)
         lk = ops.MlaLaunch(q_d, batch.kv, meta_d[0], meta_d[1], meta_d[2], meta_d[3], out_d, lse_d,
                            scale=w.scale, query_counts=batch.query_counts,
-                           prefill=args.config == "prefill")
+                           prefill=args.config == "prefill", kv_format=kv_format_of(w))
         h_o = torch.empty_like(out, device="cpu").pin_memory()
         h_l = torch.empty_like(lse, device="cpu").pin_memory()
         ev = [torch.cuda.Event() for _ in range(3)]  # inputs landed, computed, copied out
@@ -433,14 +464,16 @@ def run_ours(args, world, rank, local_rank):
     result = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "scaling": "weak", "vs_baseline": None,
+        "dtype": "fp8_e4m3 rows, bf16 operands" if kv_format_of(w) is not None else "bf16",
+        "data": "synthetic",
         "config": {
             "workload": w.name if world == 1 else f"{w.name} x{world} ranks (token-sharded)",
             "sequences": int(sum_over_ranks(float(w.sequences))),
             "query_tokens": int(tokens_all), "heads": w.heads, "row_width": w.width,
             "value_width": 512, "page_rows": 64, "parallelism": f"sequence-shard x{world}",
             "l2": "inputs larger than L2 (KV pool %.0f MB per GPU), no flush" %
-                  (w.pool_pages * 64 * w.width * 2 / 1e6),
+                  (batch.kv.numel() * batch.kv.element_size() / 1e6),
             "tflops_total": flops_all / (ms_step * 1e-3) / 1e12,
         },
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": int(h2d),
@@ -464,7 +497,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", default="decode",
-                    choices=["decode", "mtp", "prefill", "longctx", "cpu"])
+                    choices=["decode", "decode_fp8", "mtp", "prefill", "longctx", "cpu"])
     ap.add_argument("--cpu-sample", type=int, default=None,
                     help="sequences in the CPU baseline sample (default: up to 64)")
     ap.add_argument("--no-cpu-baseline", action="store_true")

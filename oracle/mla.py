@@ -171,16 +171,18 @@ def combine_partials(partial_out, partial_lse):
 
     ``partial_out [k, ..., Dv]`` holds outputs normalised over each part and ``partial_lse
     [k, ...]`` their natural-log lse. A row whose parts are all ``-inf`` yields zeros and
-    ``-inf`` with no NaN.
+    ``-inf`` with no NaN. A NaN part (a NaN in one of its visible rows) makes the merged row NaN,
+    as the unsplit attention over the same rows is (anomaly positions match the single pass).
     """
-    m = partial_lse.max(axis=0)
+    nan_part = np.isnan(partial_lse)
+    m = np.where(nan_part, -np.inf, partial_lse).max(axis=0)
     finite = np.isfinite(m)
     safe_m = np.where(finite, m, 0.0)
     with np.errstate(invalid="ignore", over="ignore"):
-        w = np.where(np.isfinite(partial_lse), np.exp(partial_lse - safe_m), 0.0)
-    total = w.sum(axis=0)
-    denom = np.where(total > 0, total, 1.0)
-    out = np.where((total > 0)[..., None], (w[..., None] * partial_out).sum(0) / denom[..., None],
-                   0.0)
-    lse = np.where(total > 0, safe_m + np.log(denom), -np.inf)
+        w = np.where(np.isneginf(partial_lse), 0.0, np.exp(partial_lse - safe_m))
+        total = w.sum(axis=0)
+        denom = np.where(total == 0, 1.0, total)
+        out = np.where((total == 0)[..., None], 0.0,
+                       (w[..., None] * partial_out).sum(0) / denom[..., None])
+        lse = np.where(total == 0, -np.inf, safe_m + np.log(denom))
     return out, lse

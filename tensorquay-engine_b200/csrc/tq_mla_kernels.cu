@@ -1056,7 +1056,8 @@ __global__ void __launch_bounds__(256) combine_kernel(Meta m, char* out, long lo
 #pragma unroll
     for (int k = 0; k < 8; ++k) acc[k] *= inv;
     store8(out + u * st_t + h * st_h + (long long)d0 * esize, out_f32, acc);
-    if (d0 == 0) lse[(long long)u * heads + h] = wsum > 0.f ? mx + logf(wsum) : -INFINITY;
+    // -inf only for an empty weight sum: a NaN partial (a NaN in a visible row) stays NaN.
+    if (d0 == 0) lse[(long long)u * heads + h] = wsum == 0.f ? -INFINITY : mx + logf(wsum);
   }
   // Tokens with no visible key: zeros and lse = -inf.
   const float z[8] = {0, 0, 0, 0, 0, 0, 0, 0};
@@ -1102,7 +1103,7 @@ __global__ void __launch_bounds__(256) merge_parts_kernel(const float* __restric
 #pragma unroll
     for (int k = 0; k < 8; ++k) acc[k] *= inv;
     store8(out + t * st_t + h * st_h + (long long)d0 * esize, out_f32, acc);
-    if (d0 == 0) lse[row] = wsum > 0.f ? mx + logf(wsum) : -INFINITY;
+    if (d0 == 0) lse[row] = wsum == 0.f ? -INFINITY : mx + logf(wsum);  // NaN stays NaN
   }
 }
 

@@ -38,8 +38,10 @@ def _workload(seed, heads, lens, per_seq=1):
     return w
 
 
-def _run(w, device, row_stride, prefill=False):
+def _run(w, device, row_stride, prefill=False, mutate=None):
     b = inputs.materialize_fp8(w, device, row_stride=row_stride)
+    if mutate is not None:
+        mutate(b)
     out = torch.empty((w.tokens, w.heads, 512), dtype=torch.bfloat16, device=device)
     lse = torch.empty((w.tokens, w.heads), dtype=torch.float32, device=device)
     launch = ops.MlaLaunch(b.q, b.kv, b.page_table, b.seq_id, b.q_pos, b.kv_len, out, lse,
@@ -86,3 +88,41 @@ def test_fp8_causal_prefill_chunks(cuda_device, lens, per_seq):
     assert launch.device_error() == 0
     assert np.isfinite(out).all()
     _check(out, lse, refs, f"fp8 prefill {lens}")
+
+
+def _pool_row(w, seq, pos):
+    return int(w.extra["page_table"][seq][pos // 64]) * 64 + pos % 64
+
+
+def test_fp8_large_scales_and_nan_codes(cuda_device):
+    """Tiles the kernel dequantizes through the conversion instructions instead of exponent
+    placement: scales of 2^8 and more (subnormal codes keep the values moderate), next to a
+    tile with scale 255 on the fast path, and a NaN code in
+    a visible row, which makes that token's output and lse NaN (the oracle's too) and leaves the
+    other tokens exact."""
+    w = _workload(73, 16, [200, 300, 90])
+    big_rows = [_pool_row(w, 1, p) for p in (3, 64, 150, 299)]
+    nan_row = _pool_row(w, 0, 17)
+
+    def mutate(b):
+        flat = b.kv.view(-1, b.kv.shape[-1])
+        gen = torch.Generator(device=flat.device)
+        gen.manual_seed(5)
+        for r in big_rows:
+            # codes 0, 1, 2 are 0, 2^-9, 2^-8: times the scales below, values of at most 4
+            small = torch.randint(0, 3, (512,), generator=gen, device=flat.device,
+                                  dtype=torch.int32).to(torch.uint8)
+            sign = (torch.randint(0, 2, (512,), generator=gen, device=flat.device,
+                                  dtype=torch.int32) * 0x80).to(torch.uint8)
+            flat[r, :512] = small | sign
+            sc = torch.tensor([256.0, 300.0, 1024.0, 255.0], device=flat.device)
+            flat[r, 512:528] = sc.view(torch.uint8)
+        flat[nan_row, 40] = 0x7F
+
+    launch, out, lse, refs = _run(w, cuda_device, 544, mutate=mutate)
+    assert launch.device_error() == 0
+    assert np.isnan(out[0]).all() and np.isnan(lse[0]).all()
+    assert np.isnan(refs[0][0][0]).all()
+    keep = [1, 2]
+    sub = [(o[keep], l[keep]) for o, l in refs]
+    _check(out[keep], lse[keep], sub, "fp8 large scales")

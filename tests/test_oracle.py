@@ -165,6 +165,21 @@ def test_lse_merge_of_splits_equals_unsplit():
     assert (o == 0).all() and np.isneginf(l_).all()
 
 
+def test_lse_merge_keeps_a_nan_split_nan():
+    """A NaN in one split's visible rows makes the merged row NaN, like the unsplit pass."""
+    rng = np.random.default_rng(4)
+    q = rng.standard_normal((4, 576))
+    rows = rng.standard_normal((300, 576))
+    rows[170, 9] = np.nan
+    full_o, full_l = omla.identity_core(q, rows, 0.07, 512)
+    assert np.isnan(full_o).all() and np.isnan(full_l).all()
+    cuts = [0, 128, 256, 300]
+    parts = [omla.identity_core(q, rows[a:b], 0.07, 512) for a, b in zip(cuts[:-1], cuts[1:])]
+    parts.append((np.zeros((4, 512)), np.full(4, -np.inf)))
+    o, l_ = omla.combine_partials(np.stack([p[0] for p in parts]), np.stack([p[1] for p in parts]))
+    assert np.isnan(o).all() and np.isnan(l_).all()
+
+
 def test_planted_mistake_in_the_oracle_is_caught():
     """The parity check fails when the oracle uses the wrong scale (the checker has teeth)."""
     g = np.load(GOLDEN / "paged_cases.npz")
