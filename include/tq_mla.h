@@ -33,7 +33,7 @@ enum { TQ_DTYPE_BF16 = 0, TQ_DTYPE_I32 = 1, TQ_DTYPE_F32 = 2, TQ_DTYPE_U8 = 3 };
 /* Paged row formats (contracts.rs:129-144), plus the 576-wide DeepSeek-style row. */
 enum {
   TQ_KV_BF16 = 0,         /* 512 bf16 latent values, 1024 B, q width 512, scale 0.0625   */
-  TQ_KV_FP8_E4M3 = 1,     /* 512 E4M3 codes + 4 f32 scales, 528 B (validated; not launched) */
+  TQ_KV_FP8_E4M3 = 1,     /* 512 E4M3 codes + 4 f32 scales, 528 B; q 512 wide (bf16) */
   TQ_KV_BF16_ROPE576 = 2  /* 512 latent + 64 RoPE bf16, 1152 B, q width 576, any scale > 0  */
 };
 
