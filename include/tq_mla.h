@@ -167,6 +167,29 @@ int32_t tq_mla_read_device_error(const void* workspace, void* stream, int32_t* f
 #define TQ_MLA_NO_ALLOC_WORKSPACE_BYTES (42ull << 20)
 int32_t tq_mla_decode_no_alloc(const TqMlaParams* params, void* stream, TqContractError* err);
 
+/* KV cache writer: the planned "latent -> 528 B KV writer" (docs/DEV-PLAN.md:116) over the row
+ * formats of docs/HOST-CONTRACTS.md:122-123 and the paged addressing of contracts.rs:182-209.
+ *   src        bf16 [T, W]   W = 576 (TQ_KV_BF16_ROPE576) or 512 (TQ_KV_BF16, TQ_KV_FP8_E4M3);
+ *                            row stride >= 2 W, address and row stride multiples of 16
+ *   kv         u8   [P, 64, payload] with strides [64 r, r, 1], r >= payload, r % 16 == 0
+ *   page_table i32  [S, L]    seq_id i32 [T]    pos i32 [T]
+ * Row t is written to pool row page_table[seq_id[t]][pos[t] / 64] * 64 + pos[t] % 64: its bf16
+ * bits as they are, or, for FP8 rows, 512 E4M3 codes and four f32 tile scales. FP8 rule per
+ * 128-value tile: a NaN in the tile gives scale NaN and codes 0x7F; amax == 0 gives scale 0 and
+ * codes 0; otherwise scale = amax / 448 and code = E4M3(x / scale) (f32 divisions rounded to
+ * nearest even, E4M3 rounded to nearest even and saturated to +-448). Bytes past the payload are
+ * not touched. A row whose seq_id, pos or page entry is out of range is skipped and, when
+ * `device_flags` (a device int32, may be null) is given, TQ_DEV_SEQ_RANGE, TQ_DEV_TABLE_SHORT or
+ * TQ_DEV_PAGE_RANGE is OR-ed into it. Two rows naming one slot in a call race (either may win).
+ * The launch grid depends only on the device, so a captured call replays for new contents. */
+typedef struct {
+  TqTensorSpec src, kv, page_table, seq_id, pos;
+  int32_t kv_format;
+} TqKvWriteSpec;
+int32_t tq_kv_write_validate(const TqKvWriteSpec* spec, TqContractError* err);
+int32_t tq_kv_write(const TqKvWriteSpec* spec, int32_t* device_flags, void* stream,
+                    TqContractError* err);
+
 /* Measurement hook, no reference counterpart. Makes later tq_mla_decode / tq_mla_prefill calls
  * on the calling thread record `begin_event` right before and `end_event` right after the
  * attention kernel, on the launch stream (both are cudaEvent_t created by the caller). Pass two

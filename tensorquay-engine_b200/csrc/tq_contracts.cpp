@@ -244,6 +244,51 @@ int32_t validate_impl(const TqMlaSpec* spec, const Count* counts, uint64_t n, in
   return TQ_OK;
 }
 
+// The KV writer's declarations: the same per-tensor checks as the attention plan, the pool as
+// the output that no input may overlap, and 16-byte vector access to the source rows.
+int32_t kv_write_validate_impl(const TqKvWriteSpec* spec, TqContractError* err) {
+  Failure f{nullptr, TQ_OK};
+  auto fail = [&](const char* field, int32_t kind) {
+    if (err) { err->field = field; err->kind = kind; }
+    return kind;
+  };
+  if (!spec) return fail("spec", TQ_ERR_INVALID_ARGUMENT);
+  const TqKvWriteSpec& s = *spec;
+  uint64_t payload = 0, width = 0;
+  switch (s.kv_format) {
+    case TQ_KV_BF16: payload = 1024; width = 512; break;
+    case TQ_KV_FP8_E4M3: payload = 528; width = 512; break;
+    case TQ_KV_BF16_ROPE576: payload = 1152; width = 576; break;
+    default: return fail("kv_format", TQ_SHAPE);
+  }
+  if (s.src.rank != 2) return fail("src", TQ_SHAPE);
+  if (s.page_table.rank != 2) return fail("page_table", TQ_SHAPE);
+  const uint64_t rows = s.src.shape[0];
+  const uint64_t sequences = s.page_table.shape[0], slots = s.page_table.shape[1];
+  const bool launching = rows != 0;
+  if (!check_kv_strides(s.kv, payload, &f)) return fail(f.field, f.kind);
+  const uint64_t src_shape[2] = {rows, width};
+  const uint64_t pool[3] = {s.kv.shape[0], kPageRows, payload};
+  const uint64_t table[2] = {sequences, slots};
+  const uint64_t tok[1] = {rows};
+  Extent in[4], out[1];
+  if (!check("src", s.src, src_shape, 2, TQ_DTYPE_BF16, Layout::PaddedOuter, launching, &in[0],
+             &f) ||
+      !check("page_table", s.page_table, table, 2, TQ_DTYPE_I32, Layout::Packed, launching,
+             &in[1], &f) ||
+      !check("seq_id", s.seq_id, tok, 1, TQ_DTYPE_I32, Layout::Packed, launching, &in[2], &f) ||
+      !check("pos", s.pos, tok, 1, TQ_DTYPE_I32, Layout::Packed, launching, &in[3], &f) ||
+      !check("kv", s.kv, pool, 3, TQ_DTYPE_U8, Layout::Checked, launching, &out[0], &f))
+    return fail(f.field, f.kind);
+  if (launching) {
+    if (s.src.strides_bytes[0] % 16) return fail("src", TQ_STRIDE);
+    if (s.src.device_address % 16) return fail("src", TQ_ALIGNMENT);
+  }
+  if (!check_aliases(in, 4, out, 1, &f)) return fail(f.field, f.kind);
+  if (err) { err->field = nullptr; err->kind = TQ_OK; }
+  return TQ_OK;
+}
+
 }  // namespace
 
 bool params_intact(const TqMlaParams* p) { return p && p->digest == digest_of(*p); }
@@ -305,6 +350,10 @@ int32_t tq_mla_validate(const TqMlaSpec* spec, const uint8_t* query_counts, uint
 int32_t tq_mla_prefill_validate(const TqMlaSpec* spec, const uint32_t* query_counts, uint64_t n,
                                 TqMlaParams* params, TqContractError* err) {
   return tq::validate_impl(spec, query_counts, n, 0, params, err);
+}
+
+int32_t tq_kv_write_validate(const TqKvWriteSpec* spec, TqContractError* err) {
+  return tq::kv_write_validate_impl(spec, err);
 }
 
 int32_t tq_mla_should_launch(const TqMlaParams* params) {

@@ -1,0 +1,188 @@
+// KV cache writer: new latent rows into the paged pool (docs/DEV-PLAN.md:116, "latent -> 528 B KV
+// writer"; row formats docs/HOST-CONTRACTS.md:122-123; paged addressing contracts.rs:182-209).
+//
+// One warp per row, grid-stride over the rows. A bf16 row (1024 or 1152 bytes) is copied with
+// 16-byte loads and stores. An FP8 row is quantized on the way: lane l holds values
+// [16 l, 16 l + 16) (two 16-byte loads of bf16), the eight lanes of a 128-value tile reduce their
+// amax and NaN flag with shuffles, and each lane writes its 16 E4M3 codes as one 16-byte store;
+// the first lane of a tile writes the tile's f32 scale after the 512 codes. The path is HBM-bound
+// (1024 B read and 528 B written per FP8 row; 2 x 1152 B per 576-wide bf16 row).
+//
+// FP8 rule per tile (the reference defines none; this library's definition): a NaN in the tile
+// gives scale NaN and codes 0x7F; amax == 0 gives scale 0 and codes 0; otherwise
+// scale = amax / 448 and code = E4M3(x / scale), both divisions IEEE round-to-nearest-even in f32
+// (__fdiv_rn; no flush to zero), the conversion round-to-nearest-even with saturation
+// (cvt.rn.satfinite.e4m3x2.f32).
+
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "tq_contracts.h"
+
+namespace tq {
+namespace kvw {
+
+constexpr int kRowsPerBlock = 8;  // one warp per row
+constexpr int kPageRows = 64;
+
+struct Args {
+  const uint8_t* src;
+  long long src_stride;  // bytes between source rows
+  uint8_t* kv;
+  long long row_stride;  // bytes between pool rows
+  long long pages;
+  const int* page_table;
+  long long sequences, slots;
+  const int* seq_id;
+  const int* pos;
+  long long rows;
+  int* flags;  // device error flags (may be null)
+};
+
+__device__ __forceinline__ void flag(const Args& a, int bit) {
+  if (a.flags) atomicOr(a.flags, bit);
+}
+
+// Two f32 values as E4M3 codes: `lo` in bits 0-7, `hi` in bits 8-15.
+__device__ __forceinline__ uint32_t e4m3x2(float lo, float hi) {
+  uint16_t r;
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+
+template <int kFormat>
+__global__ void __launch_bounds__(32 * kRowsPerBlock) kv_write_kernel(Args a) {
+  const int lane = threadIdx.x & 31;
+  const long long step = (long long)gridDim.x * kRowsPerBlock;
+  for (long long t = (long long)blockIdx.x * kRowsPerBlock + (threadIdx.x >> 5); t < a.rows;
+       t += step) {
+    const int s = a.seq_id[t], p = a.pos[t];
+    if (s < 0 || s >= a.sequences) {
+      if (lane == 0) flag(a, TQ_DEV_SEQ_RANGE);
+      continue;
+    }
+    if (p < 0 || p / kPageRows >= a.slots) {
+      if (lane == 0) flag(a, TQ_DEV_TABLE_SHORT);
+      continue;
+    }
+    const int page = a.page_table[(long long)s * a.slots + p / kPageRows];
+    if (page < 0 || page >= a.pages) {
+      if (lane == 0) flag(a, TQ_DEV_PAGE_RANGE);
+      continue;
+    }
+    uint8_t* dst = a.kv + ((long long)page * kPageRows + p % kPageRows) * a.row_stride;
+    const uint8_t* src = a.src + t * a.src_stride;
+    if constexpr (kFormat != TQ_KV_FP8_E4M3) {
+      constexpr int kUnits = (kFormat == TQ_KV_BF16_ROPE576 ? 1152 : 1024) / 16;
+#pragma unroll
+      for (int i = lane; i < kUnits; i += 32)
+        reinterpret_cast<uint4*>(dst)[i] = __ldg(reinterpret_cast<const uint4*>(src) + i);
+    } else {
+      const uint4 w0 = __ldg(reinterpret_cast<const uint4*>(src) + 2 * lane);
+      const uint4 w1 = __ldg(reinterpret_cast<const uint4*>(src) + 2 * lane + 1);
+      const uint32_t words[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+      float x[16];
+      float amax = 0.f;
+      bool nan = false;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        x[2 * i] = __uint_as_float(words[i] << 16);
+        x[2 * i + 1] = __uint_as_float(words[i] & 0xFFFF0000u);
+      }
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        nan |= x[i] != x[i];
+        amax = fmaxf(amax, fabsf(x[i]));
+      }
+      // The eight lanes of a tile are aligned groups of eight: xor 1, 2, 4 stays inside one.
+#pragma unroll
+      for (int o = 1; o < 8; o <<= 1) {
+        amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, o));
+        nan |= __shfl_xor_sync(0xFFFFFFFFu, int(nan), o) != 0;
+      }
+      float scale;
+      uint4 codes;
+      if (nan) {
+        scale = __uint_as_float(0x7FC00000u);
+        codes = make_uint4(0x7F7F7F7Fu, 0x7F7F7F7Fu, 0x7F7F7F7Fu, 0x7F7F7F7Fu);
+      } else if (amax == 0.f) {
+        scale = 0.f;
+        codes = make_uint4(0u, 0u, 0u, 0u);
+      } else {
+        scale = __fdiv_rn(amax, 448.f);
+        uint32_t c[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          c[i] = e4m3x2(__fdiv_rn(x[2 * i], scale), __fdiv_rn(x[2 * i + 1], scale));
+        codes = make_uint4(c[0] | (c[1] << 16), c[2] | (c[3] << 16), c[4] | (c[5] << 16),
+                           c[6] | (c[7] << 16));
+      }
+      reinterpret_cast<uint4*>(dst)[lane] = codes;
+      if ((lane & 7) == 0) reinterpret_cast<float*>(dst + 512)[lane >> 3] = scale;
+    }
+  }
+}
+
+int sm_count(int device) {
+  static int cached[64] = {0};
+  if (device >= 0 && device < 64 && cached[device]) return cached[device];
+  int n = 0;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device) != cudaSuccess) return 0;
+  if (device >= 0 && device < 64) cached[device] = n;
+  return n;
+}
+
+}  // namespace kvw
+}  // namespace tq
+
+extern "C" int32_t tq_kv_write(const TqKvWriteSpec* spec, int32_t* device_flags, void* stream,
+                               TqContractError* err) {
+  using namespace tq::kvw;
+  const int32_t st = tq_kv_write_validate(spec, err);
+  if (st != TQ_OK) return st;
+  const TqKvWriteSpec& s = *spec;
+  const long long rows = (long long)s.src.shape[0];
+  if (rows == 0) return TQ_OK;
+  int device = 0;
+  if (cudaGetDevice(&device) != cudaSuccess) {
+    if (err) { err->field = "device"; err->kind = TQ_ERR_CUDA; }
+    return TQ_ERR_CUDA;
+  }
+  const int sms = sm_count(device);
+  if (sms <= 0) {
+    if (err) { err->field = "device"; err->kind = TQ_ERR_CUDA; }
+    return TQ_ERR_CUDA;
+  }
+  Args a;
+  a.src = reinterpret_cast<const uint8_t*>(s.src.device_address);
+  a.src_stride = (long long)s.src.strides_bytes[0];
+  a.kv = reinterpret_cast<uint8_t*>(s.kv.device_address);
+  a.row_stride = (long long)s.kv.strides_bytes[1];
+  a.pages = (long long)s.kv.shape[0];
+  a.page_table = reinterpret_cast<const int*>(s.page_table.device_address);
+  a.sequences = (long long)s.page_table.shape[0];
+  a.slots = (long long)s.page_table.shape[1];
+  a.seq_id = reinterpret_cast<const int*>(s.seq_id.device_address);
+  a.pos = reinterpret_cast<const int*>(s.pos.device_address);
+  a.rows = rows;
+  a.flags = device_flags;
+  const long long want = (rows + kRowsPerBlock - 1) / kRowsPerBlock;
+  const int blocks = int(want < 8ll * sms ? want : 8ll * sms);
+  cudaStream_t cs = reinterpret_cast<cudaStream_t>(stream);
+  switch (s.kv_format) {
+    case TQ_KV_BF16: kv_write_kernel<TQ_KV_BF16><<<blocks, 32 * kRowsPerBlock, 0, cs>>>(a); break;
+    case TQ_KV_FP8_E4M3:
+      kv_write_kernel<TQ_KV_FP8_E4M3><<<blocks, 32 * kRowsPerBlock, 0, cs>>>(a);
+      break;
+    default:
+      kv_write_kernel<TQ_KV_BF16_ROPE576><<<blocks, 32 * kRowsPerBlock, 0, cs>>>(a);
+      break;
+  }
+  if (cudaGetLastError() != cudaSuccess) {
+    if (err) { err->field = "launch"; err->kind = TQ_ERR_CUDA; }
+    return TQ_ERR_CUDA;
+  }
+  if (err) { err->field = nullptr; err->kind = TQ_OK; }
+  return TQ_OK;
+}

@@ -77,6 +77,11 @@ class TqWorkspaceLayout(ctypes.Structure):
         "part_out")] + [("pairs", ctypes.c_int32)]
 
 
+class TqKvWriteSpec(ctypes.Structure):
+    _fields_ = [(name, TqTensorSpec) for name in ("src", "kv", "page_table", "seq_id", "pos")] + [
+        ("kv_format", ctypes.c_int32)]
+
+
 # Every exported symbol of include/tq_mla.h, with its ctypes prototype.
 _P = ctypes.POINTER
 _U64, _I32, _VP = ctypes.c_uint64, ctypes.c_int32, ctypes.c_void_p
@@ -94,6 +99,8 @@ PROTOTYPES = {
     "tq_mla_read_device_error": (_I32, [_VP, _VP, _P(_I32)]),
     "tq_mla_set_kernel_timer": (_I32, [_VP, _VP]),
     "tq_mla_decode_no_alloc": (_I32, [_P(TqMlaParams), _VP, _P(TqContractError)]),
+    "tq_kv_write_validate": (_I32, [_P(TqKvWriteSpec), _P(TqContractError)]),
+    "tq_kv_write": (_I32, [_P(TqKvWriteSpec), _VP, _VP, _P(TqContractError)]),
     "tq_philox_block": (None, [_P(ctypes.c_uint32), _P(ctypes.c_uint32), _P(ctypes.c_uint32)]),
     "tq_philox_words": (_I32, [_U64, _U64, _U64, _P(ctypes.c_uint32), _U64]),
     "tq_philox_uniform_f32": (ctypes.c_float, [ctypes.c_uint32]),

@@ -184,6 +184,34 @@ def mla_decode(q, kv, page_table, seq_id, q_pos, kv_len, *, scale, query_counts=
     return launch(stream)
 
 
+def kv_write_spec(src, kv, page_table, seq_id, pos, *, kv_format=None):
+    """Declaration of a KV-writer call: ``src`` bf16 ``[T, W]`` rows into the paged pool ``kv``."""
+    if kv_format is None:
+        kv_format = _abi.KV_BF16_ROPE576 if src.shape[-1] == 576 else _abi.KV_BF16
+    s = _abi.TqKvWriteSpec()
+    s.src = spec_of(src)
+    s.kv = pool_spec(kv, kv_format)
+    s.page_table = spec_of(page_table)
+    s.seq_id = spec_of(seq_id)
+    s.pos = spec_of(pos)
+    s.kv_format = kv_format
+    return s
+
+
+def kv_write(src, kv, page_table, seq_id, pos, *, kv_format=None, flags=None, stream=None):
+    """Write row ``t`` of ``src`` to position ``pos[t]`` of sequence ``seq_id[t]`` in ``kv``.
+
+    bf16 formats copy the row; ``KV_FP8_E4M3`` quantizes it per 128-value tile (codes plus f32
+    scales). ``flags`` is an optional device ``int32`` tensor that collects the range flags of
+    skipped rows (``TQ_DEV_*``).
+    """
+    s = kv_write_spec(src, kv, page_table, seq_id, pos, kv_format=kv_format)
+    err = _abi.TqContractError()
+    fp = ctypes.c_void_p(flags.data_ptr()) if flags is not None else None
+    raise_for(lib.tq_kv_write(ctypes.byref(s), fp, _stream_handle(stream), ctypes.byref(err)), err)
+    return kv
+
+
 def combine_parts(part_out, part_lse, out=None, lse=None, stream=None):
     """Merge ``G`` partial results (``part_out f32 [G,T,H,512]``, ``part_lse f32 [G,T,H]``)."""
     g, t, h, _ = part_out.shape

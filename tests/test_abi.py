@@ -45,6 +45,8 @@ STRUCTS = {
                                                "out_dtype"]),
     "TqWorkspaceLayout": (_abi.TqWorkspaceLayout, ["total_bytes", "part_out", "pairs"]),
     "TqContractError": (_abi.TqContractError, ["field", "kind"]),
+    "TqKvWriteSpec": (_abi.TqKvWriteSpec, ["src", "kv", "page_table", "seq_id", "pos",
+                                           "kv_format"]),
 }
 
 
