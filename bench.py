@@ -1,7 +1,8 @@
 """Benchmark of the B200 paged-MLA attention path (one JSON line on rank 0).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--config decode|decode_fp8|mtp|prefill|longctx|cpu] [--cpu-sample S]
+                    [--config decode|decode_fp8|mtp|prefill|longctx|cpu|kv_write|kv_write_fp8]
+                    [--cpu-sample S]
 
 A step is one launch of the attention path (scheduler, tcgen05 attention kernel, combine) over
 one batch of synthetic, seeded input already resident in HBM. The default workload is bf16 paged
@@ -9,7 +10,10 @@ decode: 64 sequences x 1 query token, 128 heads, 576-wide latent+RoPE rows, 512-
 cached lengths uniform in [4096, 8192], 64-row pages from a permuted pool. The pool (~0.5 GB)
 exceeds L2 (126 MB), so every step reads its rows from HBM; no L2 flush is needed.
 ``--config decode_fp8`` is the same batch with FP8 E4M3 rows (512 codes + 4 f32 scales, stored
-544 bytes apart; q 512 wide).
+544 bytes apart; q 512 wide). ``--config kv_write_fp8`` / ``kv_write`` time the KV cache writer
+instead: 128 sequences x 2048 new bf16 latent rows per step (512 wide, quantized to FP8 rows at
+stride 544; or 576 wide, copied to 1152-byte rows) scattered into a permuted page pool; the metric
+is rows written per second.
 
 With N ranks (torchrun, one GPU each) the job holds N x 64 sequences drawn from the same seeded
 stream and sharded by token count (weak scaling); there is no collective on the data path.
@@ -214,10 +218,151 @@ def cpu_baseline(name, world, budget_seqs=None, cores=None):
     }
 
 
+# ------------------------------------------------------------------------- KV writer
+
+WRITER_SEQS, WRITER_ROWS_PER_SEQ = 128, 2048
+
+
+def writer_workload(name, rank=0):
+    """Host arrays of one writer step: bf16 bits [R, W], page table, seq_id, pos (seeded)."""
+    from tq_mla import _abi
+
+    fmt = _abi.KV_FP8_E4M3 if name == "kv_write_fp8" else _abi.KV_BF16_ROPE576
+    width = 512 if fmt == _abi.KV_FP8_E4M3 else 576
+    stride = 544 if fmt == _abi.KV_FP8_E4M3 else 1152
+    rng = np.random.default_rng(1000 + rank)
+    slots = WRITER_ROWS_PER_SEQ // 64
+    pages = WRITER_SEQS * slots
+    table = rng.permutation(pages).astype(np.int32).reshape(WRITER_SEQS, slots)
+    seq_id = np.repeat(np.arange(WRITER_SEQS, dtype=np.int32), WRITER_ROWS_PER_SEQ)
+    pos = np.tile(np.arange(WRITER_ROWS_PER_SEQ, dtype=np.int32), WRITER_SEQS)
+    return fmt, width, stride, pages, table, seq_id, pos, rng
+
+
+def writer_cpu_baseline(name, rows=16384):
+    """The oracle writer (numpy quantization + scatter) on a bounded sample of the step."""
+    from oracle import kv_write as okw
+
+    fmt, width, stride, pages, table, seq_id, pos, rng = writer_workload(name)
+    x = (rng.standard_normal((rows, width))).astype(np.float32)
+    bits = (x.view(np.uint32) >> 16).astype(np.uint16)
+    pool = np.zeros((pages, 64, stride), np.uint8)
+    t0 = time.perf_counter()
+    okw.write(pool, bits, table, seq_id[:rows], pos[:rows], fmt)
+    sec = time.perf_counter() - t0
+    return {"value": rows / sec, "unit": "rows/s", "cores": 1, "kind": "port",
+            "sample": f"{rows} of the step's {len(seq_id)} rows through oracle/kv_write.py "
+                      f"(numpy, one process)", "seconds": sec}
+
+
+def run_writer(args, world, rank, local_rank):
+    import torch
+    import torch.distributed as dist
+    from tq_mla import ops
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    fmt, width, stride, pages, table, seq_id, pos, rng = writer_workload(args.config, rank)
+    rows = len(seq_id)
+    h_src = torch.randn((rows, width), generator=torch.Generator().manual_seed(7 + rank),
+                        dtype=torch.float32).to(torch.bfloat16).pin_memory()
+    src = h_src.to(dev)
+    pool = torch.zeros((pages, 64, stride), dtype=torch.uint8, device=dev)
+    d_table = torch.from_numpy(table).to(dev)
+    d_seq = torch.from_numpy(seq_id).to(dev)
+    d_pos = torch.from_numpy(pos).to(dev)
+    flags = torch.zeros(1, dtype=torch.int32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        ops.kv_write(src, pool, d_table, d_seq, d_pos, kv_format=fmt, flags=flags, stream=stream)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clock = ClockSampler(local_rank, str(ROOT / "gpurun_out" / f"clocks_rank{rank}.csv")) \
+        if (ROOT / "gpurun_out").exists() else ClockSampler(local_rank, f"/tmp/clocks{rank}.csv")
+    barrier()
+    torch.cuda.synchronize(dev)
+    with clock:
+        ev0.record(stream)
+        for _ in range(args.steps):
+            step()
+        ev1.record(stream)
+        torch.cuda.synchronize(dev)
+    barrier()
+    ms_step = max_over_ranks(ev0.elapsed_time(ev1)) / args.steps
+    # End to end: the step's rows copied in from pinned host memory, the flags read back.
+    h_flags = torch.zeros(1, dtype=torch.int32).pin_memory()
+    e2e_steps = max(3, min(args.steps, 50))
+    barrier()
+    torch.cuda.synchronize(dev)
+    ev0.record(stream)
+    for _ in range(e2e_steps):
+        src.copy_(h_src, non_blocking=True)
+        step()
+        h_flags.copy_(flags, non_blocking=True)
+    ev1.record(stream)
+    torch.cuda.synchronize(dev)
+    barrier()
+    e2e_ms = max_over_ranks(ev0.elapsed_time(ev1)) / e2e_steps
+    assert int(flags.item()) == 0, "writer flagged rows"
+    payload = 528 if stride == 544 else 1152
+    bytes_per_row = width * 2 + payload + 8  # bf16 source, payload written, seq_id + pos
+    hbm, _, _, src_name = peaks()
+    ach = rows * bytes_per_row / (ms_step * 1e-3) / 1e9
+    result = {
+        "metric": "KV rows written/s", "value": world * rows / (ms_step * 1e-3), "unit": "rows/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "bf16 -> fp8_e4m3" if stride == 544 else "bf16", "data": "synthetic",
+        "config": {"workload": f"{args.config}: {WRITER_SEQS} sequences x {WRITER_ROWS_PER_SEQ} "
+                               f"rows, width {width}, pool stride {stride}",
+                   "rows": rows, "l2": "source %.0f MB + pool %.0f MB per step, above L2; no "
+                   "flush" % (rows * width * 2 / 1e6, pages * 64 * stride / 1e6)},
+        "e2e": {"value": world * rows / (e2e_ms * 1e-3), "unit": "rows/s",
+                "h2d_bytes_per_step": rows * width * 2, "d2h_bytes_per_step": 4,
+                "ms_per_step": e2e_ms},
+        "gpu_launches": args.steps,
+        "roofline": {"bound": "hbm", "achieved": ach, "peak": hbm, "unit": "GB/s",
+                     "frac": ach / hbm, "traffic": None, "kernel": "kv_write_kernel",
+                     "peak_source": f"{src_name} (MEASURED_PEAKS.json)",
+                     "algorithmic_bytes_per_row": bytes_per_row},
+        "clocks": clock.summary(),
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        result["cpu_baseline"] = writer_cpu_baseline(args.config)
+    if rank == 0:
+        print(json.dumps(result), flush=True)
+
+
 # ------------------------------------------------------------------------- reference arm
 
 def run_reference(args, world, rank):
     if rank != 0:
+        return
+    if args.config.startswith("kv_write"):
+        base = writer_cpu_baseline(args.config)
+        line = {"impl": "reference", "metric": "KV rows written/s", "value": base["value"],
+                "unit": "rows/s", "n_gpus": world, "steps": 1, "warmup": 0,
+                "ms_per_step": 1e3 * base["seconds"], "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+                "config": {"workload": args.config}, "cpu_baseline": base,
+                "e2e": {"value": base["value"], "unit": "rows/s", "h2d_bytes_per_step": 0,
+                        "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
         return
     cores = os.cpu_count() or 1
     from tq_mla import inputs
@@ -497,7 +642,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", default="decode",
-                    choices=["decode", "decode_fp8", "mtp", "prefill", "longctx", "cpu"])
+                    choices=["decode", "decode_fp8", "mtp", "prefill", "longctx", "cpu",
+                             "kv_write", "kv_write_fp8"])
     ap.add_argument("--cpu-sample", type=int, default=None,
                     help="sequences in the CPU baseline sample (default: up to 64)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -518,7 +664,10 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
     try:
-        run_ours(args, world, rank, local_rank)
+        if args.config.startswith("kv_write"):
+            run_writer(args, world, rank, local_rank)
+        else:
+            run_ours(args, world, rank, local_rank)
     finally:
         if world > 1:
             import torch.distributed as dist

@@ -176,8 +176,9 @@ int32_t tq_mla_decode_no_alloc(const TqMlaParams* params, void* stream, TqContra
  * Row t is written to pool row page_table[seq_id[t]][pos[t] / 64] * 64 + pos[t] % 64: its bf16
  * bits as they are, or, for FP8 rows, 512 E4M3 codes and four f32 tile scales. FP8 rule per
  * 128-value tile: a NaN in the tile gives scale NaN and codes 0x7F; amax == 0 gives scale 0 and
- * codes 0; otherwise scale = amax / 448 and code = E4M3(x / scale) (f32 divisions rounded to
- * nearest even, E4M3 rounded to nearest even and saturated to +-448). Bytes past the payload are
+ * codes 0; otherwise scale = amax / 448, inv = 448 / amax and code = E4M3(x * inv), or
+ * E4M3(x / scale) when inv overflows (amax below ~1.3e-36); f32 operations rounded to nearest
+ * even, E4M3 rounded to nearest even and saturated to +-448. Bytes past the payload are
  * not touched. A row whose seq_id, pos or page entry is out of range is skipped and, when
  * `device_flags` (a device int32, may be null) is given, TQ_DEV_SEQ_RANGE, TQ_DEV_TABLE_SHORT or
  * TQ_DEV_PAGE_RANGE is OR-ed into it. Two rows naming one slot in a call race (either may win).

@@ -10,9 +10,10 @@ build defines one, per 128-value tile of a row (values widened exactly from bf16
 
 - a tile holding a NaN: scale NaN, every code 0x7F (NaN);
 - otherwise amax = max |x| (possibly +inf); amax == 0: scale 0, every code 0x00;
-- otherwise scale = f32(amax / 448) and code = E4M3(f32(x / scale)), both divisions IEEE
-  round-to-nearest-even in f32 (subnormals kept), the E4M3 conversion round-to-nearest-even with
-  saturation to +-448 (a NaN quotient, from inf / inf, gives 0x7F; a zero keeps its sign).
+- otherwise scale = f32(amax / 448), inv = f32(448 / amax) and code = E4M3(f32(x * inv)); when
+  inv overflows to +inf (amax below ~1.3e-36) the quotient is f32(x / scale) instead. All f32
+  operations round to nearest even with subnormals kept; the E4M3 conversion rounds to nearest
+  even and saturates to +-448 (a NaN quotient, from inf * 0, gives 0x7F; a zero keeps its sign).
 
 Dequantized, a code times its scale is within half an E4M3 step of x, the tile's amax maps to 448
 exactly when amax / 448 is exact, and a tile of zeros reads back as zeros.
@@ -54,7 +55,10 @@ def quantize_rows(x):
     amax = np.abs(np.where(np.isnan(t), np.float32(0), t)).max(axis=2).astype(np.float32)
     with np.errstate(divide="ignore", invalid="ignore", over="ignore", under="ignore"):
         scale = (amax / np.float32(448.0)).astype(np.float32)
-        q = (t / scale[:, :, None]).astype(np.float32)
+        inv = (np.float32(448.0) / amax).astype(np.float32)
+        q_mul = (t * inv[:, :, None]).astype(np.float32)
+        q_div = (t / scale[:, :, None]).astype(np.float32)
+        q = np.where(np.isposinf(inv)[:, :, None], q_div, q_mul).astype(np.float32)
     codes = e4m3_encode(q)
     zero = amax == 0
     codes[zero] = 0

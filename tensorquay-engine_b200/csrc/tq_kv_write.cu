@@ -10,9 +10,11 @@
 //
 // FP8 rule per tile (the reference defines none; this library's definition): a NaN in the tile
 // gives scale NaN and codes 0x7F; amax == 0 gives scale 0 and codes 0; otherwise
-// scale = amax / 448 and code = E4M3(x / scale), both divisions IEEE round-to-nearest-even in f32
-// (__fdiv_rn; no flush to zero), the conversion round-to-nearest-even with saturation
-// (cvt.rn.satfinite.e4m3x2.f32).
+// scale = amax / 448, inv = 448 / amax and code = E4M3(x * inv), or E4M3(x / scale) when inv
+// overflows (amax below ~1.3e-36). f32 operations are IEEE round-to-nearest-even with subnormals
+// kept (__fdiv_rn, __fmul_rn; no flush to zero); the conversion rounds to nearest even and
+// saturates (cvt.rn.satfinite.e4m3x2.f32). One division per lane and tile, not per value: the
+// per-value IEEE division made the writer compute-bound.
 
 #include <cuda_runtime.h>
 
@@ -51,75 +53,107 @@ __device__ __forceinline__ uint32_t e4m3x2(float lo, float hi) {
   return r;
 }
 
+// Pool row of new row t, or null (flagged) when its sequence, position or page is out of range.
+__device__ __forceinline__ uint8_t* slot_of(const Args& a, long long t, int lane) {
+  const int s = a.seq_id[t], p = a.pos[t];
+  if (s < 0 || s >= a.sequences) {
+    if (lane == 0) flag(a, TQ_DEV_SEQ_RANGE);
+    return nullptr;
+  }
+  if (p < 0 || p / kPageRows >= a.slots) {
+    if (lane == 0) flag(a, TQ_DEV_TABLE_SHORT);
+    return nullptr;
+  }
+  const int page = a.page_table[(long long)s * a.slots + p / kPageRows];
+  if (page < 0 || page >= a.pages) {
+    if (lane == 0) flag(a, TQ_DEV_PAGE_RANGE);
+    return nullptr;
+  }
+  return a.kv + ((long long)page * kPageRows + p % kPageRows) * a.row_stride;
+}
+
+// One FP8 row: this lane's 16 values (two 16-byte words of bf16) to 16 codes, plus its tile's
+// scale from the lane that starts the tile. All 32 lanes take part (shuffles).
+__device__ __forceinline__ void quantize_store(uint8_t* dst, const uint4 w0, const uint4 w1,
+                                               int lane) {
+  const uint32_t words[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+  float x[16];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    x[2 * i] = __uint_as_float(words[i] << 16);
+    x[2 * i + 1] = __uint_as_float(words[i] & 0xFFFF0000u);
+  }
+  // |x| as bf16 bit patterns order like the values, and every NaN pattern (above 0x7F80) is
+  // larger than +inf's: one packed 16-bit unsigned max gives the tile's amax and its NaN test.
+  uint32_t m = 0u;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) m = __vmaxu2(m, words[i] & 0x7FFF7FFFu);
+  // The eight lanes of a tile are aligned groups of eight: xor 1, 2, 4 stays inside one.
+#pragma unroll
+  for (int o = 1; o < 8; o <<= 1) m = __vmaxu2(m, __shfl_xor_sync(0xFFFFFFFFu, m, o));
+  const uint32_t amax_bits = max(m & 0xFFFFu, m >> 16);
+  const bool nan = amax_bits > 0x7F80u;
+  const float amax = __uint_as_float(amax_bits << 16);
+  float scale;
+  uint4 codes;
+  if (nan) {
+    scale = __uint_as_float(0x7FC00000u);
+    codes = make_uint4(0x7F7F7F7Fu, 0x7F7F7F7Fu, 0x7F7F7F7Fu, 0x7F7F7F7Fu);
+  } else if (amax == 0.f) {
+    scale = 0.f;
+    codes = make_uint4(0u, 0u, 0u, 0u);
+  } else {
+    scale = __fdiv_rn(amax, 448.f);
+    const float inv = __fdiv_rn(448.f, amax);
+    uint32_t c[8];
+    if (inv != __uint_as_float(0x7F800000u)) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        c[i] = e4m3x2(__fmul_rn(x[2 * i], inv), __fmul_rn(x[2 * i + 1], inv));
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        c[i] = e4m3x2(__fdiv_rn(x[2 * i], scale), __fdiv_rn(x[2 * i + 1], scale));
+    }
+    codes = make_uint4(c[0] | (c[1] << 16), c[2] | (c[3] << 16), c[4] | (c[5] << 16),
+                       c[6] | (c[7] << 16));
+  }
+  if (dst) {
+    reinterpret_cast<uint4*>(dst)[lane] = codes;
+    if ((lane & 7) == 0) reinterpret_cast<float*>(dst + 512)[lane >> 3] = scale;
+  }
+}
+
 template <int kFormat>
 __global__ void __launch_bounds__(32 * kRowsPerBlock) kv_write_kernel(Args a) {
   const int lane = threadIdx.x & 31;
   const long long step = (long long)gridDim.x * kRowsPerBlock;
-  for (long long t = (long long)blockIdx.x * kRowsPerBlock + (threadIdx.x >> 5); t < a.rows;
-       t += step) {
-    const int s = a.seq_id[t], p = a.pos[t];
-    if (s < 0 || s >= a.sequences) {
-      if (lane == 0) flag(a, TQ_DEV_SEQ_RANGE);
-      continue;
-    }
-    if (p < 0 || p / kPageRows >= a.slots) {
-      if (lane == 0) flag(a, TQ_DEV_TABLE_SHORT);
-      continue;
-    }
-    const int page = a.page_table[(long long)s * a.slots + p / kPageRows];
-    if (page < 0 || page >= a.pages) {
-      if (lane == 0) flag(a, TQ_DEV_PAGE_RANGE);
-      continue;
-    }
-    uint8_t* dst = a.kv + ((long long)page * kPageRows + p % kPageRows) * a.row_stride;
-    const uint8_t* src = a.src + t * a.src_stride;
-    if constexpr (kFormat != TQ_KV_FP8_E4M3) {
-      constexpr int kUnits = (kFormat == TQ_KV_BF16_ROPE576 ? 1152 : 1024) / 16;
+  const long long first = (long long)blockIdx.x * kRowsPerBlock + (threadIdx.x >> 5);
+  if constexpr (kFormat != TQ_KV_FP8_E4M3) {
+    constexpr int kUnits = (kFormat == TQ_KV_BF16_ROPE576 ? 1152 : 1024) / 16;
+    for (long long t = first; t < a.rows; t += step) {
+      uint8_t* dst = slot_of(a, t, lane);
+      if (!dst) continue;
+      const uint8_t* src = a.src + t * a.src_stride;
 #pragma unroll
       for (int i = lane; i < kUnits; i += 32)
         reinterpret_cast<uint4*>(dst)[i] = __ldg(reinterpret_cast<const uint4*>(src) + i);
-    } else {
-      const uint4 w0 = __ldg(reinterpret_cast<const uint4*>(src) + 2 * lane);
-      const uint4 w1 = __ldg(reinterpret_cast<const uint4*>(src) + 2 * lane + 1);
-      const uint32_t words[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
-      float x[16];
-      float amax = 0.f;
-      bool nan = false;
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        x[2 * i] = __uint_as_float(words[i] << 16);
-        x[2 * i + 1] = __uint_as_float(words[i] & 0xFFFF0000u);
+    }
+  } else {
+    // Two rows per warp and iteration: both rows' loads are in flight before either converts.
+    for (long long t = first; t < a.rows; t += 2 * step) {
+      const long long t2 = t + step;
+      const bool has2 = t2 < a.rows;
+      const uint4* s1 = reinterpret_cast<const uint4*>(a.src + t * a.src_stride) + 2 * lane;
+      const uint4 a0 = __ldg(s1), a1 = __ldg(s1 + 1);
+      uint4 b0 = make_uint4(0u, 0u, 0u, 0u), b1 = b0;
+      if (has2) {
+        const uint4* s2 = reinterpret_cast<const uint4*>(a.src + t2 * a.src_stride) + 2 * lane;
+        b0 = __ldg(s2);
+        b1 = __ldg(s2 + 1);
       }
-#pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        nan |= x[i] != x[i];
-        amax = fmaxf(amax, fabsf(x[i]));
-      }
-      // The eight lanes of a tile are aligned groups of eight: xor 1, 2, 4 stays inside one.
-#pragma unroll
-      for (int o = 1; o < 8; o <<= 1) {
-        amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, o));
-        nan |= __shfl_xor_sync(0xFFFFFFFFu, int(nan), o) != 0;
-      }
-      float scale;
-      uint4 codes;
-      if (nan) {
-        scale = __uint_as_float(0x7FC00000u);
-        codes = make_uint4(0x7F7F7F7Fu, 0x7F7F7F7Fu, 0x7F7F7F7Fu, 0x7F7F7F7Fu);
-      } else if (amax == 0.f) {
-        scale = 0.f;
-        codes = make_uint4(0u, 0u, 0u, 0u);
-      } else {
-        scale = __fdiv_rn(amax, 448.f);
-        uint32_t c[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i)
-          c[i] = e4m3x2(__fdiv_rn(x[2 * i], scale), __fdiv_rn(x[2 * i + 1], scale));
-        codes = make_uint4(c[0] | (c[1] << 16), c[2] | (c[3] << 16), c[4] | (c[5] << 16),
-                           c[6] | (c[7] << 16));
-      }
-      reinterpret_cast<uint4*>(dst)[lane] = codes;
-      if ((lane & 7) == 0) reinterpret_cast<float*>(dst + 512)[lane >> 3] = scale;
+      quantize_store(slot_of(a, t, lane), a0, a1, lane);
+      if (has2) quantize_store(slot_of(a, t2, lane), b0, b1, lane);
     }
   }
 }
