@@ -95,6 +95,11 @@ typedef struct {
   uint64_t tokens, heads, sequences, slots, pages, qk_width, row_stride;
   int32_t max_queries_per_sequence; /* 4 for decode plans, 0 for prefill plans */
   int32_t should_launch;            /* tokens != 0                              */
+  TqTensorSpec idx;                 /* sparse plans: i32 [T, K]; zeros otherwise */
+  TqTensorSpec k_len;               /* sparse plans: i32 [T]; zeros otherwise    */
+  uint64_t topk;                    /* K of a sparse plan, 0 otherwise            */
+  int32_t sparse;                   /* 1 for a sparse plan (tq_mla_sparse_validate) */
+  int32_t reserved;
   uint64_t digest;
 } TqMlaParams;
 
@@ -124,6 +129,8 @@ typedef struct {
   uint64_t empty_list;    /* int32[T]                                                       */
   uint64_t part_lse;      /* f32[2*pairs, 128]                                              */
   uint64_t part_out;      /* f32[2*pairs, 128 column quads, 128 rows, 4]                    */
+  uint64_t sparse_rows;   /* int32[T, K] sparse plans: each token's valid pool rows, in order */
+  uint64_t sparse_count;  /* int32[T]    sparse plans: valid entries per token               */
   int32_t pairs;          /* CTA pairs of the main kernel on this device                    */
 } TqWorkspaceLayout;
 
@@ -134,6 +141,22 @@ int32_t tq_mla_validate(const TqMlaSpec* spec, const uint8_t* query_counts, uint
 int32_t tq_mla_prefill_validate(const TqMlaSpec* spec, const uint32_t* query_counts, uint64_t n,
                                 TqMlaParams* params, TqContractError* err);
 int32_t tq_mla_should_launch(const TqMlaParams* params);
+
+/* Sparse top-k decode plan: SmlaParams::new with the DSA index tensors (contracts.rs:437-493,
+ * SmlaSpec idx / k_len at :196-200; docs/TEST-PLAN.md:190-199).
+ *   idx   i32 [T, K], K <= 2051, padded row stride allowed; -1 marks an empty entry
+ *   k_len i32 [T]
+ * Entry j of token t is valid iff j < k_len[t] and 0 <= idx[t][j] <= q_pos[t] and
+ * idx[t][j] < kv_len[seq_id[t]]; token t attends to exactly the rows of its valid entries (an
+ * entry listed twice counts twice). Invalid entries are never read. Rows are 512 wide
+ * (TQ_KV_BF16 or TQ_KV_FP8_E4M3). The plan is launched with tq_mla_decode / tq_mla_decode_no_alloc
+ * like a dense one; the launch grid does not depend on the indices, so a captured launch replays
+ * with new idx, k_len, q_pos and kv_len. A page-table entry outside the pool makes its entry
+ * invalid and sets TQ_DEV_PAGE_RANGE. */
+#define TQ_MLA_MAX_TOPK 2051
+int32_t tq_mla_sparse_validate(const TqMlaSpec* spec, const TqTensorSpec* idx,
+                               const TqTensorSpec* k_len, const uint8_t* query_counts, uint64_t n,
+                               TqMlaParams* params, TqContractError* err);
 
 /* Workspace size and layout for a validated launch on `device` (0-based CUDA ordinal). */
 int32_t tq_mla_workspace_bytes(const TqMlaParams* params, int32_t device, uint64_t* bytes);

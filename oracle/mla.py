@@ -166,6 +166,34 @@ def paged_attention(q, pool_rows, page_table, seq_id, q_pos, kv_len, *, scale, v
     return out, lse
 
 
+def sparse_entries(idx_row, k_len, q_pos, kv_len):
+    """Valid entries of one token's index row, in order (``docs/TEST-PLAN.md:199``): entry j is
+    valid iff ``j < k_len`` and ``0 <= idx[j] <= q_pos`` and ``idx[j] < kv_len``."""
+    k = max(0, min(int(k_len), len(idx_row)))
+    v = np.asarray(idx_row[:k], dtype=np.int64)
+    return v[(v >= 0) & (v <= int(q_pos)) & (v < int(kv_len))]
+
+
+def sparse_attention(q, pool_rows, page_table, seq_id, q_pos, kv_len, idx, k_len, *, scale,
+                     value_dim=512):
+    """Sparse top-k paged decode oracle in float64 (the DSA form of ``SmlaSpec``,
+    ``contracts.rs:196-200``): token ``t`` attends to the rows of its valid index entries, i.e.
+    ``mla_attention_core`` with the mask of those positions. Rows are gathered in entry order
+    (an entry listed twice would count twice; the contract's indices are unique per token)."""
+    scale = _scale(scale)
+    t_count, heads = q.shape[0], q.shape[1]
+    out = np.zeros((t_count, heads, value_dim))
+    lse = np.full((t_count, heads), -np.inf)
+    for t in range(t_count):
+        s = int(seq_id[t])
+        if s < 0 or s >= len(kv_len):
+            continue
+        v = sparse_entries(idx[t], k_len[t], q_pos[t], kv_len[s])
+        rows_idx = page_table[s][v // PAGE_ROWS].astype(np.int64) * PAGE_ROWS + v % PAGE_ROWS
+        out[t], lse[t] = identity_core(q[t], pool_rows[rows_idx], scale, value_dim)
+    return out, lse
+
+
 def combine_partials(partial_out, partial_lse):
     """Log-sum-exp merge of split results along axis 0.
 

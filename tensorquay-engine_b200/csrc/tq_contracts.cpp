@@ -168,8 +168,11 @@ uint64_t digest_of(const TqMlaParams& p) {
 }
 
 template <typename Count>
+// `idx` / `k_len` non-null: a sparse top-k plan (contracts.rs:442-470 checks them in this order:
+// the index width right after q, then idx padded and k_len packed after kv_len).
 int32_t validate_impl(const TqMlaSpec* spec, const Count* counts, uint64_t n, int max_per_seq,
-                      TqMlaParams* params, TqContractError* err) {
+                      TqMlaParams* params, TqContractError* err,
+                      const TqTensorSpec* idx = nullptr, const TqTensorSpec* k_len = nullptr) {
   Failure f{nullptr, TQ_OK};
   auto fail = [&](const char* field, int32_t kind) {
     if (err) { err->field = field; err->kind = kind; }
@@ -188,6 +191,9 @@ int32_t validate_impl(const TqMlaSpec* spec, const Count* counts, uint64_t n, in
   }
   if ((heads != 16 && heads != 32 && heads != 64 && heads != 128) || width != qk_width)
     return fail("q", TQ_SHAPE);
+  const bool sparse = idx != nullptr;
+  if (sparse && (!k_len || s.kv_format == TQ_KV_BF16_ROPE576)) return fail("kv_format", TQ_SHAPE);
+  if (sparse && (idx->rank != 2 || idx->shape[1] > TQ_MLA_MAX_TOPK)) return fail("idx", TQ_SHAPE);
   if (!scale_ok(s.kv_format, s.softmax_scale)) return fail("softmax_scale", TQ_SCALE);
   if (s.page_table.rank != 2) return fail("page_table", TQ_SHAPE);
   const uint64_t sequences = s.page_table.shape[0], slots = s.page_table.shape[1];
@@ -201,7 +207,7 @@ int32_t validate_impl(const TqMlaSpec* spec, const Count* counts, uint64_t n, in
   const uint64_t seqs[1] = {sequences};
   const uint64_t outshape[3] = {tokens, heads, 512};
   const uint64_t lseshape[2] = {tokens, heads};
-  Extent in[6], out[2];
+  Extent in[8], out[2];
   if (!check("q", s.q, query, 3, TQ_DTYPE_BF16, Layout::PaddedOuter, launching, &in[0], &f) ||
       !check("kv", s.kv, pool, 3, TQ_DTYPE_U8, Layout::Checked, launching, &in[1], &f) ||
       !check("page_table", s.page_table, table, 2, TQ_DTYPE_I32, Layout::Packed, launching,
@@ -210,6 +216,14 @@ int32_t validate_impl(const TqMlaSpec* spec, const Count* counts, uint64_t n, in
       !check("q_pos", s.q_pos, tok, 1, TQ_DTYPE_I32, Layout::Packed, launching, &in[4], &f) ||
       !check("kv_len", s.kv_len, seqs, 1, TQ_DTYPE_I32, Layout::Packed, launching, &in[5], &f))
     return fail(f.field, f.kind);
+  const uint64_t topk = sparse ? idx->shape[1] : 0;
+  if (sparse) {
+    const uint64_t idx_shape[2] = {tokens, topk};
+    if (!check("idx", *idx, idx_shape, 2, TQ_DTYPE_I32, Layout::PaddedOuter, launching, &in[6],
+               &f) ||
+        !check("k_len", *k_len, tok, 1, TQ_DTYPE_I32, Layout::Packed, launching, &in[7], &f))
+      return fail(f.field, f.kind);
+  }
   // The output may be bf16 (final) or f32 (a partial result to merge across devices).
   const int32_t out_dtype = s.out.dtype == TQ_DTYPE_F32 ? TQ_DTYPE_F32 : TQ_DTYPE_BF16;
   if (!check("out", s.out, outshape, 3, out_dtype, Layout::PaddedOuter, launching, &out[0], &f) ||
@@ -224,7 +238,7 @@ int32_t validate_impl(const TqMlaSpec* spec, const Count* counts, uint64_t n, in
     planned += c;  // n < 2^31 and c < 2^32: cannot wrap
   }
   if (planned != tokens) return fail("query_counts", TQ_QUERY_COUNT);
-  if (!check_aliases(in, 6, out, 2, &f)) return fail(f.field, f.kind);
+  if (!check_aliases(in, sparse ? 8 : 6, out, 2, &f)) return fail(f.field, f.kind);
 
   if (params) {
     std::memset(params, 0, sizeof(*params));
@@ -238,6 +252,12 @@ int32_t validate_impl(const TqMlaSpec* spec, const Count* counts, uint64_t n, in
     params->row_stride = s.kv.strides_bytes[1];
     params->max_queries_per_sequence = max_per_seq;
     params->should_launch = launching ? 1 : 0;
+    if (sparse) {
+      params->idx = *idx;
+      params->k_len = *k_len;
+      params->topk = topk;
+      params->sparse = 1;
+    }
     params->digest = digest_of(*params);
   }
   if (err) { err->field = nullptr; err->kind = TQ_OK; }
@@ -350,6 +370,16 @@ int32_t tq_mla_validate(const TqMlaSpec* spec, const uint8_t* query_counts, uint
 int32_t tq_mla_prefill_validate(const TqMlaSpec* spec, const uint32_t* query_counts, uint64_t n,
                                 TqMlaParams* params, TqContractError* err) {
   return tq::validate_impl(spec, query_counts, n, 0, params, err);
+}
+
+int32_t tq_mla_sparse_validate(const TqMlaSpec* spec, const TqTensorSpec* idx,
+                               const TqTensorSpec* k_len, const uint8_t* query_counts, uint64_t n,
+                               TqMlaParams* params, TqContractError* err) {
+  if (!idx || !k_len) {
+    if (err) { err->field = "idx"; err->kind = TQ_ERR_INVALID_ARGUMENT; }
+    return TQ_ERR_INVALID_ARGUMENT;
+  }
+  return tq::validate_impl(spec, query_counts, n, 4, params, err, idx, k_len);
 }
 
 int32_t tq_kv_write_validate(const TqKvWriteSpec* spec, TqContractError* err) {

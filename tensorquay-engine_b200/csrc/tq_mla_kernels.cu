@@ -61,6 +61,9 @@ struct Meta {
   int* empty_list;
   float* part_lse;
   float* part_out;
+  int* sparse_rows;   // sparse plans: [T, topk] valid pool rows of each token, in entry order
+  int* sparse_count;  // sparse plans: [T] valid entries (bits 0-23) and range flags (24-31)
+  long long topk;     // 0 for dense plans
 };
 
 struct MainArgs {
@@ -83,6 +86,79 @@ struct MainArgs {
   const uint8_t* kv;        // pool base (FP8 rows are read by the kernel's convert warps)
   long long kv_row_stride;  // bytes
 };
+
+// ---------------------------------------------------------------------------------------------
+// Sparse plans: each token's valid index entries (j < k_len, 0 <= idx <= q_pos, idx < kv_len;
+// docs/TEST-PLAN.md:199), in entry order, as pool rows page_table[s][idx / 64] * 64 + idx % 64.
+// One block of 256 threads per token, 256 entries at a time: a ballot per warp and a prefix over
+// the eight warps keep the order, so the result does not depend on timing. An entry whose page
+// lies outside the page table or the pool is dropped and flagged; invalid entries are never
+// used to address the pool.
+
+__global__ void __launch_bounds__(256) sparse_compact_kernel(
+    Meta m, const int* __restrict__ idx, long long idx_stride, const int* __restrict__ k_len,
+    const int* __restrict__ seq_id, const int* __restrict__ q_pos,
+    const int* __restrict__ kv_len, const int* __restrict__ page_table, long long slots,
+    long long pool_pages, int S, int T) {
+  __shared__ int warp_n[8];
+  __shared__ int block_flags;
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  for (int t = blockIdx.x; t < T; t += gridDim.x) {
+    const int s = seq_id[t];
+    int flags = 0, count = 0;
+    if (s < 0 || s >= S) {
+      flags = TQ_DEV_SEQ_RANGE;
+    } else {
+      const long long kl = min((long long)k_len[t], m.topk);
+      const int qp = q_pos[t], kvl = kv_len[s];
+      const int* row_idx = idx + (long long)t * idx_stride;
+      const int* pt = page_table + (long long)s * slots;
+      int* out = m.sparse_rows + (long long)t * m.topk;
+      for (long long j0 = 0; j0 < kl; j0 += 256) {
+        const long long j = j0 + threadIdx.x;
+        bool ok = false;
+        int row = 0;
+        if (j < kl) {
+          const int v = row_idx[j];
+          if (v >= 0 && v <= qp && v < kvl) {
+            const long long pg = v / kPageRows;
+            if (pg >= slots) {
+              flags |= TQ_DEV_TABLE_SHORT;
+            } else {
+              const int page = pt[pg];
+              if (page < 0 || page >= pool_pages) {
+                flags |= TQ_DEV_PAGE_RANGE;
+              } else {
+                ok = true;
+                row = page * kPageRows + v % kPageRows;
+              }
+            }
+          }
+        }
+        const unsigned bal = __ballot_sync(0xFFFFFFFFu, ok);
+        if (lane == 0) warp_n[w] = __popc(bal);
+        __syncthreads();
+        int before = 0, total = 0;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          before += i < w ? warp_n[i] : 0;
+          total += warp_n[i];
+        }
+        if (ok) out[count + before + __popc(bal & ((1u << lane) - 1u))] = row;
+        count += total;
+        __syncthreads();
+      }
+    }
+    // Flags of any thread reach the count word (bits 24-31).
+    flags = __reduce_or_sync(0xFFFFFFFFu, flags);
+    if (threadIdx.x == 0) block_flags = 0;
+    __syncthreads();
+    if (lane == 0 && flags) atomicOr(&block_flags, flags);
+    __syncthreads();
+    if (threadIdx.x == 0) m.sparse_count[t] = count | (block_flags << 24);
+    __syncthreads();
+  }
+}
 
 // ---------------------------------------------------------------------------------------------
 // Scheduler: one block of 1024 threads.
@@ -118,6 +194,7 @@ __global__ void __launch_bounds__(1024) schedule_kernel(Meta m, const int* __res
                                                         const int* __restrict__ kv_len, int T,
                                                         int S, long long slots, long long pool_pages,
                                                         int pairs) {
+  // Sparse plans: a token's keys are its valid index entries, counted by sparse_compact_kernel.
   __shared__ long long sh[32];
   __shared__ int s_err;
   ptx::grid_launch_dependents();  // the attention kernel may start its prologue meanwhile
@@ -134,7 +211,11 @@ __global__ void __launch_bounds__(1024) schedule_kernel(Meta m, const int* __res
   for (int u = lo; u < hi; ++u) {
     const int s = seq_id[u];
     long long n = 0;
-    if (s < 0 || s >= S) {
+    if (m.sparse_count) {
+      const int v = m.sparse_count[u];
+      n = v & 0xFFFFFF;
+      if (v >> 24) atomicOr(&s_err, v >> 24);
+    } else if (s < 0 || s >= S) {
       atomicOr(&s_err, TQ_DEV_SEQ_RANGE);
     } else {
       long long kl = kv_len[s];
@@ -311,16 +392,21 @@ struct Waiter {
 // ---------------------------------------------------------------------------------------------
 // Main kernel.
 
-// kFp8: FP8 E4M3 rows (512 codes, then 4 f32 scales, one per 128 values; no RoPE part). Four
-// more warps (6-9) read each page's rows with plain loads, dequantize them to bf16 and write the
-// same shared-memory operand layout the TMA gives bf16 rows, zeros past the cached length; the
-// MMA and softmax warps are unchanged.
-template <bool kRope, bool kFp8 = false>
-__global__ void __launch_bounds__(kFp8 ? kThreadsFp8 : kThreads, 1)
+// kFp8: FP8 E4M3 rows (512 codes, then 4 f32 scales, one per 128 values; no RoPE part).
+// kSparse: a token's keys are its valid top-k index entries (the compacted pool rows of
+// sparse_compact_kernel), 64 per page, instead of its sequence's positions.
+// Either way four more warps (6-9) gather each page's rows and write the shared-memory operand
+// layout the TMA gives dense bf16 rows, zeros past the token's keys: FP8 rows with plain loads
+// and dequantization to bf16, sparse bf16 rows with cp.async. The MMA and softmax warps are
+// unchanged.
+template <bool kRope, bool kFp8 = false, bool kSparse = false>
+__global__ void __launch_bounds__((kFp8 || kSparse) ? kThreadsFp8 : kThreads, 1)
     mla_paged_kernel(const __grid_constant__ CUtensorMap tm_q,
                      const __grid_constant__ CUtensorMap tm_kv,
                      const __grid_constant__ CUtensorMap tm_v, const MainArgs a) {
   static_assert(!(kRope && kFp8), "FP8 rows carry no RoPE part");
+  static_assert(!(kRope && kSparse), "sparse plans use 512-wide rows");
+  constexpr bool kGather = kFp8 || kSparse;  // convert warps fill the pages' ring slots
   constexpr int kQkChunks = kRope ? 9 : 8;               // 64-dim chunks of the query width
   constexpr int kQSmemChunks = kQkChunks - kQTmemDims / 64;
   constexpr uint32_t kStageLoadBytes = (kQkChunks + 4) * kKvChunkBytes;
@@ -341,9 +427,9 @@ __global__ void __launch_bounds__(kFp8 ? kThreadsFp8 : kThreads, 1)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
-      // FP8: a page's stage is complete when the four convert warps have arrived; a query
+      // FP8 / sparse: a page's stage is complete when the four convert warps have arrived; a query
       // slot's TMA arrives once with its bytes plus three plain arrivals.
-      ptx::mbar_init(bar(kBarKvFull + s), kFp8 ? kConvertWarps : 1);
+      ptx::mbar_init(bar(kBarKvFull + s), kGather ? kConvertWarps : 1);
       ptx::mbar_init(bar(kBarKvEmpty + s), 1);
       ptx::mbar_init(bar(kBarKvGrant + s), 1);
     }
@@ -413,9 +499,9 @@ __global__ void __launch_bounds__(kFp8 ? kThreadsFp8 : kThreads, 1)
         // Page-table entries are read three pages ahead of their loads: a dependent global read
         // at load time would add its latency to every page's arrival.
         const int* pt = a.page_table + (long long)sq * a.slots;
-        int pf0 = s.np > 0 ? pt[s.p0] : 0;
-        int pf1 = s.np > 1 ? pt[s.p0 + 1] : 0;
-        int pf2 = s.np > 2 ? pt[s.p0 + 2] : 0;
+        int pf0 = (!kGather && s.np > 0) ? pt[s.p0] : 0;
+        int pf1 = (!kGather && s.np > 1) ? pt[s.p0 + 1] : 0;
+        int pf2 = (!kGather && s.np > 2) ? pt[s.p0 + 2] : 0;
         // Query dims [0, 384) pass through two ring slots, three 64-dim chunks each, on their way
         // to TMEM (tcgen05.cp by the MMA warp). The query boxes are 128 rows high: rows past the
         // head count lie outside the tensor and arrive as zeros.
@@ -428,7 +514,7 @@ __global__ void __launch_bounds__(kFp8 ? kThreadsFp8 : kThreads, 1)
           }
           const uint32_t fb = bar(kBarKvFull + stage);
           ptx::mbar_expect_tx(fb, 3 * kQChunkBytes);
-          if constexpr (kFp8) {
+          if constexpr (kGather) {
             for (int k = 1; k < kConvertWarps; ++k) ptx::mbar_arrive(fb);
           }
           for (int k = 0; k < 3; ++k)
@@ -443,7 +529,7 @@ __global__ void __launch_bounds__(kFp8 ? kThreadsFp8 : kThreads, 1)
           ptx::tma_load_3d(base + kSmQ + k * kQChunkBytes, &tm_q, bar(kBarQSmemFull),
                            kQTmemDims + 64 * k, 0, s.u);
         ++useq;
-        // FP8: the convert warps fill the pages' stages; this loop waits for each page's slot
+        // FP8 / sparse: the convert warps fill the pages' stages; this loop waits for each page's slot
         // to be free and grants it to them. This thread is the only waiter on kBarKvEmpty and
         // waits on every slot in ring order: a parity wait tells completions apart only modulo
         // 2, so a waiter that skipped slots could pass two phases early or block one phase late.
@@ -454,13 +540,13 @@ __global__ void __launch_bounds__(kFp8 ? kThreadsFp8 : kThreads, 1)
           const int page = pf0;
           pf0 = pf1;
           pf1 = pf2;
-          pf2 = (!kFp8 && j + 3 < s.np) ? pt[s.p0 + j + 3] : 0;
+          pf2 = (!kGather && j + 3 < s.np) ? pt[s.p0 + j + 3] : 0;
           wt.where = (1 << 24) | int(it & 0xFFFFFF);
           if (!wt.wait<false>(bar(kBarKvEmpty + stage), ((it / kStages) & 1u) ^ 1u)) {
             ok = false;
             break;
           }
-          if constexpr (kFp8) {
+          if constexpr (kGather) {
             ptx::mbar_arrive(bar(kBarKvGrant + stage));
             continue;
           }
@@ -519,8 +605,8 @@ __global__ void __launch_bounds__(kFp8 ? kThreadsFp8 : kThreads, 1)
       const int valid = min(kPageRows, n - p * kPageRows);
       const int own_valid = max(0, min(kKeysPerCta, valid - key0));
       const int peer_valid = max(0, min(kKeysPerCta, valid - (kKeysPerCta - key0)));
-      // FP8: the convert warps already wrote zeros past the cached length.
-      if (!kFp8 && (own_valid < kKeysPerCta || peer_valid < kKeysPerCta)) {
+      // FP8 / sparse: the convert warps already wrote zeros past the token's keys.
+      if (!kGather && (own_valid < kKeysPerCta || peer_valid < kKeysPerCta)) {
         uint8_t* st_ptr = sm + kSmKv + stage * kStageBytes;
         const int own_words = (kKeysPerCta - own_valid) * 8;
         const int peer_words = (kKeysPerCta - peer_valid) * 8;
@@ -654,15 +740,18 @@ __global__ void __launch_bounds__(kFp8 ? kThreadsFp8 : kThreads, 1)
     __syncwarp();
     wt.drain(bar(kBarDrain), 0);
   } else if (warp >= 6) {
-    // ------------------------------------------------------------------ FP8 convert warps
+    // ------------------------------------------------------------------ convert warps
     // Warp cw handles this CTA's keys key0 + 8 cw + [0, 8) across all 512 dims (lane: dims
-    // [16 lane, 16 lane + 16), one 16-byte load of codes) and the peer's keys
-    // (32 - key0) + 8 cw + [0, 8) across this CTA's 256 value dims (two keys per load, 16 lanes
-    // each). All loads of a page are in flight together; each 16-byte group of codes becomes two
-    // bf16 16-byte units written at their 128B-swizzled places (unit u of row r at u ^ (r % 8)).
-    // Keys past the cached length (and pages outside the pool) are written as zeros and their
-    // rows are never read.
-    if constexpr (kFp8) {
+    // [16 lane, 16 lane + 16)) and the peer's keys (32 - key0) + 8 cw + [0, 8) across this CTA's
+    // 256 value dims (two keys per instruction, 16 lanes each). Each lane's 16 dims are two bf16
+    // 16-byte units, written at their 128B-swizzled places (unit u of row r at u ^ (r % 8)).
+    // Keys past the token's count (and rows of pages outside the pool) are written as zeros and
+    // their rows are never read. A page's pool rows: page_table[seq][p] * 64 + key (dense), or
+    // the token's compacted valid entries p * 64 + key (sparse).
+    // FP8 rows: all loads of a page are in flight together (registers), then each 16-byte group
+    // of codes is dequantized (code x tile scale, rounded once to bf16) and stored. Sparse bf16
+    // rows: cp.async copies straight into the stage after the grant, zero-filled past the count.
+    if constexpr (kGather) {
       const int cw = warp - 6, hl = lane & 15;
       uint32_t it = 0;
       uint32_t grant_parity = 0;  // bit s: parity of the next grant phase of stage s
@@ -670,70 +759,126 @@ __global__ void __launch_bounds__(kFp8 ? kThreadsFp8 : kThreads, 1)
       bool ok = true;
       while (ok && walker.next(meta, s)) {
         const int n = meta.unit_n[s.u];
-        const int* pt = a.page_table + (long long)a.seq_id[s.u] * a.slots;
+        const int* pt = kSparse ? nullptr : a.page_table + (long long)a.seq_id[s.u] * a.slots;
+        const int* srows = kSparse ? meta.sparse_rows + (long long)s.u * meta.topk : nullptr;
         it += 2;  // the segment's two query slots, filled by the TMA producer
         for (int j = 0; j < s.np; ++j, ++it) {
           const uint32_t stage = it % kStages;
-          const int page = pt[s.p0 + j];
-          const int valid = min(kPageRows, n - (s.p0 + j) * kPageRows);
-          const long long row0 = (long long)page * kPageRows;
-          const bool page_ok = page >= 0 && row0 < a.pool_rows;
-          if (!page_ok && cw == 0 && lane == 0) atomicOr(a.meta.header + kHdrError, TQ_DEV_PAGE_RANGE);
-          uint4 own[8], pr[4];
-          float own_sc[8], pr_sc[4];
-#pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            const int key = key0 + 8 * cw + i;
-            own[i] = make_uint4(0, 0, 0, 0);
-            own_sc[i] = 0.f;
-            if (page_ok && key < valid) {
-              const uint8_t* rp = a.kv + (row0 + key) * a.kv_row_stride;
-              own[i] = __ldg(reinterpret_cast<const uint4*>(rp) + lane);
-              own_sc[i] = __ldg(reinterpret_cast<const float*>(rp + kFp8RowCodes) + (lane >> 3));
-            }
+          const int p = s.p0 + j;
+          const int valid = min(kPageRows, n - p * kPageRows);
+          long long row0 = 0;
+          bool page_ok = true;
+          if constexpr (!kSparse) {
+            const int page = pt[p];
+            row0 = (long long)page * kPageRows;
+            page_ok = page >= 0 && row0 < a.pool_rows;
+            if (!page_ok && cw == 0 && lane == 0)
+              atomicOr(a.meta.header + kHdrError, TQ_DEV_PAGE_RANGE);
           }
-#pragma unroll
-          for (int p = 0; p < 4; ++p) {
-            const int key = (kKeysPerCta - key0) + 8 * cw + 2 * p + (lane >> 4);
-            pr[p] = make_uint4(0, 0, 0, 0);
-            pr_sc[p] = 0.f;
-            if (page_ok && key < valid) {
-              const uint8_t* rp = a.kv + (row0 + key) * a.kv_row_stride;
-              pr[p] = __ldg(reinterpret_cast<const uint4*>(rp + vdim0) + hl);
-              pr_sc[p] = __ldg(reinterpret_cast<const float*>(rp + kFp8RowCodes) +
-                               ((vdim0 + 16 * hl) >> 7));
-            }
-          }
-          wt.where = (7 << 24) | int(it & 0xFFFFFF);
-          const bool got = wt.wait<false>(bar(kBarKvGrant + stage), (grant_parity >> stage) & 1u);
-          if (!__all_sync(0xFFFFFFFFu, got)) { ok = false; break; }
-          grant_parity ^= 1u << stage;
-          uint8_t* st_ptr = sm + kSmKv + stage * kStageBytes;
-          auto put16 = [&](uint8_t* rowp, int u0, int r8, const uint4& c, float sc) {
-            uint4 lo, hi;
-            lo.x = ptx::e4m3x2_scaled_bf16x2(c.x, sc);
-            lo.y = ptx::e4m3x2_scaled_bf16x2(c.x >> 16, sc);
-            lo.z = ptx::e4m3x2_scaled_bf16x2(c.y, sc);
-            lo.w = ptx::e4m3x2_scaled_bf16x2(c.y >> 16, sc);
-            hi.x = ptx::e4m3x2_scaled_bf16x2(c.z, sc);
-            hi.y = ptx::e4m3x2_scaled_bf16x2(c.z >> 16, sc);
-            hi.z = ptx::e4m3x2_scaled_bf16x2(c.w, sc);
-            hi.w = ptx::e4m3x2_scaled_bf16x2(c.w >> 16, sc);
-            *reinterpret_cast<uint4*>(rowp + ((u0 ^ r8) << 4)) = lo;
-            *reinterpret_cast<uint4*>(rowp + (((u0 + 1) ^ r8) << 4)) = hi;
+          // Pool row of key k < valid of this page.
+          auto row_of = [&](int k) -> long long {
+            if constexpr (kSparse) return (long long)srows[p * kPageRows + k];
+            else return row0 + k;
           };
+          if constexpr (kFp8) {
+            uint4 own[8], pr[4];
+            float own_sc[8], pr_sc[4];
 #pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            const int r = 8 * cw + i;
-            put16(st_ptr + (r >> 3) * kOwnGroupBytes + (lane >> 2) * kAtomBytes + (r & 7) * 128,
-                  2 * (lane & 3), r & 7, own[i], own_sc[i]);
-          }
+            for (int i = 0; i < 8; ++i) {
+              const int key = key0 + 8 * cw + i;
+              own[i] = make_uint4(0, 0, 0, 0);
+              own_sc[i] = 0.f;
+              if (page_ok && key < valid) {
+                const uint8_t* rp = a.kv + row_of(key) * a.kv_row_stride;
+                own[i] = __ldg(reinterpret_cast<const uint4*>(rp) + lane);
+                own_sc[i] = __ldg(reinterpret_cast<const float*>(rp + kFp8RowCodes) + (lane >> 3));
+              }
+            }
 #pragma unroll
-          for (int p = 0; p < 4; ++p) {
-            const int r = 8 * cw + 2 * p + (lane >> 4);
-            put16(st_ptr + kPvxOffset + (r >> 3) * kPeerGroupBytes + (hl >> 2) * kAtomBytes +
-                      (r & 7) * 128,
-                  2 * (hl & 3), r & 7, pr[p], pr_sc[p]);
+            for (int q = 0; q < 4; ++q) {
+              const int key = (kKeysPerCta - key0) + 8 * cw + 2 * q + (lane >> 4);
+              pr[q] = make_uint4(0, 0, 0, 0);
+              pr_sc[q] = 0.f;
+              if (page_ok && key < valid) {
+                const uint8_t* rp = a.kv + row_of(key) * a.kv_row_stride;
+                pr[q] = __ldg(reinterpret_cast<const uint4*>(rp + vdim0) + hl);
+                pr_sc[q] = __ldg(reinterpret_cast<const float*>(rp + kFp8RowCodes) +
+                                 ((vdim0 + 16 * hl) >> 7));
+              }
+            }
+            wt.where = (7 << 24) | int(it & 0xFFFFFF);
+            const bool got =
+                wt.wait<false>(bar(kBarKvGrant + stage), (grant_parity >> stage) & 1u);
+            if (!__all_sync(0xFFFFFFFFu, got)) { ok = false; break; }
+            grant_parity ^= 1u << stage;
+            uint8_t* st_ptr = sm + kSmKv + stage * kStageBytes;
+            auto put16 = [&](uint8_t* rowp, int u0, int r8, const uint4& c, float sc) {
+              uint4 lo, hi;
+              lo.x = ptx::e4m3x2_scaled_bf16x2(c.x, sc);
+              lo.y = ptx::e4m3x2_scaled_bf16x2(c.x >> 16, sc);
+              lo.z = ptx::e4m3x2_scaled_bf16x2(c.y, sc);
+              lo.w = ptx::e4m3x2_scaled_bf16x2(c.y >> 16, sc);
+              hi.x = ptx::e4m3x2_scaled_bf16x2(c.z, sc);
+              hi.y = ptx::e4m3x2_scaled_bf16x2(c.z >> 16, sc);
+              hi.z = ptx::e4m3x2_scaled_bf16x2(c.w, sc);
+              hi.w = ptx::e4m3x2_scaled_bf16x2(c.w >> 16, sc);
+              *reinterpret_cast<uint4*>(rowp + ((u0 ^ r8) << 4)) = lo;
+              *reinterpret_cast<uint4*>(rowp + (((u0 + 1) ^ r8) << 4)) = hi;
+            };
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              const int r = 8 * cw + i;
+              put16(st_ptr + (r >> 3) * kOwnGroupBytes + (lane >> 2) * kAtomBytes + (r & 7) * 128,
+                    2 * (lane & 3), r & 7, own[i], own_sc[i]);
+            }
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              const int r = 8 * cw + 2 * q + (lane >> 4);
+              put16(st_ptr + kPvxOffset + (r >> 3) * kPeerGroupBytes + (hl >> 2) * kAtomBytes +
+                        (r & 7) * 128,
+                    2 * (hl & 3), r & 7, pr[q], pr_sc[q]);
+            }
+          } else {
+            // Sparse bf16 rows: row numbers read before the grant, copies issued after it.
+            long long own_row[8], pr_row[4];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              const int key = key0 + 8 * cw + i;
+              own_row[i] = key < valid ? row_of(key) : -1;
+            }
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              const int key = (kKeysPerCta - key0) + 8 * cw + 2 * q + (lane >> 4);
+              pr_row[q] = key < valid ? row_of(key) : -1;
+            }
+            wt.where = (7 << 24) | int(it & 0xFFFFFF);
+            const bool got =
+                wt.wait<false>(bar(kBarKvGrant + stage), (grant_parity >> stage) & 1u);
+            if (!__all_sync(0xFFFFFFFFu, got)) { ok = false; break; }
+            grant_parity ^= 1u << stage;
+            const uint32_t st_base = base + kSmKv + stage * kStageBytes;
+            // Two 16-byte units (dims [8 u0, 8 u0 + 16) of the chunk) of one row; a row of -1
+            // is written as zeros without a read.
+            auto copy2 = [&](uint32_t rowp, int u0, int r8, long long row, int byte0) {
+              const uint8_t* src = a.kv + (row < 0 ? 0 : row * a.kv_row_stride + byte0);
+              const uint32_t nbytes = row < 0 ? 0u : 16u;
+              ptx::cp_async_16(rowp + ((u0 ^ r8) << 4), src, nbytes);
+              ptx::cp_async_16(rowp + (((u0 + 1) ^ r8) << 4), src + (row < 0 ? 0 : 16), nbytes);
+            };
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              const int r = 8 * cw + i;
+              copy2(st_base + (r >> 3) * kOwnGroupBytes + (lane >> 2) * kAtomBytes + (r & 7) * 128,
+                    2 * (lane & 3), r & 7, own_row[i], 32 * lane);
+            }
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              const int r = 8 * cw + 2 * q + (lane >> 4);
+              copy2(st_base + kPvxOffset + (r >> 3) * kPeerGroupBytes + (hl >> 2) * kAtomBytes +
+                        (r & 7) * 128,
+                    2 * (hl & 3), r & 7, pr_row[q], 2 * vdim0 + 32 * hl);
+            }
+            ptx::cp_async_wait_all();
           }
           ptx::fence_proxy_async_smem();  // the MMAs read the stage through the async proxy
           __syncwarp();
@@ -1214,9 +1359,9 @@ bool encode_bf16(CUtensorMap* map, const void* addr, int rank, const cuuint64_t*
             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <bool kRope, bool kFp8 = false>
+template <bool kRope, bool kFp8 = false, bool kSparse = false>
 cudaError_t prepare_kernel() {
-  return cudaFuncSetAttribute(mla_paged_kernel<kRope, kFp8>,
+  return cudaFuncSetAttribute(mla_paged_kernel<kRope, kFp8, kSparse>,
                               cudaFuncAttributeMaxDynamicSharedMemorySize, int(kSmBytes));
 }
 
@@ -1234,7 +1379,9 @@ int pairs_for_device(int device) {
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
   int clusters = 0;
   if (prepare_kernel<true>() == cudaSuccess && prepare_kernel<false>() == cudaSuccess &&
-      prepare_kernel<false, true>() == cudaSuccess) {
+      prepare_kernel<false, true>() == cudaSuccess &&
+      prepare_kernel<false, false, true>() == cudaSuccess &&
+      prepare_kernel<false, true, true>() == cudaSuccess) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * (sms / 2), 1, 1);
     cfg.blockDim = dim3(kThreads, 1, 1);
@@ -1258,7 +1405,7 @@ int pairs_for_device(int device) {
 
 uint64_t align256(uint64_t x) { return (x + 255) & ~uint64_t(255); }
 
-void layout_for(uint64_t tokens, int pairs, TqWorkspaceLayout* L) {
+void layout_for(uint64_t tokens, int pairs, bool sparse, uint64_t topk, TqWorkspaceLayout* L) {
   uint64_t o = 0;
   auto take = [&](uint64_t bytes) {
     const uint64_t at = o;
@@ -1278,6 +1425,10 @@ void layout_for(uint64_t tokens, int pairs, TqWorkspaceLayout* L) {
   L->empty_list = take(tokens * 4);
   L->part_lse = take(uint64_t(2 * pairs) * kHeadsTile * 4);
   L->part_out = take(uint64_t(2 * pairs) * kHeadsTile * kValueDim * 4);
+  if (sparse) {  // offsets never 0 (the header comes first), so 0 means "dense plan"
+    L->sparse_rows = take(tokens * topk * 4);
+    L->sparse_count = take(tokens * 4);
+  }
   L->total_bytes = o;
   L->pairs = pairs;
 }
@@ -1296,6 +1447,9 @@ Meta meta_at(char* ws, const TqWorkspaceLayout& L) {
   m.empty_list = reinterpret_cast<int*>(ws + L.empty_list);
   m.part_lse = reinterpret_cast<float*>(ws + L.part_lse);
   m.part_out = reinterpret_cast<float*>(ws + L.part_out);
+  m.sparse_rows = L.sparse_rows ? reinterpret_cast<int*>(ws + L.sparse_rows) : nullptr;
+  m.sparse_count = L.sparse_count ? reinterpret_cast<int*>(ws + L.sparse_count) : nullptr;
+  m.topk = 0;
   return m;
 }
 
@@ -1320,12 +1474,13 @@ int32_t launch(const TqMlaParams* params, void* workspace, uint64_t workspace_by
   const TqMlaSpec& s = params->spec;
   const bool rope = s.kv_format == TQ_KV_BF16_ROPE576;
   const bool fp8 = s.kv_format == TQ_KV_FP8_E4M3;
+  const bool sparse = params->sparse != 0;
   int device = 0;
   if (cudaGetDevice(&device) != cudaSuccess) return set_err(err, "device", TQ_ERR_CUDA);
   const int pairs = pairs_for_device(device);
   if (pairs <= 0) return set_err(err, "device", TQ_ERR_CUDA);
   TqWorkspaceLayout L;
-  layout_for(params->tokens, pairs, &L);
+  layout_for(params->tokens, pairs, params->sparse != 0, params->topk, &L);
   if (!workspace || (reinterpret_cast<uintptr_t>(workspace) & 255) ||
       workspace_bytes < L.total_bytes)
     return set_err(err, "workspace", TQ_ERR_WORKSPACE);
@@ -1346,6 +1501,19 @@ int32_t launch(const TqMlaParams* params, void* workspace, uint64_t workspace_by
   char* ws = static_cast<char*>(workspace);
   Meta m = meta_at(ws, L);
   const int T = int(params->tokens), H = int(params->heads), S = int(params->sequences);
+  if (sparse) {
+    m.topk = (long long)params->topk;
+    const int blocks = T < 8 * pairs ? T : 8 * pairs;
+    sparse_compact_kernel<<<blocks, 256, 0, st>>>(
+        m, reinterpret_cast<const int*>(params->idx.device_address),
+        (long long)(params->idx.strides_bytes[0] / 4),
+        reinterpret_cast<const int*>(params->k_len.device_address),
+        reinterpret_cast<const int*>(s.seq_id.device_address),
+        reinterpret_cast<const int*>(s.q_pos.device_address),
+        reinterpret_cast<const int*>(s.kv_len.device_address),
+        reinterpret_cast<const int*>(s.page_table.device_address), (long long)params->slots,
+        (long long)params->pages, S, T);
+  }
 
   schedule_kernel<<<1, 1024, 0, st>>>(m, reinterpret_cast<const int*>(s.seq_id.device_address),
                                       reinterpret_cast<const int*>(s.q_pos.device_address),
@@ -1369,8 +1537,8 @@ int32_t launch(const TqMlaParams* params, void* workspace, uint64_t workspace_by
     const void* ka = reinterpret_cast<const void*>(s.kv.device_address);
     if (!encode_bf16(&tq_map, qa, 3, qdims, qstr, qbox, CU_TENSOR_MAP_SWIZZLE_128B))
       return set_err(err, "tensor_map", TQ_ERR_CUDA);
-    if (fp8) {
-      tkv = tq_map;  // FP8 rows are read with plain loads: the KV maps are not used
+    if (fp8 || sparse) {
+      tkv = tq_map;  // the convert warps gather the rows: the KV maps are not used
       tv = tq_map;
     } else if (!encode_bf16(&tkv, ka, 4, kdims, kstr, kbox, CU_TENSOR_MAP_SWIZZLE_128B) ||
                !encode_bf16(&tv, ka, 4, kdims, kstr, vbox, CU_TENSOR_MAP_SWIZZLE_128B)) {
@@ -1398,7 +1566,7 @@ int32_t launch(const TqMlaParams* params, void* workspace, uint64_t workspace_by
 
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * pairs, 1, 1);
-    cfg.blockDim = dim3(fp8 ? kThreadsFp8 : kThreads, 1, 1);
+    cfg.blockDim = dim3((fp8 || sparse) ? kThreadsFp8 : kThreads, 1, 1);
     cfg.dynamicSmemBytes = kSmBytes;
     cfg.stream = st;
     cudaLaunchAttribute attr[2];
@@ -1412,10 +1580,17 @@ int32_t launch(const TqMlaParams* params, void* workspace, uint64_t workspace_by
     cfg.numAttrs = 2;
     if (t_timer_begin && cudaEventRecord(t_timer_begin, st) != cudaSuccess)
       return set_err(err, "timer", TQ_ERR_CUDA);
-    cudaError_t e =
-        rope  ? cudaLaunchKernelEx(&cfg, mla_paged_kernel<true>, tq_map, tkv, tv, a)
-        : fp8 ? cudaLaunchKernelEx(&cfg, mla_paged_kernel<false, true>, tq_map, tkv, tv, a)
-              : cudaLaunchKernelEx(&cfg, mla_paged_kernel<false>, tq_map, tkv, tv, a);
+    cudaError_t e;
+    if (rope)
+      e = cudaLaunchKernelEx(&cfg, mla_paged_kernel<true>, tq_map, tkv, tv, a);
+    else if (sparse && fp8)
+      e = cudaLaunchKernelEx(&cfg, mla_paged_kernel<false, true, true>, tq_map, tkv, tv, a);
+    else if (sparse)
+      e = cudaLaunchKernelEx(&cfg, mla_paged_kernel<false, false, true>, tq_map, tkv, tv, a);
+    else if (fp8)
+      e = cudaLaunchKernelEx(&cfg, mla_paged_kernel<false, true>, tq_map, tkv, tv, a);
+    else
+      e = cudaLaunchKernelEx(&cfg, mla_paged_kernel<false>, tq_map, tkv, tv, a);
     if (e != cudaSuccess) return set_err(err, "launch", TQ_ERR_CUDA);
     if (t_timer_end && cudaEventRecord(t_timer_end, st) != cudaSuccess)
       return set_err(err, "timer", TQ_ERR_CUDA);
@@ -1479,7 +1654,7 @@ int32_t tq_mla_workspace_layout(const TqMlaParams* params, int32_t device,
   if (!tq::params_intact(params)) return TQ_ERR_PARAMS;
   const int pairs = pairs_for_device(device);
   if (pairs <= 0) return TQ_ERR_CUDA;
-  layout_for(params->tokens, pairs, layout);
+  layout_for(params->tokens, pairs, params->sparse != 0, params->topk, layout);
   return TQ_OK;
 }
 
@@ -1508,7 +1683,7 @@ int32_t tq_mla_decode_no_alloc(const TqMlaParams* params, void* stream, TqContra
   const int pairs = pairs_for_device(device);
   if (pairs <= 0) return set_err(err, "device", TQ_ERR_CUDA);
   TqWorkspaceLayout L;
-  layout_for(params->tokens, pairs, &L);
+  layout_for(params->tokens, pairs, params->sparse != 0, params->topk, &L);
   if (L.total_bytes > TQ_MLA_NO_ALLOC_WORKSPACE_BYTES)
     return set_err(err, "no_alloc_workspace", TQ_ERR_WORKSPACE);
   void* ws = no_alloc_workspace(device);

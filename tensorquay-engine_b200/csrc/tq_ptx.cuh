@@ -365,6 +365,16 @@ __device__ __forceinline__ uint32_t e4m3x2_scaled_bf16x2(uint32_t codes, float s
   return pack_bf16x2(lo * scale, hi * scale);
 }
 
+// 16-byte global -> shared copy that completes asynchronously; src_bytes 0 writes zeros and
+// reads nothing (the source address is then not dereferenced).
+__device__ __forceinline__ void cp_async_16(uint32_t dst, const void* src, uint32_t src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src),
+               "r"(src_bytes)
+               : "memory");
+}
+// Waits for every cp.async this thread issued.
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
 __device__ __forceinline__ float bf16_lo(uint32_t v) { return __uint_as_float(v << 16); }
 __device__ __forceinline__ float bf16_hi(uint32_t v) { return __uint_as_float(v & 0xFFFF0000u); }
 

@@ -56,6 +56,8 @@ class TqMlaParams(ctypes.Structure):
         ("row_stride", ctypes.c_uint64),
         ("max_queries_per_sequence", ctypes.c_int32),
         ("should_launch", ctypes.c_int32),
+        ("idx", TqTensorSpec), ("k_len", TqTensorSpec),
+        ("topk", ctypes.c_uint64), ("sparse", ctypes.c_int32), ("reserved", ctypes.c_int32),
         ("digest", ctypes.c_uint64),
     ]
 
@@ -74,7 +76,7 @@ class TqWorkspaceLayout(ctypes.Structure):
     _fields_ = [(name, ctypes.c_uint64) for name in (
         "total_bytes", "header", "unit_n", "unit_pages", "unit_gstart", "unit_first",
         "unit_nsplit", "unit_split_off", "pair_begin", "combine_list", "empty_list", "part_lse",
-        "part_out")] + [("pairs", ctypes.c_int32)]
+        "part_out", "sparse_rows", "sparse_count")] + [("pairs", ctypes.c_int32)]
 
 
 class TqKvWriteSpec(ctypes.Structure):
@@ -91,6 +93,9 @@ PROTOTYPES = {
     "tq_mla_prefill_validate": (_I32, [_P(TqMlaSpec), _P(ctypes.c_uint32), _U64,
                                        _P(TqMlaParams), _P(TqContractError)]),
     "tq_mla_should_launch": (_I32, [_P(TqMlaParams)]),
+    "tq_mla_sparse_validate": (_I32, [_P(TqMlaSpec), _P(TqTensorSpec), _P(TqTensorSpec),
+                                      _P(ctypes.c_uint8), _U64, _P(TqMlaParams),
+                                      _P(TqContractError)]),
     "tq_mla_workspace_bytes": (_I32, [_P(TqMlaParams), _I32, _P(_U64)]),
     "tq_mla_workspace_layout": (_I32, [_P(TqMlaParams), _I32, _P(TqWorkspaceLayout)]),
     "tq_mla_decode": (_I32, [_P(TqMlaParams), _VP, _U64, _VP, _P(TqContractError)]),

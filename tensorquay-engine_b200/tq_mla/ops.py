@@ -78,11 +78,23 @@ def make_spec(q, kv, page_table, seq_id, q_pos, kv_len, out, lse, *, scale, kv_f
     return s
 
 
-def validate(spec, query_counts, *, prefill=False):
-    """Validate ``spec`` against the host plan; returns ``TqMlaParams`` or raises."""
+def validate(spec, query_counts, *, prefill=False, idx=None, k_len=None):
+    """Validate ``spec`` against the host plan; returns ``TqMlaParams`` or raises.
+
+    With ``idx`` / ``k_len`` (tensor declarations, ``TqTensorSpec``) the plan is a sparse top-k
+    decode plan (``tq_mla_sparse_validate``).
+    """
     params = _abi.TqMlaParams()
     err = _abi.TqContractError()
     counts = list(int(c) for c in query_counts)
+    if idx is not None:
+        if any(c < 0 or c > 255 for c in counts):
+            raise ContractError("query_counts", 9)
+        arr = (ctypes.c_uint8 * max(1, len(counts)))(*counts)
+        st = lib.tq_mla_sparse_validate(ctypes.byref(spec), ctypes.byref(idx), ctypes.byref(k_len),
+                                        arr, len(counts), ctypes.byref(params), ctypes.byref(err))
+        raise_for(st, err)
+        return params
     if prefill:
         arr = (ctypes.c_uint32 * max(1, len(counts)))(*counts)
         st = lib.tq_mla_prefill_validate(ctypes.byref(spec), arr, len(counts),
@@ -125,12 +137,18 @@ class MlaLaunch:
     """
 
     def __init__(self, q, kv, page_table, seq_id, q_pos, kv_len, out, lse, *, scale,
-                 query_counts, prefill=False, kv_format=None, workspace=None):
-        self.tensors = (q, kv, page_table, seq_id, q_pos, kv_len, out, lse)
+                 query_counts, prefill=False, kv_format=None, workspace=None, idx=None,
+                 k_len=None):
+        self.tensors = (q, kv, page_table, seq_id, q_pos, kv_len, out, lse, idx, k_len)
         self.spec = make_spec(q, kv, page_table, seq_id, q_pos, kv_len, out, lse, scale=scale,
                               kv_format=kv_format)
         self.prefill = prefill
-        self.params = validate(self.spec, query_counts, prefill=prefill)
+        if (idx is None) != (k_len is None):
+            raise ValueError("a sparse plan needs both idx and k_len")
+        sparse = None if idx is None else (spec_of(idx), spec_of(k_len))
+        self.params = validate(self.spec, query_counts, prefill=prefill,
+                               idx=sparse[0] if sparse else None,
+                               k_len=sparse[1] if sparse else None)
         self.out, self.lse = out, lse
         need = workspace_bytes(self.params, q.device.index) if self.params.should_launch else 0
         if workspace is None:
@@ -166,11 +184,14 @@ def set_kernel_timer(begin=None, end=None):
 
 
 def mla_decode(q, kv, page_table, seq_id, q_pos, kv_len, *, scale, query_counts=None, out=None,
-               lse=None, out_dtype=torch.bfloat16, prefill=False, kv_format=None, stream=None):
-    """Dense paged absorbed-MLA attention: returns ``(out [T,H,512], lse [T,H])``.
+               lse=None, out_dtype=torch.bfloat16, prefill=False, kv_format=None, stream=None,
+               idx=None, k_len=None):
+    """Paged absorbed-MLA attention: returns ``(out [T,H,512], lse [T,H])``.
 
-    Token ``t`` attends to positions ``[0, min(kv_len[seq_id[t]], q_pos[t] + 1))`` of its
-    sequence, whose rows live in ``kv`` pages listed by ``page_table[seq_id[t]]``.
+    Dense: token ``t`` attends to positions ``[0, min(kv_len[seq_id[t]], q_pos[t] + 1))`` of its
+    sequence, whose rows live in ``kv`` pages listed by ``page_table[seq_id[t]]``. Sparse (``idx``
+    i32 ``[T, K]`` and ``k_len`` i32 ``[T]`` given): token ``t`` attends to the positions
+    ``idx[t, j]`` with ``j < k_len[t]``, ``0 <= idx <= q_pos[t]`` and ``idx < kv_len``.
     """
     t, h = q.shape[0], q.shape[1]
     if out is None:
@@ -180,7 +201,8 @@ def mla_decode(q, kv, page_table, seq_id, q_pos, kv_len, *, scale, query_counts=
     if query_counts is None:
         query_counts = torch.bincount(seq_id.cpu().long(), minlength=page_table.shape[0]).tolist()
     launch = MlaLaunch(q, kv, page_table, seq_id, q_pos, kv_len, out, lse, scale=scale,
-                       query_counts=query_counts, prefill=prefill, kv_format=kv_format)
+                       query_counts=query_counts, prefill=prefill, kv_format=kv_format, idx=idx,
+                       k_len=k_len)
     return launch(stream)
 
 

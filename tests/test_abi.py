@@ -40,10 +40,12 @@ STRUCTS = {
     "TqMlaSpec": (_abi.TqMlaSpec, ["q", "kv", "page_table", "seq_id", "q_pos", "kv_len", "out",
                                    "lse", "kv_format", "softmax_scale"]),
     "TqMlaParams": (_abi.TqMlaParams, ["spec", "tokens", "heads", "row_stride",
-                                       "max_queries_per_sequence", "should_launch", "digest"]),
+                                       "max_queries_per_sequence", "should_launch", "idx",
+                                       "k_len", "topk", "sparse", "digest"]),
     "TqCombineParams": (_abi.TqCombineParams, ["parts", "part_out", "out_stride_head",
                                                "out_dtype"]),
-    "TqWorkspaceLayout": (_abi.TqWorkspaceLayout, ["total_bytes", "part_out", "pairs"]),
+    "TqWorkspaceLayout": (_abi.TqWorkspaceLayout, ["total_bytes", "part_out", "sparse_rows",
+                                                   "sparse_count", "pairs"]),
     "TqContractError": (_abi.TqContractError, ["field", "kind"]),
     "TqKvWriteSpec": (_abi.TqKvWriteSpec, ["src", "kv", "page_table", "seq_id", "pos",
                                            "kv_format"]),
