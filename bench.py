@@ -1,7 +1,8 @@
 """Benchmark of the B200 paged-MLA attention path (one JSON line on rank 0).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--config decode|decode_fp8|mtp|prefill|longctx|cpu|kv_write|kv_write_fp8]
+                    [--config decode|decode_fp8|mtp|prefill|longctx|cpu|kv_write|kv_write_fp8|
+                              sparse|sparse_fp8]
                     [--cpu-sample S]
 
 A step is one launch of the attention path (scheduler, tcgen05 attention kernel, combine) over
@@ -13,7 +14,10 @@ exceeds L2 (126 MB), so every step reads its rows from HBM; no L2 flush is neede
 544 bytes apart; q 512 wide). ``--config kv_write_fp8`` / ``kv_write`` time the KV cache writer
 instead: 128 sequences x 2048 new bf16 latent rows per step (512 wide, quantized to FP8 rows at
 stride 544; or 576 wide, copied to 1152-byte rows) scattered into a permuted page pool; the metric
-is rows written per second.
+is rows written per second. ``--config sparse`` / ``sparse_fp8`` time sparse top-k decode: 64
+sequences x 1 token, 32 heads, 32K cached positions, 2051 index entries per token of which 2048
+are valid, bf16 or FP8 rows; four index sets rotate between steps so the rows read are not
+L2-resident.
 
 With N ranks (torchrun, one GPU each) the job holds N x 64 sequences drawn from the same seeded
 stream and sharded by token count (weak scaling); there is no collective on the data path.
@@ -62,7 +66,7 @@ def workload_for(name, world, rank):
     if world == 1:
         return inputs.config(name)
     base = {"decode": 64, "decode_fp8": 64, "mtp": 512, "prefill": 8, "longctx": 4,
-            "cpu": 4}[name]
+            "cpu": 4, "sparse": 64, "sparse_fp8": 64}[name]
     if name in ("cpu",):
         return inputs.config(name)
     full = inputs.config(name, batch=base * world)
@@ -348,10 +352,194 @@ def run_writer(args, world, rank, local_rank):
         print(json.dumps(result), flush=True)
 
 
+# ------------------------------------------------------------------------- sparse top-k
+
+SPARSE_K, SPARSE_VALID, SPARSE_SETS = 2051, 2048, 4
+
+
+def sparse_indices(w, set_id):
+    """Index set ``set_id`` of a sparse workload: per token 2048 unique random positions in
+    [0, q_pos], then three -1 entries, all in one shuffled row of 2051."""
+    rng = np.random.default_rng(7000 + 31 * set_id + int(w.seed))
+    seq, q_pos = w.seq_id(), w.q_pos()
+    idx = np.full((w.tokens, SPARSE_K), -1, np.int32)
+    for t in range(w.tokens):
+        vis = int(min(w.kv_len[seq[t]], q_pos[t] + 1))
+        sel = rng.choice(vis, size=min(vis, SPARSE_VALID), replace=False).astype(np.int32)
+        row = np.concatenate([sel, np.full(SPARSE_K - len(sel), -1, np.int32)])
+        rng.shuffle(row)
+        idx[t] = row
+    return idx, np.full(w.tokens, SPARSE_K, np.int32)
+
+
+def sparse_cpu_baseline(name, tokens=8):
+    """The oracle (float64 sparse gather + attention) on a bounded sample of tokens."""
+    from oracle import generate as ogen, mla as omla
+    from oracle import fp8 as ofp8
+    from tq_mla import inputs
+
+    w = inputs.config(name)
+    idx, k_len = sparse_indices(w, 0)
+    rng = np.random.default_rng(3)
+    t0 = time.perf_counter()
+    for t in range(tokens):
+        q = rng.standard_normal((1, w.heads, 512))
+        if w.extra.get("kv_format") == "fp8_e4m3":
+            raw = np.zeros((SPARSE_VALID, 544), np.uint8)
+            raw[:, :512] = rng.integers(0, 0x7E, size=(SPARSE_VALID, 512), dtype=np.uint8)
+            raw[:, 512:528] = np.full((SPARSE_VALID, 4), 0.01, np.float32).view(np.uint8)
+            rows = ofp8.dequant_rows(raw)
+        else:
+            rows = rng.standard_normal((SPARSE_VALID, 512))
+        v = omla.sparse_entries(idx[t], k_len[t], w.q_pos()[t], w.kv_len[w.seq_id()[t]])
+        omla.identity_core(q[0], rows[: len(v)], w.scale, 512)
+    sec = time.perf_counter() - t0
+    return {"value": tokens / sec, "unit": UNIT, "cores": 1, "kind": "port",
+            "sample": f"{tokens} of {w.tokens} query tokens of {w.name}: float64 entry "
+                      f"validation, row gather{_fp8_note(w)} and attention (oracle/mla.py), one "
+                      f"process", "seconds": sec}
+
+
+def run_sparse(args, world, rank, local_rank):
+    import torch
+    import torch.distributed as dist
+    from tq_mla import inputs, ops
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    w = workload_for(args.config, world, rank)
+    batch = inputs.materialize(w, dev)
+    fmt = kv_format_of(w)
+    out = torch.empty((w.tokens, w.heads, 512), dtype=torch.bfloat16, device=dev)
+    lse = torch.empty((w.tokens, w.heads), dtype=torch.float32, device=dev)
+    sets = [sparse_indices(w, i) for i in range(SPARSE_SETS)]
+    d_sets = [(torch.from_numpy(i).to(dev), torch.from_numpy(k).to(dev)) for i, k in sets]
+    launches = [ops.MlaLaunch(batch.q, batch.kv, batch.page_table, batch.seq_id, batch.q_pos,
+                              batch.kv_len, out, lse, scale=w.scale,
+                              query_counts=batch.query_counts, kv_format=fmt, idx=i, k_len=k)
+                for i, k in d_sets]
+    stream = torch.cuda.current_stream(dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    for i in range(max(args.warmup, SPARSE_SETS)):
+        launches[i % SPARSE_SETS](stream)
+    torch.cuda.synchronize(dev)
+    assert all(l.device_error() == 0 for l in launches)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clock = ClockSampler(local_rank, str(ROOT / "gpurun_out" / f"clocks_rank{rank}.csv")) \
+        if (ROOT / "gpurun_out").exists() else ClockSampler(local_rank, f"/tmp/clocks{rank}.csv")
+    barrier()
+    torch.cuda.synchronize(dev)
+    with clock:
+        ev0.record(stream)
+        for i in range(args.steps):
+            launches[i % SPARSE_SETS](stream)
+        ev1.record(stream)
+        torch.cuda.synchronize(dev)
+    barrier()
+    ms_step = max_over_ranks(ev0.elapsed_time(ev1)) / args.steps
+    # The attention kernel alone (events around it; a second pass, as for dense decode).
+    k_steps = min(args.steps, 300)
+    kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(k_steps)]
+    for b_, e_ in kev:
+        b_.record(stream)
+        e_.record(stream)
+    torch.cuda.synchronize(dev)
+    for i, (b_, e_) in enumerate(kev):
+        ops.set_kernel_timer(b_, e_)
+        launches[i % SPARSE_SETS](stream)
+    torch.cuda.synchronize(dev)
+    ops.set_kernel_timer()
+    kernel_ms = sum(b_.elapsed_time(e_) for b_, e_ in kev) / k_steps
+    # End to end: q and the step's indices copied in from pinned memory, out and lse copied back.
+    h_q = batch.q.cpu().pin_memory()
+    h_sets = [(torch.from_numpy(i).pin_memory(), torch.from_numpy(k).pin_memory()) for i, k in sets]
+    h_out = torch.empty_like(out, device="cpu").pin_memory()
+    h_lse = torch.empty_like(lse, device="cpu").pin_memory()
+    e2e_steps = max(SPARSE_SETS, min(args.steps, 200))
+    barrier()
+    torch.cuda.synchronize(dev)
+    ev0.record(stream)
+    for i in range(e2e_steps):
+        j = i % SPARSE_SETS
+        batch.q.copy_(h_q, non_blocking=True)
+        d_sets[j][0].copy_(h_sets[j][0], non_blocking=True)
+        d_sets[j][1].copy_(h_sets[j][1], non_blocking=True)
+        launches[j](stream)
+        h_out.copy_(out, non_blocking=True)
+        h_lse.copy_(lse, non_blocking=True)
+    ev1.record(stream)
+    torch.cuda.synchronize(dev)
+    barrier()
+    e2e_ms = max_over_ranks(ev0.elapsed_time(ev1)) / e2e_steps
+    assert all(l.device_error() == 0 for l in launches)
+    row_bytes = 528 if fmt is not None else 1024
+    valid = sum(int(min(SPARSE_VALID, k)) for k in w.kv_len[w.seq_id()])
+    bytes_step = (valid * row_bytes + w.tokens * w.heads * 512 * 2 + w.tokens * SPARSE_K * 4
+                  + w.tokens * 4 + w.tokens * w.heads * (512 * 2 + 4))
+    flops_step = 2.0 * valid * w.heads * (512 + 512)
+    hbm, tc_burst, _, src = peaks()
+    ach_gbs = bytes_step / (kernel_ms * 1e-3) / 1e9
+    tokens_all = w.tokens * world
+    h2d = h_q.numel() * 2 + h_sets[0][0].numel() * 4 + h_sets[0][1].numel() * 4
+    d2h = h_out.numel() * 2 + h_lse.numel() * 4
+    result = {
+        "metric": "MLA sparse top-k decode tokens/s", "value": tokens_all / (ms_step * 1e-3),
+        "unit": UNIT, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "fp8_e4m3 rows, bf16 operands" if fmt is not None else "bf16",
+        "data": "synthetic",
+        "config": {"workload": w.name if world == 1 else f"{w.name} x{world} ranks",
+                   "query_tokens": tokens_all, "heads": w.heads, "topk_entries": SPARSE_K,
+                   "valid_entries_per_token": SPARSE_VALID,
+                   "l2": f"{SPARSE_SETS} index sets rotate: %.0f MB of rows per step, %.0f MB "
+                         "across the sets (L2 126 MB)" % (valid * row_bytes / 1e6,
+                                                          SPARSE_SETS * valid * row_bytes / 1e6)},
+        "e2e": {"value": tokens_all / (e2e_ms * 1e-3), "unit": UNIT,
+                "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
+                "ms_per_step": e2e_ms},
+        "gpu_launches": (LAUNCHES_PER_STEP + 1) * args.steps,
+        "roofline": {"bound": "hbm", "achieved": ach_gbs, "peak": hbm, "unit": "GB/s",
+                     "frac": ach_gbs / hbm, "traffic": None, "kernel": "mla_paged_kernel",
+                     "kernel_ms_per_launch": kernel_ms,
+                     "peak_source": f"{src} (MEASURED_PEAKS.json)",
+                     "algorithmic_bytes_per_launch": bytes_step, "flops_per_launch": flops_step,
+                     "tflops": flops_step / (kernel_ms * 1e-3) / 1e12,
+                     "step_frac": bytes_step / (ms_step * 1e-3) / 1e9 / hbm},
+        "clocks": clock.summary(),
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        result["cpu_baseline"] = sparse_cpu_baseline(args.config)
+    if rank == 0:
+        print(json.dumps(result), flush=True)
+
+
 # ------------------------------------------------------------------------- reference arm
 
 def run_reference(args, world, rank):
     if rank != 0:
+        return
+    if args.config.startswith("sparse"):
+        base = sparse_cpu_baseline(args.config, tokens=16)
+        line = {"impl": "reference", "metric": "MLA sparse top-k decode tokens/s",
+                "value": base["value"], "unit": UNIT, "n_gpus": world, "steps": 1, "warmup": 0,
+                "ms_per_step": 1e3 * base["seconds"], "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
+                "config": {"workload": args.config}, "cpu_baseline": base,
+                "e2e": {"value": base["value"], "unit": UNIT, "h2d_bytes_per_step": 0,
+                        "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
         return
     if args.config.startswith("kv_write"):
         base = writer_cpu_baseline(args.config)
@@ -643,7 +831,7 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", default="decode",
                     choices=["decode", "decode_fp8", "mtp", "prefill", "longctx", "cpu",
-                             "kv_write", "kv_write_fp8"])
+                             "kv_write", "kv_write_fp8", "sparse", "sparse_fp8"])
     ap.add_argument("--cpu-sample", type=int, default=None,
                     help="sequences in the CPU baseline sample (default: up to 64)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -666,6 +854,8 @@ def main():
     try:
         if args.config.startswith("kv_write"):
             run_writer(args, world, rank, local_rank)
+        elif args.config.startswith("sparse"):
+            run_sparse(args, world, rank, local_rank)
         else:
             run_ours(args, world, rank, local_rank)
     finally:

@@ -146,6 +146,18 @@ def config(name, *, batch=None):
         kv = np.array([17, 64, 200, 1000], dtype=np.int64)
         w = Workload("cpu_decode_h16", 0, 16, 576, kv, np.ones(4, np.int64), kv - 1, scale)
         return _finish(w, pool_pages=64)
+    if name in ("sparse", "sparse_fp8"):
+        # Sparse top-k decode in the reference's SMLA-P-001 shape: sequences x 1 token, 32 heads,
+        # 32K cached positions each, bf16 (1024-byte) or FP8 (528 of 544 bytes) rows; the top-k
+        # index sets are drawn by the bench (2048 valid of 2051 entries per token).
+        b = 64 if batch is None else batch
+        kv = np.full(b, 32768, dtype=np.int64)
+        w = Workload(f"{name}_b{b}_h32_ctx32k_k2048", 1, 32, 512, kv, np.ones(b, np.int64),
+                     kv - 1, 0.0625)
+        if name == "sparse_fp8":
+            w.extra["kv_format"] = "fp8_e4m3"
+            w.extra["kv_row_bytes"] = FP8_ROW_PAYLOAD
+        return _finish(w)
     if name == "decode_fp8":
         # The decode batch with FP8 E4M3 rows (512 codes + 4 f32 scales; no RoPE part, q width
         # 512, the format's fixed scale 1/16).
