@@ -90,10 +90,14 @@ struct MainArgs {
 // ---------------------------------------------------------------------------------------------
 // Sparse plans: each token's valid index entries (j < k_len, 0 <= idx <= q_pos, idx < kv_len;
 // docs/TEST-PLAN.md:199), in entry order, as pool rows page_table[s][idx / 64] * 64 + idx % 64.
-// One block of 256 threads per token, 256 entries at a time: a ballot per warp and a prefix over
-// the eight warps keep the order, so the result does not depend on timing. An entry whose page
-// lies outside the page table or the pool is dropped and flagged; invalid entries are never
-// used to address the pool.
+// One block of 256 threads per token; thread i owns entries [9 i, 9 i + 9) (256 x 9 >= 2051), so
+// all its index and page-table loads are in flight together, and one exclusive scan of the
+// per-thread counts places every valid entry at its rank: the order does not depend on timing.
+// An entry whose page lies outside the page table or the pool is dropped and flagged; invalid
+// entries are never used to address the pool.
+
+constexpr int kCompactPerThread = 9;
+static_assert(TQ_MLA_MAX_TOPK <= 256 * kCompactPerThread, "index row exceeds one block's reach");
 
 __global__ void __launch_bounds__(256) sparse_compact_kernel(
     Meta m, const int* __restrict__ idx, long long idx_stride, const int* __restrict__ k_len,
@@ -104,8 +108,10 @@ __global__ void __launch_bounds__(256) sparse_compact_kernel(
   __shared__ int block_flags;
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
   for (int t = blockIdx.x; t < T; t += gridDim.x) {
+    if (threadIdx.x == 0) block_flags = 0;
     const int s = seq_id[t];
-    int flags = 0, count = 0;
+    int flags = 0, mine = 0;
+    int rows[kCompactPerThread];
     if (s < 0 || s >= S) {
       flags = TQ_DEV_SEQ_RANGE;
     } else {
@@ -113,50 +119,52 @@ __global__ void __launch_bounds__(256) sparse_compact_kernel(
       const int qp = q_pos[t], kvl = kv_len[s];
       const int* row_idx = idx + (long long)t * idx_stride;
       const int* pt = page_table + (long long)s * slots;
-      int* out = m.sparse_rows + (long long)t * m.topk;
-      for (long long j0 = 0; j0 < kl; j0 += 256) {
-        const long long j = j0 + threadIdx.x;
-        bool ok = false;
-        int row = 0;
-        if (j < kl) {
-          const int v = row_idx[j];
-          if (v >= 0 && v <= qp && v < kvl) {
-            const long long pg = v / kPageRows;
-            if (pg >= slots) {
-              flags |= TQ_DEV_TABLE_SHORT;
-            } else {
-              const int page = pt[pg];
-              if (page < 0 || page >= pool_pages) {
-                flags |= TQ_DEV_PAGE_RANGE;
-              } else {
-                ok = true;
-                row = page * kPageRows + v % kPageRows;
-              }
-            }
+      const long long j0 = (long long)threadIdx.x * kCompactPerThread;
+      int v[kCompactPerThread];
+#pragma unroll
+      for (int i = 0; i < kCompactPerThread; ++i) v[i] = j0 + i < kl ? row_idx[j0 + i] : -1;
+#pragma unroll
+      for (int i = 0; i < kCompactPerThread; ++i) {
+        rows[i] = -1;
+        if (v[i] >= 0 && v[i] <= qp && v[i] < kvl) {
+          const long long pg = v[i] / kPageRows;
+          if (pg >= slots) {
+            flags |= TQ_DEV_TABLE_SHORT;
+          } else {
+            const int page = pt[pg];
+            if (page < 0 || page >= pool_pages) flags |= TQ_DEV_PAGE_RANGE;
+            else rows[i] = page * kPageRows + v[i] % kPageRows;
           }
         }
-        const unsigned bal = __ballot_sync(0xFFFFFFFFu, ok);
-        if (lane == 0) warp_n[w] = __popc(bal);
-        __syncthreads();
-        int before = 0, total = 0;
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          before += i < w ? warp_n[i] : 0;
-          total += warp_n[i];
-        }
-        if (ok) out[count + before + __popc(bal & ((1u << lane) - 1u))] = row;
-        count += total;
-        __syncthreads();
+        mine += rows[i] >= 0;
       }
     }
-    // Flags of any thread reach the count word (bits 24-31).
+    // Exclusive scan of the per-thread counts (entry order = thread order, then i).
+    int incl = mine;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+      if (lane >= o) incl += y;
+    }
+    if (lane == 31) warp_n[w] = incl;
     flags = __reduce_or_sync(0xFFFFFFFFu, flags);
-    if (threadIdx.x == 0) block_flags = 0;
     __syncthreads();
     if (lane == 0 && flags) atomicOr(&block_flags, flags);
+    int before = incl - mine, total = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      before += i < w ? warp_n[i] : 0;
+      total += warp_n[i];
+    }
+    if (mine) {
+      int* out = m.sparse_rows + (long long)t * m.topk + before;
+#pragma unroll
+      for (int i = 0; i < kCompactPerThread; ++i)
+        if (rows[i] >= 0) *out++ = rows[i];
+    }
     __syncthreads();
-    if (threadIdx.x == 0) m.sparse_count[t] = count | (block_flags << 24);
-    __syncthreads();
+    if (threadIdx.x == 0) m.sparse_count[t] = total | (block_flags << 24);
+    __syncthreads();  // warp_n and block_flags are reused by the next token
   }
 }
 
