@@ -13,7 +13,12 @@ It writes, under ``tests/golden/``:
     the upstream SDPA output;
   - ``paged_cases.npz``: paged bf16 cases whose inputs come from the seeded generator and whose
     expected ``out``/``lse`` come from the reference's own ``mla_attention_core``, imported from
-    the checkout and called with identity key absorption and ``[I_512 | 0]`` value projection.
+    the checkout and called with identity key absorption and ``[I_512 | 0]`` value projection;
+  - ``sparse_cases.npz``: sparse top-k cases on the same kind of seeded inputs, with index rows
+    drawn here (stored in the file) that mix valid entries with -1, positions past q_pos or
+    kv_len, extreme values and stale padding after k_len; the expected ``out``/``lse`` come
+    from ``mla_attention_core`` with the mask of each token's valid positions
+    (``docs/TEST-PLAN.md:199``).
 Nothing at test time reads the reference checkout; the tests read only these files.
 """
 
@@ -140,9 +145,84 @@ def paged_cases(ref: Path):
     np.savez_compressed(HERE / "paged_cases.npz", **out)
 
 
+SPARSE_CASES = {
+    # name: (seed, heads, kv_len list, queries per sequence, K)
+    "sparse_h32": (6, 32, [700, 64, 1500, 3000], [1, 2, 1, 3], 300),
+    "sparse_k2051": (8, 32, [1, 65, 2047], [1, 1, 4], 2051),
+}
+
+
+def sparse_cases(ref: Path):
+    sys.path.insert(0, str(ref / "reference/src"))
+    from tq_reference import mla_attention
+
+    out = {}
+    for name, (seed, heads, lens, per, k) in SPARSE_CASES.items():
+        width, scale = 512, 0.0625
+        lens = np.array(lens, dtype=np.int64)
+        per = np.array(per, dtype=np.int64)
+        table, pool_pages = generate.page_tables(seed, lens, None)
+        pool_bits = generate.kv_pool(seed, lens, table, pool_pages, width)
+        tokens = int(per.sum())
+        q_bits = generate.queries(seed, tokens, heads, width)
+        seq_id = np.repeat(np.arange(len(lens)), per).astype(np.int32)
+        q_pos = np.concatenate([lens[b] - per[b] + np.arange(per[b])
+                                for b in range(len(lens))]).astype(np.int32)
+        rng = np.random.default_rng(seed)
+        idx = np.full((tokens, k), -1, np.int32)
+        k_len = np.zeros(tokens, np.int32)
+        masks = []
+        for t in range(tokens):
+            kl_seq = int(lens[seq_id[t]])
+            vis = min(kl_seq, int(q_pos[t]) + 1)
+            n = min(vis, k - 6)
+            sel = rng.choice(vis, size=n, replace=False)
+            junk = [-1, int(q_pos[t]) + 1, kl_seq, 2 ** 31 - 1, -2, -2 ** 31]
+            row = np.concatenate([sel, junk]).astype(np.int64)
+            rng.shuffle(row)
+            kl = min(k, len(row))
+            idx[t, :kl] = row[:kl]
+            k_len[t] = kl
+            idx[t, kl:] = rng.integers(0, max(1, vis), size=k - kl)  # stale padding
+            v = idx[t, : k_len[t]].astype(np.int64)
+            v = v[(v >= 0) & (v <= q_pos[t]) & (v < kl_seq)]
+            m = np.zeros(kl_seq, dtype=bool)
+            m[v] = True
+            masks.append(m)
+        rows = generate.bf16_to_f64(pool_bits)
+        q = generate.bf16_to_f64(q_bits)
+        w_uk = np.broadcast_to(np.eye(width), (heads, width, width)).copy()
+        w_uv = np.broadcast_to(np.eye(512, width), (heads, 512, width)).copy()
+        exp_out = np.zeros((tokens, heads, 512))
+        exp_lse = np.zeros((tokens, heads))
+        for t in range(tokens):
+            b = int(seq_id[t])
+            pos = np.arange(lens[b])
+            latent = rows[table[b, pos // 64].astype(np.int64) * 64 + pos % 64]
+            res = mla_attention.mla_attention_core(q[t : t + 1], latent, w_uk, w_uv,
+                                                   masks[t][None, :], scale=scale)
+            exp_out[t] = res.out[0]
+            exp_lse[t] = res.lse[0]
+        out[f"{name}__meta"] = np.array([seed, heads, width, pool_pages])
+        out[f"{name}__kv_len"] = lens
+        out[f"{name}__per_seq"] = per
+        out[f"{name}__page_table"] = table
+        out[f"{name}__seq_id"] = seq_id
+        out[f"{name}__q_pos"] = q_pos
+        out[f"{name}__idx"] = idx
+        out[f"{name}__k_len"] = k_len
+        out[f"{name}__scale"] = np.array(scale)
+        out[f"{name}__q_sha256"] = np.array(hashlib.sha256(q_bits.tobytes()).hexdigest())
+        out[f"{name}__pool_sha256"] = np.array(hashlib.sha256(pool_bits.tobytes()).hexdigest())
+        out[f"{name}__out"] = exp_out
+        out[f"{name}__lse"] = exp_lse
+    np.savez_compressed(HERE / "sparse_cases.npz", **out)
+
+
 if __name__ == "__main__":
     reference = Path(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
     copy_philox(reference)
     upstream_cases(reference)
     paged_cases(reference)
+    sparse_cases(reference)
     print("golden fixtures written to", HERE)

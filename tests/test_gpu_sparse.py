@@ -260,3 +260,26 @@ def test_graph_replay_with_new_indices_is_exact_and_deterministic(cuda_device):
             graph.replay()
         torch.cuda.synchronize()
         assert torch.equal(out, first[0]) and torch.equal(lse, first[1])
+
+
+@pytest.mark.parametrize("name", ["sparse_h32", "sparse_k2051"])
+def test_sparse_golden_cases_from_reference(cuda_device, name):
+    """The kernel on the seeded inputs of tests/golden/sparse_cases.npz against the reference's
+    mla_attention_core run with each token's valid-position mask."""
+    from conftest import GOLDEN
+
+    g = np.load(GOLDEN / "sparse_cases.npz")
+    seed, heads, width, pool_pages = (int(x) for x in g[f"{name}__meta"])
+    w = gh.workload(seed, heads, g[f"{name}__kv_len"], per_seq=g[f"{name}__per_seq"],
+                    width=width, pool_pages=pool_pages, scale=float(g[f"{name}__scale"]))
+    np.testing.assert_array_equal(w.extra["page_table"], g[f"{name}__page_table"])
+    b = inputs.materialize(w, cuda_device)
+    q_ok, pool_ok = gh.oracle_inputs_match(b, w)
+    assert q_ok and pool_ok, "device generator differs from the oracle generator"
+    np.testing.assert_array_equal(w.q_pos(), g[f"{name}__q_pos"])
+    launch, out, lse, _, _ = _launch(b, w, g[f"{name}__idx"], g[f"{name}__k_len"], cuda_device)
+    launch()
+    torch.cuda.synchronize()
+    assert launch.device_error() == 0
+    assert_parity(_np(out), lse.double().cpu().numpy(), g[f"{name}__out"], g[f"{name}__lse"],
+                  label=name)

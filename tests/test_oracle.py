@@ -194,3 +194,25 @@ def test_planted_mistake_in_the_oracle_is_caught():
     assert_parity(good[0], good[1], g[f"{name}__out"], g[f"{name}__lse"])
     with pytest.raises(AssertionError):
         assert_parity(bad[0], bad[1], g[f"{name}__out"], g[f"{name}__lse"])
+
+
+@pytest.mark.parametrize("name", ["sparse_h32", "sparse_k2051"])
+def test_sparse_oracle_matches_reference_core_with_the_valid_mask(name):
+    """The sparse oracle against ``mla_attention_core`` run by the reference on the same seeded
+    inputs with each token's valid-position mask (tests/golden/sparse_cases.npz)."""
+    g = np.load(GOLDEN / "sparse_cases.npz")
+    seed, heads, width, pool_pages = (int(x) for x in g[f"{name}__meta"])
+    lens = g[f"{name}__kv_len"]
+    table, pp = ogen.page_tables(seed, lens, pool_pages)
+    np.testing.assert_array_equal(table, g[f"{name}__page_table"])
+    pool = ogen.kv_pool(seed, lens, table, pp, width)
+    tokens = int(g[f"{name}__per_seq"].sum())
+    q = ogen.queries(seed, tokens, heads, width)
+    assert hashlib.sha256(pool.tobytes()).hexdigest() == str(g[f"{name}__pool_sha256"])
+    assert hashlib.sha256(q.tobytes()).hexdigest() == str(g[f"{name}__q_sha256"])
+    out, lse = omla.sparse_attention(ogen.bf16_to_f64(q), ogen.bf16_to_f64(pool), table,
+                                     g[f"{name}__seq_id"], g[f"{name}__q_pos"], lens,
+                                     g[f"{name}__idx"], g[f"{name}__k_len"],
+                                     scale=float(g[f"{name}__scale"]))
+    np.testing.assert_allclose(out, g[f"{name}__out"], rtol=0, atol=1e-12)
+    np.testing.assert_allclose(lse, g[f"{name}__lse"], rtol=0, atol=1e-12)
