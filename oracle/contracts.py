@@ -188,13 +188,27 @@ def _scale_ok(spec):
     return bool(np.isfinite(f32)) and float(f32) > 0
 
 
-def validate(spec: Spec, query_counts, max_per_seq=MAX_DECODE_QUERIES):
-    """Raise ``ContractError`` for the first violation; return ``should_launch`` otherwise."""
+MAX_INDICES = 2051  # contracts.rs:28
+
+
+def validate(spec: Spec, query_counts, max_per_seq=MAX_DECODE_QUERIES, idx=None, k_len=None):
+    """Raise ``ContractError`` for the first violation; return ``should_launch`` otherwise.
+
+    With ``idx`` / ``k_len`` (``Tensor``) the plan is a sparse top-k plan: the index width is
+    checked right after q (``contracts.rs:442-445``), idx as a padded ``[T, K]`` i32 tensor and
+    k_len as a packed ``[T]`` one after kv_len (``:469-470``), and both are alias-check inputs.
+    Sparse plans take the 512-wide formats of the reference (``KvFormat``, ``:127-144``).
+    """
     tokens, heads, width = spec.q.shape
+    sparse = idx is not None
     if spec.kv_format not in PAYLOAD:
         _fail("kv_format", SHAPE)
     if heads not in HEADS or width != QK_WIDTH[spec.kv_format]:
         _fail("q", SHAPE)
+    if sparse and (k_len is None or spec.kv_format == KV_BF16_ROPE576):
+        _fail("kv_format", SHAPE)
+    if sparse and (len(idx.shape) != 2 or idx.shape[1] > MAX_INDICES):
+        _fail("idx", SHAPE)
     if not _scale_ok(spec):
         _fail("softmax_scale", SCALE)
     sequences, slots = spec.page_table.shape
@@ -211,6 +225,11 @@ def validate(spec: Spec, query_counts, max_per_seq=MAX_DECODE_QUERIES):
         _check("q_pos", spec.q_pos, [tokens], I32, "packed", launching),
         _check("kv_len", spec.kv_len, [sequences], I32, "packed", launching),
     ]
+    if sparse:
+        inputs += [
+            _check("idx", idx, [tokens, idx.shape[1]], I32, "padded", launching),
+            _check("k_len", k_len, [tokens], I32, "packed", launching),
+        ]
     outputs = [
         _check("out", spec.out, [tokens, heads, V_WIDTH], F32 if spec.out.dtype == F32 else BF16,
                "padded", launching),

@@ -3,7 +3,8 @@
 The index tensors follow SmlaParams::new (crates/tq-core/src/contracts.rs:442-470): the index
 width above 2051 is rejected right after q, idx is checked as a padded [T, K] i32 tensor and k_len
 as a packed [T] i32 tensor after kv_len, and both take part in the alias check. Fake numeric
-addresses (slot << 48) as in the dense contract tests.
+addresses (slot << 48) as in the dense contract tests. Every verdict of the C validator is
+compared with the oracle restatement (oracle/contracts.py validate with idx / k_len).
 """
 
 import ctypes
@@ -18,34 +19,52 @@ SHAPE, DTYPE, STRIDE, ADDRESS, CAPACITY, QUERY_COUNT, ALIAS = 1, 2, 4, 6, 7, 9, 
 I32 = _abi.DTYPE_I32
 
 
-def tspec(shape, strides, dtype, slot):
-    t = _abi.TqTensorSpec()
-    t.rank = len(shape)
-    for i, (d, st) in enumerate(zip(shape, strides)):
-        t.shape[i], t.strides_bytes[i] = d, st
-    t.dtype = dtype
-    t.device_address = slot << 48
-    t.buffer_bytes = (sum((d - 1) * st for d, st in zip(shape, strides)) + strides[-1]
-                      if all(shape) else 0)
-    return t
+class T:
+    """An oracle tensor declaration whose fields can be edited like the C struct's."""
+
+    def __init__(self, shape, strides, slot):
+        self.o = oc.Tensor(list(shape), list(strides), oc.I32, slot << 48, 0)
+        self.o.capacity = oc.wide_span(self.o)
+
+    def c(self):
+        t = _abi.TqTensorSpec()
+        t.rank = len(self.o.shape)
+        for i, (d, st) in enumerate(zip(self.o.shape, self.o.strides)):
+            t.shape[i], t.strides_bytes[i] = d & U64, st & U64
+        t.dtype = self.o.dtype
+        t.device_address = self.o.address & U64
+        t.buffer_bytes = self.o.capacity & U64
+        return t
+
+
+U64 = (1 << 64) - 1
 
 
 def verdict(spec, idx, k_len, counts):
+    """The C verdict (field, kind) or None, after checking the oracle gives the same one."""
     c = to_c(spec)
     params = _abi.TqMlaParams()
     err = _abi.TqContractError()
     arr = (ctypes.c_uint8 * max(1, len(counts)))(*[x & 0xFF for x in counts])
-    st = _abi.lib.tq_mla_sparse_validate(ctypes.byref(c), ctypes.byref(idx), ctypes.byref(k_len),
+    ci, ck = idx.c(), k_len.c()
+    st = _abi.lib.tq_mla_sparse_validate(ctypes.byref(c), ctypes.byref(ci), ctypes.byref(ck),
                                          arr, len(counts), ctypes.byref(params),
                                          ctypes.byref(err))
-    return (None if st == 0 else (err.field.decode(), st)), params
+    cv = None if st == 0 else (err.field.decode(), st)
+    try:
+        oc.validate(spec, counts, idx=idx.o, k_len=k_len.o)
+        ov = None
+    except oc.ContractError as e:
+        ov = (e.field, e.kind)
+    assert cv == ov, (cv, ov)
+    return cv, params
 
 
 def case(counts=(1, 2, 4), heads=32, k=2048, fmt=oc.KV_BF16, idx_row=None):
     t = sum(counts)
     spec = smla(t, heads, len(counts), fmt)
-    idx = tspec([t, k], [idx_row or 4 * max(k, 1), 4], I32, 40)  # canonical empty stride
-    k_len = tspec([t], [4], I32, 41)
+    idx = T([t, k], [idx_row or 4 * max(k, 1), 4], 40)  # canonical empty stride for K = 0
+    k_len = T([t], [4], 41)
     return spec, idx, k_len, list(counts)
 
 
@@ -73,21 +92,21 @@ def test_rejections():
     spec, idx, k_len, counts = case(fmt=oc.KV_BF16_ROPE576)
     assert verdict(spec, idx, k_len, counts)[0] == ("kv_format", SHAPE)
     spec, idx, k_len, counts = case()
-    idx.dtype = _abi.DTYPE_F32
+    idx.o.dtype = oc.F32
     assert verdict(spec, idx, k_len, counts)[0] == ("idx", DTYPE)
     spec, idx, k_len, counts = case()
-    idx.shape[0] -= 1
+    idx.o.shape[0] -= 1
     assert verdict(spec, idx, k_len, counts)[0] == ("idx", SHAPE)
     spec, idx, k_len, counts = case(idx_row=4 * 2048 + 2)
     assert verdict(spec, idx, k_len, counts)[0] == ("idx", STRIDE)
     spec, idx, k_len, counts = case()
-    k_len.strides_bytes[0] = 8
+    k_len.o.strides[0] = 8
     assert verdict(spec, idx, k_len, counts)[0] == ("k_len", STRIDE)
     spec, idx, k_len, counts = case()
-    k_len.device_address = 0
+    k_len.o.address = 0
     assert verdict(spec, idx, k_len, counts)[0] == ("k_len", ADDRESS)
     spec, idx, k_len, counts = case()
-    idx.buffer_bytes -= 1
+    idx.o.capacity -= 1
     assert verdict(spec, idx, k_len, counts)[0] == ("idx", CAPACITY)
     spec, idx, k_len, counts = case(counts=(5,))
     assert verdict(spec, idx, k_len, counts)[0] == ("query_counts", QUERY_COUNT)
@@ -97,14 +116,14 @@ def test_rejections():
 
 def test_index_tensors_take_part_in_the_alias_check():
     spec, idx, k_len, counts = case()
-    idx.device_address = spec.out.address + 64
+    idx.o.address = spec.out.address + 64
     assert verdict(spec, idx, k_len, counts)[0] == ("out", ALIAS)
 
 
 def test_empty_batch_needs_no_index_storage():
     spec, idx, k_len, counts = case(counts=(0, 0))
     for t in (idx, k_len):
-        t.device_address = 0
-        t.buffer_bytes = 0
+        t.o.address = 0
+        t.o.capacity = 0
     v, params = verdict(spec, idx, k_len, counts)
     assert v is None and params.should_launch == 0
