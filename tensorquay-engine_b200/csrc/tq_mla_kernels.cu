@@ -408,7 +408,7 @@ struct Waiter {
 // and dequantization to bf16, sparse bf16 rows with cp.async. The MMA and softmax warps are
 // unchanged.
 template <bool kRope, bool kFp8 = false, bool kSparse = false>
-__global__ void __launch_bounds__((kFp8 || kSparse) ? kThreadsFp8 : kThreads, 1)
+__global__ void __launch_bounds__((kFp8 || kSparse) ? kThreadsGather : kThreads, 1)
     mla_paged_kernel(const __grid_constant__ CUtensorMap tm_q,
                      const __grid_constant__ CUtensorMap tm_kv,
                      const __grid_constant__ CUtensorMap tm_v, const MainArgs a) {
@@ -1574,7 +1574,7 @@ int32_t launch(const TqMlaParams* params, void* workspace, uint64_t workspace_by
 
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * pairs, 1, 1);
-    cfg.blockDim = dim3((fp8 || sparse) ? kThreadsFp8 : kThreads, 1, 1);
+    cfg.blockDim = dim3((fp8 || sparse) ? kThreadsGather : kThreads, 1, 1);
     cfg.dynamicSmemBytes = kSmBytes;
     cfg.stream = st;
     cudaLaunchAttribute attr[2];

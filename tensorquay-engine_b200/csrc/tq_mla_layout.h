@@ -30,8 +30,8 @@ constexpr int kSegmentCostPages = 8;
 constexpr int kSoftmaxWarps = 4;
 constexpr int kSoftmaxThreads = 32 * kSoftmaxWarps;
 constexpr int kThreads = 64 + kSoftmaxThreads;  // warp 0 TMA, warp 1 MMA, warps 2-5 softmax
-constexpr int kConvertWarps = 4;                 // FP8 rows: warps 6-9 dequantize the pages
-constexpr int kThreadsFp8 = kThreads + 32 * kConvertWarps;
+constexpr int kConvertWarps = 4;                 // FP8 rows, sparse plans: warps 6-9 fill the pages
+constexpr int kThreadsGather = kThreads + 32 * kConvertWarps;
 constexpr int kFp8RowCodes = 512;                // E4M3 codes per row, then 4 f32 scales
 constexpr int kQTmemDims = 384;                 // query dims held in TMEM (A operand)
 
