@@ -205,10 +205,19 @@ int32_t tq_mla_decode_no_alloc(const TqMlaParams* params, void* stream, TqContra
  * not touched. A row whose seq_id, pos or page entry is out of range is skipped and, when
  * `device_flags` (a device int32, may be null) is given, TQ_DEV_SEQ_RANGE, TQ_DEV_TABLE_SHORT or
  * TQ_DEV_PAGE_RANGE is OR-ed into it. Two rows naming one slot in a call race (either may win).
- * The launch grid depends only on the device, so a captured call replays for new contents. */
+ * The launch grid depends only on the device, so a captured call replays for new contents.
+ * Optional RMSNorm of each row's 512 latent values before the write (the norm of the planned
+ * "kv_a -> norm -> cache write" prologue; docs/DEV-PLAN.md:116): with norm_weight a bf16 [512]
+ * tensor (rank 0 switches it off) and norm_eps finite and > 0, each latent value becomes
+ * bf16(x * r * w) with r = 1 / sqrt(sum(x^2) / 512 + eps). All f32 operations are IEEE
+ * round-to-nearest (no fused multiply-add); the sum adds each 16-value run in order, then
+ * combines the 32 runs pairwise at distances 16, 8, 4, 2, 1. The 64 RoPE values of a 576-wide
+ * row are copied unchanged; FP8 rows quantize the normalised bf16 values. */
 typedef struct {
   TqTensorSpec src, kv, page_table, seq_id, pos;
   int32_t kv_format;
+  TqTensorSpec norm_weight; /* bf16 [512], or rank 0 for no norm */
+  float norm_eps;
 } TqKvWriteSpec;
 int32_t tq_kv_write_validate(const TqKvWriteSpec* spec, TqContractError* err);
 int32_t tq_kv_write(const TqKvWriteSpec* spec, int32_t* device_flags, void* stream,

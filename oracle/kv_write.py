@@ -68,6 +68,34 @@ def quantize_rows(x):
     return codes.reshape(rows, FP8_CODES), scale
 
 
+def rms_norm_rows(src_bf16_bits, weight_bf16_bits, eps):
+    """RMSNorm of each row's 512 latent values with the writer's f32 arithmetic, bit for bit:
+    per 16-value run the squares are added in dim order, the 32 run sums are combined pairwise at
+    distances 16, 8, 4, 2, 1, mean = sum / 512, r = 1 / sqrt(mean + eps), y = bf16((x * r) * w),
+    every operation an IEEE round-to-nearest f32 operation (no fused multiply-add). Returns the
+    new bf16 bits (uint16 ``[R, 512]``)."""
+    from oracle.fp8 import bf16_round
+
+    f32 = np.float32
+    x = (np.asarray(src_bf16_bits, dtype=np.uint16)[:, :512].astype(np.uint32) << 16).view(f32)
+    w = (np.asarray(weight_bf16_bits, dtype=np.uint16).astype(np.uint32) << 16).view(f32)
+    runs = x.reshape(-1, 32, 16)
+    acc = np.zeros(runs.shape[:2], f32)
+    with np.errstate(over="ignore", invalid="ignore", under="ignore"):
+        for i in range(16):
+            acc = (acc + (runs[:, :, i] * runs[:, :, i]).astype(f32)).astype(f32)
+        lanes = np.arange(32)
+        for o in (16, 8, 4, 2, 1):
+            acc = (acc + acc[:, lanes ^ o]).astype(f32)
+        total = acc[:, 0]
+        r = (f32(1.0) / np.sqrt(((total / f32(512.0)).astype(f32) + f32(eps)).astype(f32))).astype(f32)
+        y = ((x * r[:, None]).astype(f32) * w[None, :]).astype(f32)
+    bits = (bf16_round(y).astype(np.float32).view(np.uint32) >> 16).astype(np.uint16)
+    nan = np.isnan(y)
+    bits[nan] = 0x7FC0
+    return bits
+
+
 def row_bytes(src_bf16_bits, kv_format):
     """Payload bytes of each new row: ``src_bf16_bits`` is uint16 ``[R, W]`` (bf16 bit patterns).
 
@@ -84,7 +112,8 @@ def row_bytes(src_bf16_bits, kv_format):
     return out
 
 
-def write(pool_u8, src_bf16_bits, page_table, seq_id, pos, kv_format):
+def write(pool_u8, src_bf16_bits, page_table, seq_id, pos, kv_format, norm_weight_bits=None,
+          norm_eps=None):
     """Apply the writer to a copy of ``pool_u8`` (``[P, 64, r]``); returns (pool, skipped mask).
 
     Row t goes to ``page_table[seq_id[t]][pos[t] // 64] * 64 + pos[t] % 64``. A row whose
@@ -95,6 +124,9 @@ def write(pool_u8, src_bf16_bits, page_table, seq_id, pos, kv_format):
     pool = np.array(pool_u8, copy=True)
     pages, _, stride = pool.shape
     flat = pool.reshape(pages * PAGE_ROWS, stride)
+    if norm_weight_bits is not None:
+        src_bf16_bits = np.array(src_bf16_bits, dtype=np.uint16, copy=True)
+        src_bf16_bits[:, :512] = rms_norm_rows(src_bf16_bits, norm_weight_bits, norm_eps)
     payload = row_bytes(src_bf16_bits, kv_format)
     s_count, slots = page_table.shape
     skipped = np.zeros(len(seq_id), bool)

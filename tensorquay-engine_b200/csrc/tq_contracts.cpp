@@ -291,7 +291,7 @@ int32_t kv_write_validate_impl(const TqKvWriteSpec* spec, TqContractError* err) 
   const uint64_t pool[3] = {s.kv.shape[0], kPageRows, payload};
   const uint64_t table[2] = {sequences, slots};
   const uint64_t tok[1] = {rows};
-  Extent in[4], out[1];
+  Extent in[5], out[1];
   if (!check("src", s.src, src_shape, 2, TQ_DTYPE_BF16, Layout::PaddedOuter, launching, &in[0],
              &f) ||
       !check("page_table", s.page_table, table, 2, TQ_DTYPE_I32, Layout::Packed, launching,
@@ -304,7 +304,17 @@ int32_t kv_write_validate_impl(const TqKvWriteSpec* spec, TqContractError* err) 
     if (s.src.strides_bytes[0] % 16) return fail("src", TQ_STRIDE);
     if (s.src.device_address % 16) return fail("src", TQ_ALIGNMENT);
   }
-  if (!check_aliases(in, 4, out, 1, &f)) return fail(f.field, f.kind);
+  int n_in = 4;
+  if (s.norm_weight.rank != 0) {
+    const uint64_t w_shape[1] = {512};
+    if (!check("norm_weight", s.norm_weight, w_shape, 1, TQ_DTYPE_BF16, Layout::Packed,
+               launching, &in[4], &f))
+      return fail(f.field, f.kind);
+    if (launching && s.norm_weight.device_address % 16) return fail("norm_weight", TQ_ALIGNMENT);
+    if (!(std::isfinite(s.norm_eps) && s.norm_eps > 0.f)) return fail("norm_eps", TQ_SCALE);
+    n_in = 5;
+  }
+  if (!check_aliases(in, n_in, out, 1, &f)) return fail(f.field, f.kind);
   if (err) { err->field = nullptr; err->kind = TQ_OK; }
   return TQ_OK;
 }

@@ -40,6 +40,8 @@ struct Args {
   const int* pos;
   long long rows;
   int* flags;  // device error flags (may be null)
+  const uint16_t* norm_w;  // RMSNorm weight, bf16 [512], or null
+  float norm_eps;
 };
 
 __device__ __forceinline__ void flag(const Args& a, int bit) {
@@ -124,6 +126,43 @@ __device__ __forceinline__ void quantize_store(uint8_t* dst, const uint4 w0, con
   }
 }
 
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+
+// RMSNorm of one row's 512 latent values, this lane holding values [16 lane, 16 lane + 16) as
+// two 16-byte words of bf16 (in place). Only IEEE round-to-nearest f32 operations, in a fixed
+// order: the lane's squares added in dim order, the 32 lane sums combined pairwise at distances
+// 16, 8, 4, 2, 1 (both lanes of a pair get the same sum), mean = sum / 512, r = 1 / sqrt(mean +
+// eps), y = bf16((x * r) * w). All 32 lanes take part.
+__device__ __forceinline__ void rms_norm_16(uint4& w0, uint4& w1, const uint16_t* nw, float eps,
+                                            int lane) {
+  uint32_t words[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+  float acc = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const float lo = __uint_as_float(words[i] << 16), hi = __uint_as_float(words[i] & 0xFFFF0000u);
+    acc = __fadd_rn(acc, __fmul_rn(lo, lo));
+    acc = __fadd_rn(acc, __fmul_rn(hi, hi));
+  }
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) acc = __fadd_rn(acc, __shfl_xor_sync(0xFFFFFFFFu, acc, o));
+  const float r = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(__fdiv_rn(acc, 512.f), eps)));
+  const uint4 g0 = __ldg(reinterpret_cast<const uint4*>(nw) + 2 * lane);
+  const uint4 g1 = __ldg(reinterpret_cast<const uint4*>(nw) + 2 * lane + 1);
+  const uint32_t gw[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const float lo = __uint_as_float(words[i] << 16), hi = __uint_as_float(words[i] & 0xFFFF0000u);
+    const float wl = __uint_as_float(gw[i] << 16), wh = __uint_as_float(gw[i] & 0xFFFF0000u);
+    words[i] = pack_bf16x2(__fmul_rn(__fmul_rn(lo, r), wl), __fmul_rn(__fmul_rn(hi, r), wh));
+  }
+  w0 = make_uint4(words[0], words[1], words[2], words[3]);
+  w1 = make_uint4(words[4], words[5], words[6], words[7]);
+}
+
 template <int kFormat>
 __global__ void __launch_bounds__(32 * kRowsPerBlock) kv_write_kernel(Args a) {
   const int lane = threadIdx.x & 31;
@@ -135,6 +174,18 @@ __global__ void __launch_bounds__(32 * kRowsPerBlock) kv_write_kernel(Args a) {
       uint8_t* dst = slot_of(a, t, lane);
       if (!dst) continue;
       const uint8_t* src = a.src + t * a.src_stride;
+      if (a.norm_w) {
+        // Latent values normalised (this lane: units 2 lane, 2 lane + 1); RoPE units copied.
+        uint4 w0 = __ldg(reinterpret_cast<const uint4*>(src) + 2 * lane);
+        uint4 w1 = __ldg(reinterpret_cast<const uint4*>(src) + 2 * lane + 1);
+        rms_norm_16(w0, w1, a.norm_w, a.norm_eps, lane);
+        reinterpret_cast<uint4*>(dst)[2 * lane] = w0;
+        reinterpret_cast<uint4*>(dst)[2 * lane + 1] = w1;
+        if (kUnits > 64 && lane < kUnits - 64)
+          reinterpret_cast<uint4*>(dst)[64 + lane] =
+              __ldg(reinterpret_cast<const uint4*>(src) + 64 + lane);
+        continue;
+      }
 #pragma unroll
       for (int i = lane; i < kUnits; i += 32)
         reinterpret_cast<uint4*>(dst)[i] = __ldg(reinterpret_cast<const uint4*>(src) + i);
@@ -145,12 +196,16 @@ __global__ void __launch_bounds__(32 * kRowsPerBlock) kv_write_kernel(Args a) {
       const long long t2 = t + step;
       const bool has2 = t2 < a.rows;
       const uint4* s1 = reinterpret_cast<const uint4*>(a.src + t * a.src_stride) + 2 * lane;
-      const uint4 a0 = __ldg(s1), a1 = __ldg(s1 + 1);
+      uint4 a0 = __ldg(s1), a1 = __ldg(s1 + 1);
       uint4 b0 = make_uint4(0u, 0u, 0u, 0u), b1 = b0;
       if (has2) {
         const uint4* s2 = reinterpret_cast<const uint4*>(a.src + t2 * a.src_stride) + 2 * lane;
         b0 = __ldg(s2);
         b1 = __ldg(s2 + 1);
+      }
+      if (a.norm_w) {  // quantize the normalised bf16 values
+        rms_norm_16(a0, a1, a.norm_w, a.norm_eps, lane);
+        if (has2) rms_norm_16(b0, b1, a.norm_w, a.norm_eps, lane);
       }
       quantize_store(slot_of(a, t, lane), a0, a1, lane);
       if (has2) quantize_store(slot_of(a, t2, lane), b0, b1, lane);
@@ -201,6 +256,9 @@ extern "C" int32_t tq_kv_write(const TqKvWriteSpec* spec, int32_t* device_flags,
   a.pos = reinterpret_cast<const int*>(s.pos.device_address);
   a.rows = rows;
   a.flags = device_flags;
+  a.norm_w = s.norm_weight.rank != 0 ? reinterpret_cast<const uint16_t*>(s.norm_weight.device_address)
+                                     : nullptr;
+  a.norm_eps = s.norm_eps;
   const long long want = (rows + kRowsPerBlock - 1) / kRowsPerBlock;
   const int blocks = int(want < 8ll * sms ? want : 8ll * sms);
   cudaStream_t cs = reinterpret_cast<cudaStream_t>(stream);

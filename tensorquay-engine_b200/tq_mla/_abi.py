@@ -81,7 +81,7 @@ class TqWorkspaceLayout(ctypes.Structure):
 
 class TqKvWriteSpec(ctypes.Structure):
     _fields_ = [(name, TqTensorSpec) for name in ("src", "kv", "page_table", "seq_id", "pos")] + [
-        ("kv_format", ctypes.c_int32)]
+        ("kv_format", ctypes.c_int32), ("norm_weight", TqTensorSpec), ("norm_eps", ctypes.c_float)]
 
 
 # Every exported symbol of include/tq_mla.h, with its ctypes prototype.

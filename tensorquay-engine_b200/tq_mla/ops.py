@@ -206,7 +206,8 @@ def mla_decode(q, kv, page_table, seq_id, q_pos, kv_len, *, scale, query_counts=
     return launch(stream)
 
 
-def kv_write_spec(src, kv, page_table, seq_id, pos, *, kv_format=None):
+def kv_write_spec(src, kv, page_table, seq_id, pos, *, kv_format=None, norm_weight=None,
+                  norm_eps=1e-6):
     """Declaration of a KV-writer call: ``src`` bf16 ``[T, W]`` rows into the paged pool ``kv``."""
     if kv_format is None:
         kv_format = _abi.KV_BF16_ROPE576 if src.shape[-1] == 576 else _abi.KV_BF16
@@ -217,17 +218,23 @@ def kv_write_spec(src, kv, page_table, seq_id, pos, *, kv_format=None):
     s.seq_id = spec_of(seq_id)
     s.pos = spec_of(pos)
     s.kv_format = kv_format
+    if norm_weight is not None:
+        s.norm_weight = spec_of(norm_weight)
+        s.norm_eps = float(norm_eps)
     return s
 
 
-def kv_write(src, kv, page_table, seq_id, pos, *, kv_format=None, flags=None, stream=None):
+def kv_write(src, kv, page_table, seq_id, pos, *, kv_format=None, flags=None, stream=None,
+             norm_weight=None, norm_eps=1e-6):
     """Write row ``t`` of ``src`` to position ``pos[t]`` of sequence ``seq_id[t]`` in ``kv``.
 
     bf16 formats copy the row; ``KV_FP8_E4M3`` quantizes it per 128-value tile (codes plus f32
-    scales). ``flags`` is an optional device ``int32`` tensor that collects the range flags of
-    skipped rows (``TQ_DEV_*``).
+    scales). With ``norm_weight`` (bf16 ``[512]``) the row's 512 latent values are RMS-normalised
+    first (``norm_eps`` > 0). ``flags`` is an optional device ``int32`` tensor that collects the
+    range flags of skipped rows (``TQ_DEV_*``).
     """
-    s = kv_write_spec(src, kv, page_table, seq_id, pos, kv_format=kv_format)
+    s = kv_write_spec(src, kv, page_table, seq_id, pos, kv_format=kv_format,
+                      norm_weight=norm_weight, norm_eps=norm_eps)
     err = _abi.TqContractError()
     fp = ctypes.c_void_p(flags.data_ptr()) if flags is not None else None
     raise_for(lib.tq_kv_write(ctypes.byref(s), fp, _stream_handle(stream), ctypes.byref(err)), err)

@@ -48,7 +48,7 @@ STRUCTS = {
                                                    "sparse_count", "pairs"]),
     "TqContractError": (_abi.TqContractError, ["field", "kind"]),
     "TqKvWriteSpec": (_abi.TqKvWriteSpec, ["src", "kv", "page_table", "seq_id", "pos",
-                                           "kv_format"]),
+                                           "kv_format", "norm_weight", "norm_eps"]),
 }
 
 

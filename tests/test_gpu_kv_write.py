@@ -80,6 +80,33 @@ def test_writer_matches_the_oracle_bit_for_bit(cuda_device, fmt, row_stride):
     np.testing.assert_array_equal(got, want)
 
 
+@pytest.mark.parametrize("fmt,row_stride", [
+    (_abi.KV_FP8_E4M3, 544), (_abi.KV_BF16, 1024), (_abi.KV_BF16_ROPE576, 1152),
+])
+def test_writer_with_rms_norm_matches_the_oracle_bit_for_bit(cuda_device, fmt, row_stride):
+    """The optional RMSNorm before the write: the oracle restates the kernel's f32 operation order,
+    so every byte of the pool matches (the 64 RoPE values of a 576-wide row are copied)."""
+    pool, table, seq_id, pos, src = _case(31 + fmt, fmt, row_stride, rows=2000)
+    src = src.clone()
+    src[:16] = torch.randn((16, src.shape[1])).to(torch.bfloat16)  # no NaN or inf rows
+    src[16:] = torch.nan_to_num(src[16:].float(), nan=0.0, posinf=1.0,
+                                neginf=-1.0).to(torch.bfloat16)
+    rng = np.random.default_rng(fmt)
+    weight = torch.from_numpy(rng.uniform(0.25, 2.0, 512).astype(np.float32)).to(torch.bfloat16)
+    d_pool = pool.to(cuda_device)
+    flags = torch.zeros(1, dtype=torch.int32, device=cuda_device)
+    ops.kv_write(src.to(cuda_device), d_pool, torch.from_numpy(table).to(cuda_device),
+                 torch.from_numpy(seq_id).to(cuda_device), torch.from_numpy(pos).to(cuda_device),
+                 kv_format=fmt, flags=flags, norm_weight=weight.to(cuda_device), norm_eps=1e-6)
+    torch.cuda.synchronize()
+    bits = src.view(torch.int16).numpy().view(np.uint16)
+    wbits = weight.view(torch.int16).numpy().view(np.uint16)
+    want, skipped = okw.write(pool.numpy(), bits, table, seq_id, pos, fmt,
+                              norm_weight_bits=wbits, norm_eps=1e-6)
+    assert int(flags.item()) == 0 and not skipped.any()
+    np.testing.assert_array_equal(d_pool.cpu().numpy(), want)
+
+
 def test_fp8_special_tiles_land_as_defined(cuda_device):
     pool, table, seq_id, pos, src = _case(5, _abi.KV_FP8_E4M3, 544, rows=8)
     got, _ = _run(pool, table, seq_id, pos, src, _abi.KV_FP8_E4M3, cuda_device)

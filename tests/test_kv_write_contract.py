@@ -92,3 +92,26 @@ def test_empty_call_needs_no_storage():
     assert verdict(s) is None
     err = _abi.TqContractError()
     assert _abi.lib.tq_kv_write(ctypes.byref(s), None, None, ctypes.byref(err)) == 0
+
+
+def test_norm_weight_and_eps():
+    s = spec()
+    s.norm_weight = tensor([512], [2], _abi.DTYPE_BF16, 6 * GiB)
+    s.norm_eps = 1e-6
+    assert verdict(s) is None
+    s.norm_eps = 0.0
+    assert verdict(s) == ("norm_eps", 10)
+    s.norm_eps = float("nan")
+    assert verdict(s) == ("norm_eps", 10)
+    s = spec()
+    s.norm_weight = tensor([576], [2], _abi.DTYPE_BF16, 6 * GiB)
+    s.norm_eps = 1e-6
+    assert verdict(s) == ("norm_weight", SHAPE)
+    s = spec()
+    s.norm_weight = tensor([512], [2], _abi.DTYPE_BF16, 6 * GiB + 8)
+    s.norm_eps = 1e-6
+    assert verdict(s) == ("norm_weight", ALIGNMENT)
+    s = spec()
+    s.norm_weight = tensor([512], [2], _abi.DTYPE_BF16, 2 * GiB + 4096)  # inside the pool
+    s.norm_eps = 1e-6
+    assert verdict(s) == ("kv", ALIAS)

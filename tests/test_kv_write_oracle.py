@@ -66,3 +66,17 @@ def test_write_scatters_rows_and_skips_bad_slots():
     changed = np.flatnonzero((new != pool).any(axis=2).reshape(-1))
     assert set(changed.tolist()) <= {70, 3, 150}
     assert (new.reshape(-1, 544)[:, 528:] == pool.reshape(-1, 544)[:, 528:]).all()
+
+
+def test_rms_norm_rows_is_rmsnorm_to_bf16_rounding():
+    rng = np.random.default_rng(3)
+    x = (rng.standard_normal((6, 512)) * np.exp(rng.uniform(-8, 8, (6, 1)))).astype(np.float32)
+    w = rng.uniform(0.5, 1.5, 512).astype(np.float32)
+    bits = lambda a: (torch.from_numpy(a).to(torch.bfloat16).view(torch.int16).numpy()
+                      .view(np.uint16))
+    xb, wb = bits(x), bits(w)
+    got = (okw.rms_norm_rows(xb, wb, 1e-6).astype(np.uint32) << 16).view(np.float32)
+    xf = (xb.astype(np.uint32) << 16).view(np.float32).astype(np.float64)
+    wf = (wb.astype(np.uint32) << 16).view(np.float32).astype(np.float64)
+    want = xf / np.sqrt((xf ** 2).mean(axis=1, keepdims=True) + 1e-6) * wf
+    np.testing.assert_allclose(got, want, rtol=2 ** -8, atol=1e-30)
