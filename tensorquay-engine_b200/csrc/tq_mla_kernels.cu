@@ -763,6 +763,9 @@ __global__ void __launch_bounds__((kFp8 || kSparse) ? kThreadsGather : kThreads,
       const int cw = warp - 6, hl = lane & 15;
       uint32_t it = 0;
       uint32_t grant_parity = 0;  // bit s: parity of the next grant phase of stage s
+      // Sparse bf16: the next page's pool rows, read while this page's copies are in flight.
+      int next_own[8], next_pr[4];
+      bool have_next = false;
       Seg s;
       bool ok = true;
       while (ok && walker.next(meta, s)) {
@@ -847,17 +850,25 @@ __global__ void __launch_bounds__((kFp8 || kSparse) ? kThreadsGather : kThreads,
                     2 * (hl & 3), r & 7, pr[q], pr_sc[q]);
             }
           } else {
-            // Sparse bf16 rows: row numbers read before the grant, copies issued after it.
-            long long own_row[8], pr_row[4];
+            // Sparse bf16 rows: the page's row numbers (read while the previous page of the
+            // segment was in flight, else now), then the grant, then the copies.
+            int own_row[8], pr_row[4];
+            if (have_next) {
 #pragma unroll
-            for (int i = 0; i < 8; ++i) {
-              const int key = key0 + 8 * cw + i;
-              own_row[i] = key < valid ? row_of(key) : -1;
-            }
+              for (int i = 0; i < 8; ++i) own_row[i] = next_own[i];
 #pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              const int key = (kKeysPerCta - key0) + 8 * cw + 2 * q + (lane >> 4);
-              pr_row[q] = key < valid ? row_of(key) : -1;
+              for (int q = 0; q < 4; ++q) pr_row[q] = next_pr[q];
+            } else {
+#pragma unroll
+              for (int i = 0; i < 8; ++i) {
+                const int key = key0 + 8 * cw + i;
+                own_row[i] = key < valid ? int(row_of(key)) : -1;
+              }
+#pragma unroll
+              for (int q = 0; q < 4; ++q) {
+                const int key = (kKeysPerCta - key0) + 8 * cw + 2 * q + (lane >> 4);
+                pr_row[q] = key < valid ? int(row_of(key)) : -1;
+              }
             }
             wt.where = (7 << 24) | int(it & 0xFFFFFF);
             const bool got =
@@ -867,8 +878,9 @@ __global__ void __launch_bounds__((kFp8 || kSparse) ? kThreadsGather : kThreads,
             const uint32_t st_base = base + kSmKv + stage * kStageBytes;
             // Two 16-byte units (dims [8 u0, 8 u0 + 16) of the chunk) of one row; a row of -1
             // is written as zeros without a read.
-            auto copy2 = [&](uint32_t rowp, int u0, int r8, long long row, int byte0) {
-              const uint8_t* src = a.kv + (row < 0 ? 0 : row * a.kv_row_stride + byte0);
+            auto copy2 = [&](uint32_t rowp, int u0, int r8, int row, int byte0) {
+              const uint8_t* src =
+                  a.kv + (row < 0 ? 0 : (long long)row * a.kv_row_stride + byte0);
               const uint32_t nbytes = row < 0 ? 0u : 16u;
               ptx::cp_async_16(rowp + ((u0 ^ r8) << 4), src, nbytes);
               ptx::cp_async_16(rowp + (((u0 + 1) ^ r8) << 4), src + (row < 0 ? 0 : 16), nbytes);
@@ -885,6 +897,21 @@ __global__ void __launch_bounds__((kFp8 || kSparse) ? kThreadsGather : kThreads,
               copy2(st_base + kPvxOffset + (r >> 3) * kPeerGroupBytes + (hl >> 2) * kAtomBytes +
                         (r & 7) * 128,
                     2 * (hl & 3), r & 7, pr_row[q], 2 * vdim0 + 32 * hl);
+            }
+            have_next = j + 1 < s.np;
+            if (have_next) {
+              const int pn = p + 1;
+              const int vn = min(kPageRows, n - pn * kPageRows);
+#pragma unroll
+              for (int i = 0; i < 8; ++i) {
+                const int key = key0 + 8 * cw + i;
+                next_own[i] = key < vn ? srows[pn * kPageRows + key] : -1;
+              }
+#pragma unroll
+              for (int q = 0; q < 4; ++q) {
+                const int key = (kKeysPerCta - key0) + 8 * cw + 2 * q + (lane >> 4);
+                next_pr[q] = key < vn ? srows[pn * kPageRows + key] : -1;
+              }
             }
             ptx::cp_async_wait_all();
           }
