@@ -766,6 +766,7 @@ __global__ void __launch_bounds__((kFp8 || kSparse) ? kThreadsGather : kThreads,
       // Sparse bf16: the next page's pool rows, read while this page's copies are in flight.
       int next_own[8], next_pr[4];
       bool have_next = false;
+      int next_page = 0;  // dense: the segment's next page-table entry, read one page ahead
       Seg s;
       bool ok = true;
       while (ok && walker.next(meta, s)) {
@@ -780,7 +781,9 @@ __global__ void __launch_bounds__((kFp8 || kSparse) ? kThreadsGather : kThreads,
           long long row0 = 0;
           bool page_ok = true;
           if constexpr (!kSparse) {
-            const int page = pt[p];
+            const int page = (have_next && j > 0) ? next_page : pt[p];
+            if (j + 1 < s.np) next_page = pt[p + 1];  // used by the next page; no wait here
+            have_next = j + 1 < s.np;
             row0 = (long long)page * kPageRows;
             page_ok = page >= 0 && row0 < a.pool_rows;
             if (!page_ok && cw == 0 && lane == 0)
