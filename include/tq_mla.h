@@ -205,7 +205,8 @@ int32_t tq_mla_decode_no_alloc(const TqMlaParams* params, void* stream, TqContra
  * not touched. A row whose seq_id, pos or page entry is out of range is skipped and, when
  * `device_flags` (a device int32, may be null) is given, TQ_DEV_SEQ_RANGE, TQ_DEV_TABLE_SHORT or
  * TQ_DEV_PAGE_RANGE is OR-ed into it. Two rows naming one slot in a call race (either may win).
- * The launch grid depends only on the device, so a captured call replays for new contents.
+ * The launch grid depends only on the device and the row count, so a captured call replays
+ * for new contents of the same shapes.
  * Optional RMSNorm of each row's 512 latent values before the write (the norm of the planned
  * "kv_a -> norm -> cache write" prologue; docs/DEV-PLAN.md:116): with norm_weight a bf16 [512]
  * tensor (rank 0 switches it off) and norm_eps finite and > 0, each latent value becomes

@@ -19,6 +19,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <mutex>
 
 #include "tq_contracts.h"
 
@@ -214,11 +215,14 @@ __global__ void __launch_bounds__(32 * kRowsPerBlock) kv_write_kernel(Args a) {
 }
 
 int sm_count(int device) {
-  static int cached[64] = {0};
-  if (device >= 0 && device < 64 && cached[device]) return cached[device];
+  static std::mutex mu;
+  static int cached[128] = {0};
+  if (device < 0 || device >= 128) return 0;
+  std::lock_guard<std::mutex> lock(mu);
+  if (cached[device]) return cached[device];
   int n = 0;
   if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device) != cudaSuccess) return 0;
-  if (device >= 0 && device < 64) cached[device] = n;
+  cached[device] = n;
   return n;
 }
 

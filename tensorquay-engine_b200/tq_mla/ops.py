@@ -145,6 +145,8 @@ class MlaLaunch:
         self.prefill = prefill
         if (idx is None) != (k_len is None):
             raise ValueError("a sparse plan needs both idx and k_len")
+        if idx is not None and prefill:
+            raise ValueError("sparse top-k plans are decode plans (no prefill form)")
         sparse = None if idx is None else (spec_of(idx), spec_of(k_len))
         self.params = validate(self.spec, query_counts, prefill=prefill,
                                idx=sparse[0] if sparse else None,
