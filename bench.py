@@ -36,6 +36,7 @@ import multiprocessing as mp
 import os
 import subprocess
 import sys
+import tempfile
 import time
 from pathlib import Path
 
@@ -48,7 +49,6 @@ sys.path.insert(0, str(ROOT))
 METRIC = "MLA paged decode tokens/s"
 UNIT = "tokens/s"
 LAUNCHES_PER_STEP = 3  # scheduler + attention + combine
-REF_TIME_BUDGET_S = 90.0
 
 
 def peaks():
@@ -60,20 +60,43 @@ def peaks():
     return 6650.0, 1590.0, 1400.0, "fallback"
 
 
+# Sequences per rank when a job of N ranks is sharded (weak scaling: N times the one-GPU batch).
+SHARD_BASE = {"decode": 64, "decode_fp8": 64, "mtp": 512, "prefill": 8, "longctx": 4, "cpu": 4,
+              "sparse": 64, "sparse_fp8": 64}
+
+
 def workload_for(name, world, rank):
     from tq_mla import inputs
 
-    if world == 1:
+    if world == 1 or name == "cpu":
         return inputs.config(name)
-    base = {"decode": 64, "decode_fp8": 64, "mtp": 512, "prefill": 8, "longctx": 4,
-            "cpu": 4, "sparse": 64, "sparse_fp8": 64}[name]
-    if name in ("cpu",):
-        return inputs.config(name)
-    full = inputs.config(name, batch=base * world)
+    full = inputs.config(name, batch=SHARD_BASE[name] * world)
     return inputs.shard(full, world, rank)
 
 
+def config_block(name, world, sequences, tokens, heads, width, pool_bytes, parallelism=None):
+    """The line's ``config``: the workload's fixed description (no measured values), the same
+    for the GPU arm and the reference arm of one configuration and rank count. ``sequences``,
+    ``tokens`` and ``pool_bytes`` are the whole job's."""
+    return {
+        "workload": name if world == 1 else f"{name} x{world} ranks (token-sharded)",
+        "sequences": int(sequences), "query_tokens": int(tokens), "heads": int(heads),
+        "row_width": int(width), "value_width": 512, "page_rows": 64,
+        "parallelism": parallelism or f"sequence-shard x{world}",
+        "l2": "inputs larger than L2 (KV pool %.0f MB per GPU on average), no flush"
+              % (pool_bytes / world / 1e6),
+    }
+
+
 # ------------------------------------------------------------------------- clocks
+
+def clock_log_path(args, rank):
+    """Where the nvidia-smi samples of the timed region go: ``--clock-log`` (a file name, with
+    ``{rank}`` replaced), else a file in the system temporary directory."""
+    if getattr(args, "clock_log", None):
+        return args.clock_log.replace("{rank}", str(rank))
+    return os.path.join(tempfile.gettempdir(), f"tq_bench_clocks_rank{rank}.csv")
+
 
 class ClockSampler:
     def __init__(self, device_index, path):
@@ -130,63 +153,153 @@ class ClockSampler:
 
 # ------------------------------------------------------------------------- CPU leg
 
-def _cpu_worker(args):
-    """Time the oracle's float64 paged attention for a few sequences of a workload.
+BLAS_ENV = ("OMP_NUM_THREADS", "OPENBLAS_NUM_THREADS", "MKL_NUM_THREADS", "BLIS_NUM_THREADS",
+            "NUMEXPR_NUM_THREADS", "VECLIB_MAXIMUM_THREADS")
 
-    Inputs are regenerated here from the seed (untimed); the timed part is the gather through
-    the sequence's block table plus the attention, as the reference CPU path does per sequence.
+
+def _cpu_proc(conn, name, batch, seqs):
+    """One CPU worker: builds its sequences' inputs once from the seeded generator (untimed),
+    then, per step, times the block-table gather plus the float64 attention of each of them.
+
+    Inputs come from the oracle's NumPy generator: the same Philox streams as the GPU batch,
+    with no product library loaded. FP8 rows are random finite codes with a fixed tile scale
+    (their values do not change the float64 work); the timed part then also decodes them.
     """
-    os.environ.setdefault("OMP_NUM_THREADS", "1")
-    name, world, seqs = args
     sys.path.insert(0, str(ROOT))
     from oracle import fp8 as ofp8, generate as ogen, mla as omla
-    from tq_mla import inputs  # host metadata only (no device)
 
-    w = workload_for(name, world, 0) if world > 1 else inputs.config(name)
-    tok_global = np.concatenate([[0], np.cumsum(w.q_per_seq)[:-1]])
-    tok_off = np.concatenate([[0], np.cumsum(w.kv_len)[:-1]])
-    tokens = 0
-    elapsed = 0.0
+    w = ogen.config(name, batch=batch)
+    fp8 = w.kv_format == "fp8_e4m3"
+    jobs = []
     for b in seqs:
-        n = int(w.kv_len[b])
-        t = int(w.q_per_seq[b])
-        fp8 = w.extra.get("kv_format") == "fp8_e4m3"
+        n, t = int(w.kv_len[b]), int(w.q_per_seq[b])
         pages = (n + 63) // 64
-        perm = np.random.default_rng(b).permutation(pages)
+        table = w.page_table[b:b + 1, :pages].copy()
+        # A private pool holding just this sequence's pages, at their permuted page slots.
+        local = np.argsort(np.argsort(table[0])).astype(np.int32)[None, :]
         pos = np.arange(n)
+        rows = local[0, pos // 64].astype(np.int64) * 64 + pos % 64
         if fp8:
-            # FP8 rows: random finite codes and tile scales of the generator's magnitude; the
-            # timed part then also decodes the sequence's rows.
             rng = np.random.default_rng(int(w.seed) * 1000 + b)
             pool = np.zeros((pages * 64, 544), np.uint8)
             codes = rng.integers(0, 0x7E, size=(n, 512), dtype=np.uint8)
-            codes |= (rng.integers(0, 2, size=(n, 512), dtype=np.uint8) << 7)
-            pool[perm[pos // 64] * 64 + pos % 64, :512] = codes
-            scales = np.full((n, 4), 4.0 / 448.0, np.float32)
-            pool[perm[pos // 64] * 64 + pos % 64, 512:528] = scales.view(np.uint8)
+            codes |= rng.integers(0, 2, size=(n, 512), dtype=np.uint8) << 7
+            pool[rows, :512] = codes
+            pool[rows, 512:528] = np.full((n, 4), 4.0 / 448.0, np.float32).view(np.uint8)
         else:
-            rows = ogen.bf16_to_f64(ogen.normal_bf16(w.seed, ogen.STREAM_KV,
-                                                     int(tok_off[b]) * w.width,
-                                                     n * w.width)).reshape(n, w.width)
             pool = np.zeros((pages * 64, w.width))
-            pool[perm[pos // 64] * 64 + pos % 64] = rows
-        table = perm[None, :].astype(np.int32)
-        q = ogen.bf16_to_f64(ogen.normal_bf16(w.seed, ogen.STREAM_Q,
-                                              int(tok_global[b]) * w.heads * w.width,
-                                              t * w.heads * w.width)).reshape(t, w.heads, w.width)
-        seq_id = np.zeros(t, np.int32)
+            pool[rows] = w.sequence_rows(b)
+        q = w.sequence_queries(b)
+        q_pos = (w.prefix[b] + np.arange(t)).astype(np.int32)
+        jobs.append((q, pool, local, np.zeros(t, np.int32), q_pos, np.array([n]), t))
+    conn.send(("ready", sum(j[-1] for j in jobs)))
+    while True:
+        msg = conn.recv()
+        if msg is None:
+            break
+        t0 = time.perf_counter()
+        for q, pool, table, seq_id, q_pos, kv_len, _ in jobs:
+            values = ofp8.dequant_rows(pool) if fp8 else pool
+            omla.paged_attention(q, values, table, seq_id, q_pos, kv_len, scale=w.scale,
+                                 value_dim=512)
+        conn.send(time.perf_counter() - t0)
+    conn.close()
+
+
+class CpuTeam:
+    """``procs`` spawned processes, each with one BLAS thread, over a fixed set of sequences.
+
+    The thread limits are put into this process's environment before the children start, so
+    each child's BLAS library sees them when it loads; the parent's own settings are restored
+    afterwards. A step sends every worker its go signal and ends when the last one replies: the
+    step time is that wall-clock interval (the slowest process plus the message round trip).
+    """
+
+    def __init__(self, name, batch, seqs, procs):
+        seqs = list(seqs)
+        procs = max(1, min(procs, len(seqs)))
+        saved = {k: os.environ.get(k) for k in BLAS_ENV}
+        for k in BLAS_ENV:
+            os.environ[k] = "1"
+        ctx = mp.get_context("spawn")
+        self.conns, self.procs = [], []
+        try:
+            for i in range(procs):
+                a, b = ctx.Pipe()
+                p = ctx.Process(target=_cpu_proc, args=(b, name, batch, seqs[i::procs]),
+                                daemon=True)
+                p.start()
+                self.conns.append(a)
+                self.procs.append(p)
+        finally:
+            for k, v in saved.items():
+                if v is None:
+                    os.environ.pop(k, None)
+                else:
+                    os.environ[k] = v
+        self.tokens = sum(c.recv()[1] for c in self.conns)
+        self.sequences = len(seqs)
+
+    def step(self):
+        t0 = time.perf_counter()
+        for c in self.conns:
+            c.send(True)
+        busy = max(c.recv() for c in self.conns)
+        return time.perf_counter() - t0, busy
+
+    def close(self):
+        for c in self.conns:
+            c.send(None)
+        for p in self.procs:
+            p.join(timeout=30)
+
+
+def cpu_sample(name, world):
+    """The sequences a CPU step covers: the whole batch for the decode batches, else a fixed
+    spread of sequences of the (unsharded) job, so a step stays within about a second."""
+    sys.path.insert(0, str(ROOT))
+    from oracle import generate as ogen
+
+    batch = None if world == 1 else SHARD_BASE[name] * world
+    w = ogen.config(name, batch=batch)
+    cap = {"decode": 64, "decode_fp8": 64, "cpu": 4, "mtp": 16, "prefill": 1,
+           "longctx": 1}.get(name, 8)
+    n = min(w.sequences, cap)
+    picks = np.unique(np.linspace(0, w.sequences - 1, n).astype(int))
+    return w, batch, picks
+
+
+def single_process_seconds(name, batch, seqs):
+    """The same work in this process with its default BLAS threads (the second timing)."""
+    from oracle import fp8 as ofp8, generate as ogen, mla as omla
+
+    w = ogen.config(name, batch=batch)
+    total, tokens = 0.0, 0
+    for b in seqs:
+        n, t = int(w.kv_len[b]), int(w.q_per_seq[b])
+        if w.kv_format == "fp8_e4m3":
+            rng = np.random.default_rng(b)
+            raw = np.zeros((n, 544), np.uint8)
+            raw[:, :512] = rng.integers(0, 0x7E, size=(n, 512), dtype=np.uint8)
+            raw[:, 512:528] = np.full((n, 4), 4.0 / 448.0, np.float32).view(np.uint8)
+            rows = None
+        else:
+            rows = w.sequence_rows(b)
+        q = w.sequence_queries(b)
+        table = np.arange((n + 63) // 64, dtype=np.int32)[None, :]
         q_pos = (w.prefix[b] + np.arange(t)).astype(np.int32)
         t0 = time.perf_counter()
-        values = ofp8.dequant_rows(pool) if fp8 else pool
-        omla.paged_attention(q, values, table, seq_id, q_pos, np.array([n]), scale=w.scale,
-                             value_dim=512)
-        elapsed += time.perf_counter() - t0
+        values = ofp8.dequant_rows(raw) if rows is None else rows
+        omla.paged_attention(q, values, table, np.zeros(t, np.int32), q_pos, np.array([n]),
+                             scale=w.scale, value_dim=512)
+        total += time.perf_counter() - t0
         tokens += t
-    return tokens, elapsed
+    return tokens, total
 
 
 def _fp8_note(w):
-    return " and FP8 E4M3 row decoding" if w.extra.get("kv_format") == "fp8_e4m3" else ""
+    return " and FP8 E4M3 row decoding" if getattr(w, "kv_format", None) == "fp8_e4m3" or \
+        getattr(w, "extra", {}).get("kv_format") == "fp8_e4m3" else ""
 
 
 def kv_format_of(w):
@@ -195,31 +308,42 @@ def kv_format_of(w):
     return _abi.KV_FP8_E4M3 if w.extra.get("kv_format") == "fp8_e4m3" else None
 
 
-def cpu_baseline(name, world, budget_seqs=None, cores=None):
-    from tq_mla import inputs
-
-    w = inputs.config(name)
-    cores = cores or os.cpu_count() or 1
-    n_seq = budget_seqs or min(w.sequences, 64)
-    picks = np.linspace(0, w.sequences - 1, n_seq).astype(int)
-    chunks = [list(picks[i::cores]) for i in range(cores) if len(picks[i::cores])]
-    ctx = mp.get_context("spawn")
-    with ctx.Pool(len(chunks)) as pool:
-        res = pool.map(_cpu_worker, [(name, 1, c) for c in chunks])
-    tokens = sum(r[0] for r in res)
-    wall = max(r[1] for r in res)
+def cpu_measure(name, world, steps, warmup, single_seqs=8):
+    """Times the CPU path: ``steps`` steps of the sample over one process per host core, plus
+    one pass over a few of its sequences in a single process with default BLAS threads."""
+    w, batch, picks = cpu_sample(name, world)
+    cores = os.cpu_count() or 1
+    team = CpuTeam(name, batch, picks, cores)
+    try:
+        for _ in range(warmup):
+            team.step()
+        walls = [team.step()[0] for _ in range(steps)]
+    finally:
+        team.close()
+    st, ss = single_process_seconds(name, batch, picks[:single_seqs])
+    value = team.tokens * len(walls) / sum(walls)
+    sample = (f"{team.tokens} query tokens per step ({team.sequences} of {w.sequences} "
+              f"sequences{'' if team.sequences == w.sequences else ', spread over the batch'}) of "
+              f"{w.name}; inputs from the seeded generator (oracle/generate.py, no product "
+              f"library); timed part = block-table gather{_fp8_note(w)} + float64 attention "
+              f"(oracle restatement of mla_attention_core); {len(team.procs)} spawned processes x "
+              f"1 BLAS thread, step = wall time until the last process finishes")
     return {
-        "value": tokens / wall if wall > 0 else None,
-        "unit": UNIT,
-        "cores": len(chunks),
-        "kind": "port",
-        "sample": f"{tokens} query tokens ({n_seq} of {w.sequences} sequences, spread over the "
-                  f"batch) of {w.name}; float64 oracle restatement of mla_attention_core with "
-                  f"block-table gather{_fp8_note(w)}; {len(chunks)} spawn processes x 1 BLAS "
-                  f"thread; "
-                  f"throughput = tokens / slowest process",
-        "seconds": wall,
+        "value": value, "unit": UNIT, "cores": len(team.procs), "kind": "port",
+        "sample": sample, "steps": len(walls), "warmup": warmup,
+        "ms_per_step": 1e3 * float(np.mean(walls)),
+        "ms_per_step_p10_p50_p90": [1e3 * float(np.percentile(walls, p)) for p in (10, 50, 90)],
+        "single_process": {"value": st / ss if ss > 0 else None, "unit": UNIT,
+                           "tokens": st, "seconds": ss,
+                           "sample": f"first {len(picks[:single_seqs])} sequences of the sample "
+                                     f"in one process, default BLAS threads"},
+        "host_cores": cores,
     }
+
+
+def cpu_baseline(name, world):
+    """The ``cpu_baseline`` object of the GPU arm's line (rank 0, one GPU)."""
+    return cpu_measure(name, world, steps=10, warmup=1)
 
 
 # ------------------------------------------------------------------------- KV writer
@@ -296,8 +420,7 @@ def run_writer(args, world, rank, local_rank):
         step()
     torch.cuda.synchronize(dev)
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    clock = ClockSampler(local_rank, str(ROOT / "gpurun_out" / f"clocks_rank{rank}.csv")) \
-        if (ROOT / "gpurun_out").exists() else ClockSampler(local_rank, f"/tmp/clocks{rank}.csv")
+    clock = ClockSampler(local_rank, clock_log_path(args, rank))
     barrier()
     torch.cuda.synchronize(dev)
     with clock:
@@ -436,8 +559,7 @@ def run_sparse(args, world, rank, local_rank):
     torch.cuda.synchronize(dev)
     assert all(l.device_error() == 0 for l in launches)
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    clock = ClockSampler(local_rank, str(ROOT / "gpurun_out" / f"clocks_rank{rank}.csv")) \
-        if (ROOT / "gpurun_out").exists() else ClockSampler(local_rank, f"/tmp/clocks{rank}.csv")
+    clock = ClockSampler(local_rank, clock_log_path(args, rank))
     barrier()
     torch.cuda.synchronize(dev)
     with clock:
@@ -552,48 +674,31 @@ def run_reference(args, world, rank):
                         "d2h_bytes_per_step": 0}}
         print(json.dumps(line), flush=True)
         return
-    cores = os.cpu_count() or 1
-    from tq_mla import inputs
-
-    w = inputs.config(args.config)
-    per_step = max(cores, 1)
-    picks_all = np.arange(w.sequences)
-    times, tokens = [], []
-    # Each step is one sequence per host core (about a second of float64 work); the run stops
-    # early once REF_TIME_BUDGET_S seconds have been timed, so any --steps ends in minutes.
-    warmup = min(args.warmup, 1)
-    started = time.perf_counter()
-    ctx = mp.get_context("spawn")
-    with ctx.Pool(cores) as pool:
-        for step in range(warmup + args.steps):
-            if step > warmup and time.perf_counter() - started > REF_TIME_BUDGET_S:
-                break
-            sample = np.roll(picks_all, -step * per_step)[:per_step]
-            chunks = [[int(s)] for s in sample]
-            t0 = time.perf_counter()
-            res = pool.map(_cpu_worker, [(args.config, 1, c) for c in chunks])
-            wall = time.perf_counter() - t0
-            if step >= warmup:
-                tok = sum(r[0] for r in res)
-                busy = max(r[1] for r in res)
-                times.append(busy)
-                tokens.append(tok)
-    value = sum(tokens) / sum(times)
+    # Dense configurations: the oracle's float64 restatement of mla_attention_core over the same
+    # seeded inputs, one spawned process per host core; no product library is loaded.
+    base = cpu_measure(args.config, world, steps=args.steps, warmup=args.warmup)
+    w, _, _ = cpu_sample(args.config, world)
     dtype = "f64" + (" (FP8 E4M3 rows decoded to f64)" if _fp8_note(w) else "")
     line = {
-        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT,
-        "n_gpus": world, "steps": len(times), "steps_requested": args.steps, "warmup": warmup,
-        "ms_per_step": 1e3 * float(np.mean(times)), "higher_is_better": True,
+        "impl": "reference", "metric": METRIC, "value": base["value"], "unit": UNIT,
+        "n_gpus": world, "steps": base["steps"], "warmup": base["warmup"],
+        "ms_per_step": base["ms_per_step"], "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": dtype, "data": "synthetic",
-        "config": {"workload": w.name, "heads": w.heads, "row_width": w.width,
-                   "sequences_per_step": per_step},
-        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port",
-                         "sample": f"{per_step} sequences of {w.name} per step, one per spawn "
-                                   f"process (1 BLAS thread each); timed part = block-table "
-                                   f"gather{_fp8_note(w)} + float64 attention per sequence"},
-        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "config": job_config(args.config, world, w),
+        "cpu_baseline": base,
+        "e2e": {"value": base["value"], "unit": UNIT, "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
+
+
+def job_config(name, world, w):
+    """``config`` of a dense configuration from its whole-job workload (product or oracle)."""
+    fp8 = getattr(w, "kv_format", None) == "fp8_e4m3" or \
+        getattr(w, "extra", {}).get("kv_format") == "fp8_e4m3"
+    row_stride = 544 if fp8 else 2 * w.width
+    return config_block(w.name, world, w.sequences, w.tokens, w.heads, w.width,
+                        w.pool_pages * 64 * row_stride)
 
 
 # ------------------------------------------------------------------------- our arm
@@ -669,8 +774,7 @@ def run_ours(args, world, rank, local_rank):
 
     # ---- device-resident timing
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    clock = ClockSampler(local_rank, str(ROOT / "gpurun_out" / f"clocks_rank{rank}.csv")) \
-        if (ROOT / "gpurun_out").exists() else ClockSampler(local_rank, f"/tmp/clocks{rank}.csv")
+    clock = ClockSampler(local_rank, clock_log_path(args, rank))
     barrier()
     torch.cuda.synchronize(dev)
     with clock:
@@ -818,7 +922,7 @@ def run_ours(args, world, rank, local_rank):
         "device_error_flags": err,
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        result["cpu_baseline"] = cpu_baseline(args.config, world, args.cpu_sample)
+        result["cpu_baseline"] = cpu_baseline(args.config, world)
     if rank == 0:
         print(json.dumps(result), flush=True)
 
@@ -832,9 +936,9 @@ def main():
     ap.add_argument("--config", default="decode",
                     choices=["decode", "decode_fp8", "mtp", "prefill", "longctx", "cpu",
                              "kv_write", "kv_write_fp8", "sparse", "sparse_fp8"])
-    ap.add_argument("--cpu-sample", type=int, default=None,
-                    help="sequences in the CPU baseline sample (default: up to 64)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--clock-log", default=None,
+                    help="file for the nvidia-smi clock samples ({rank} is replaced)")
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))

@@ -118,3 +118,91 @@ def kv_pool(seed: int, kv_len, page_table, pool_pages: int, width: int) -> np.nd
 
 def queries(seed: int, tokens: int, heads: int, width: int) -> np.ndarray:
     return normal_bf16(seed, STREAM_Q, 0, tokens * heads * width).reshape(tokens, heads, width)
+
+
+class Workload:
+    """Host metadata of one seeded configuration, restated without the product library.
+
+    Mirrors the product's workload table (lengths, query counts, prefixes, page tables) so the
+    CPU legs of the benchmark and the tests can rebuild a batch from the seed alone.
+    """
+
+    def __init__(self, name, seed, heads, width, kv_len, q_per_seq, prefix, scale,
+                 pool_pages=None, kv_format="bf16"):
+        self.name, self.seed, self.heads, self.width = name, seed, heads, width
+        self.kv_len = np.asarray(kv_len, dtype=np.int64)
+        self.q_per_seq = np.asarray(q_per_seq, dtype=np.int64)
+        self.prefix = np.asarray(prefix, dtype=np.int64)
+        self.scale = float(scale)
+        self.kv_format = kv_format
+        self.page_table, self.pool_pages = page_tables(seed, self.kv_len, pool_pages)
+        self.token_start = np.concatenate([[0], np.cumsum(self.q_per_seq)[:-1]]).astype(np.int64)
+        self.tok_off = np.concatenate([[0], np.cumsum(self.kv_len)[:-1]]).astype(np.int64)
+
+    @property
+    def sequences(self):
+        return len(self.kv_len)
+
+    @property
+    def tokens(self):
+        return int(self.q_per_seq.sum())
+
+    def seq_id(self):
+        return np.repeat(np.arange(self.sequences), self.q_per_seq).astype(np.int32)
+
+    def q_pos(self):
+        if not self.sequences:
+            return np.zeros(0, np.int32)
+        return np.concatenate([self.prefix[b] + np.arange(self.q_per_seq[b])
+                               for b in range(self.sequences)]).astype(np.int32)
+
+    def sequence_rows(self, b):
+        """Float64 cache rows ``[kv_len[b], width]`` of sequence ``b`` (bf16 values)."""
+        n = int(self.kv_len[b])
+        return bf16_to_f64(normal_bf16(self.seed, STREAM_KV, int(self.tok_off[b]) * self.width,
+                                       n * self.width)).reshape(n, self.width)
+
+    def sequence_queries(self, b):
+        """Float64 queries ``[q_per_seq[b], heads, width]`` of sequence ``b`` (bf16 values)."""
+        t = int(self.q_per_seq[b])
+        per = self.heads * self.width
+        return bf16_to_f64(normal_bf16(self.seed, STREAM_Q, int(self.token_start[b]) * per,
+                                       t * per)).reshape(t, self.heads, self.width)
+
+
+def config(name, batch=None):
+    """The five seeded configurations (and the FP8 decode batch), metadata only.
+
+    ``cpu``: 4 x 1 token, 16 heads, lengths {17, 64, 200, 1000}, a 64-page pool, seed 0.
+    ``decode`` / ``decode_fp8``: 64 x 1 token, 128 heads, lengths U[4096, 8192], seed 1.
+    ``prefill``: 8 x 2048 new tokens over prefixes U[0, 6144] (stream 5), seed 2.
+    ``longctx``: 4 x 1 token over 131072 cached rows, seed 3.
+    ``mtp``: 512 x 2 tokens, lengths lognormal(median 8192, sigma 1) clipped to [256, 65536],
+    seed 4.
+    """
+    scale = 1.0 / np.sqrt(192.0)
+    if name == "cpu":
+        kv = np.array([17, 64, 200, 1000], dtype=np.int64)
+        return Workload("cpu_decode_h16", 0, 16, 576, kv, np.ones(4), kv - 1, scale, 64)
+    if name in ("decode", "decode_fp8"):
+        b = 64 if batch is None else batch
+        kv = bounded(1, STREAM_LEN, b, 4096, 8192)
+        if name == "decode_fp8":
+            return Workload("decode_fp8_b64_h128_ctx4k-8k", 1, 128, 512, kv, np.ones(b), kv - 1,
+                            0.0625, kv_format="fp8_e4m3")
+        return Workload("decode_b64_h128_ctx4k-8k", 1, 128, 576, kv, np.ones(b), kv - 1, scale)
+    if name == "prefill":
+        b = 8 if batch is None else batch
+        pre = bounded(2, STREAM_PREFIX, b, 0, 6144)
+        return Workload("prefill_8x2048_prefix0-6k_h128", 2, 128, 576, pre + 2048,
+                        np.full(b, 2048), pre, scale)
+    if name == "longctx":
+        b = 4 if batch is None else batch
+        kv = np.full(b, 131072, dtype=np.int64)
+        return Workload("longctx_b4_131072_h128", 3, 128, 576, kv, np.ones(b), kv - 1, scale)
+    if name == "mtp":
+        b = 512 if batch is None else batch
+        kv = lognormal_lengths(4, b, 8192.0, 1.0, 256, 65536)
+        return Workload("mtp_512x2_lognormal8k_h128", 4, 128, 576, kv, np.full(b, 2), kv - 2,
+                        scale)
+    raise KeyError(name)
