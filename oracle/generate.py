@@ -196,6 +196,11 @@ def config(name, batch=None):
         pre = bounded(2, STREAM_PREFIX, b, 0, 6144)
         return Workload("prefill_8x2048_prefix0-6k_h128", 2, 128, 576, pre + 2048,
                         np.full(b, 2048), pre, scale)
+    if name in ("sparse", "sparse_fp8"):
+        b = 64 if batch is None else batch
+        kv = np.full(b, 32768, dtype=np.int64)
+        return Workload(f"{name}_b{b}_h32_ctx32k_k2048", 1, 32, 512, kv, np.ones(b), kv - 1,
+                        0.0625, kv_format="fp8_e4m3" if name == "sparse_fp8" else "bf16")
     if name == "longctx":
         b = 4 if batch is None else batch
         kv = np.full(b, 131072, dtype=np.int64)

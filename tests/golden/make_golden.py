@@ -76,8 +76,9 @@ def upstream_cases(ref: Path):
         data = json.loads(path.read_text())
         for case in data["cases"]:
             dims = case["dims"]
+            w_kv_b = _array(case["inputs"]["kv_b_proj_weight"]).astype(np.float64)
             w_uk, w_uv = mla_attention.split_kv_b(
-                _array(case["inputs"]["kv_b_proj_weight"]).astype(np.float64),
+                w_kv_b,
                 num_heads=dims["num_heads"],
                 qk_nope_head_dim=dims["qk_nope_head_dim"],
                 v_head_dim=dims["v_head_dim"],
@@ -93,6 +94,12 @@ def upstream_cases(ref: Path):
                 out[f"{key}__latent"] = np.ascontiguousarray(latent[b, 0])
                 out[f"{key}__w_uk"] = w_uk
                 out[f"{key}__w_uv"] = w_uv
+                # The packed weight and its head dims, for checking the oracle's split_kv_b
+                # against the reference's split of the same weight (w_uk, w_uv above).
+                out[f"{key}__w_kv_b"] = w_kv_b
+                out[f"{key}__kv_b_dims"] = np.array([dims["num_heads"],
+                                                     dims["qk_nope_head_dim"],
+                                                     dims["v_head_dim"]])
                 out[f"{key}__mask"] = np.ascontiguousarray(mask[b, 0])
                 out[f"{key}__scale"] = np.array(scale)
                 out[f"{key}__expected"] = np.ascontiguousarray(expected[b])
@@ -220,7 +227,9 @@ def sparse_cases(ref: Path):
 
 
 if __name__ == "__main__":
-    reference = Path(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) != 2:
+        raise SystemExit("usage: python tests/golden/make_golden.py <reference checkout>")
+    reference = Path(sys.argv[1])
     copy_philox(reference)
     upstream_cases(reference)
     paged_cases(reference)

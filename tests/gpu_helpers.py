@@ -62,3 +62,27 @@ def oracle_inputs_match(b, w):
     pool_bits = kv.reshape(-1, w.width).view(torch.int16).cpu().numpy().view(np.uint16)
     ref_pool = ogen.kv_pool(w.seed, w.kv_len, w.extra["page_table"], w.pool_pages, w.width)
     return np.array_equal(q_bits, ref_q), np.array_equal(pool_bits, ref_pool)
+
+
+def oracle_tokens(b, w, tokens):
+    """Oracle ``(out, lse)`` for the selected query ``tokens`` from the device inputs the kernel
+    read: each sequence's cached rows are gathered on the device through its page table once,
+    widened to float64 on the host, and the token sees its first ``min(kv_len, q_pos + 1)``."""
+    table = w.extra["page_table"]
+    seq, qpos = w.seq_id(), w.q_pos()
+    dev = b.q.device
+    order = sorted(int(t) for t in tokens)
+    rows_of, cur = None, None
+    out = np.zeros((len(order), w.heads, 512))
+    lse = np.full((len(order), w.heads), -np.inf)
+    for i, t in enumerate(order):
+        s = int(seq[t])
+        if s != cur:
+            n_all = int(w.kv_len[s])
+            pages = torch.from_numpy(table[s, : (n_all + 63) // 64].astype(np.int64)).to(dev)
+            rows_of = b.kv[pages].reshape(-1, b.kv.shape[-1])[:n_all].double().cpu().numpy()
+            cur = s
+        n = max(0, min(int(w.kv_len[s]), int(qpos[t]) + 1))
+        q = b.q[t].double().cpu().numpy()
+        out[i], lse[i] = omla.identity_core(q, rows_of[:n], w.scale, 512)
+    return order, out, lse

@@ -12,7 +12,8 @@ from oracle import generate as ogen
 from tq_mla import inputs
 
 
-@pytest.mark.parametrize("name", ["cpu", "decode", "decode_fp8", "prefill", "longctx", "mtp"])
+@pytest.mark.parametrize("name", ["cpu", "decode", "decode_fp8", "prefill", "longctx", "mtp",
+                                  "sparse", "sparse_fp8"])
 def test_oracle_workload_metadata_matches_the_product(name):
     """The oracle's restated workload table gives the product's metadata bit for bit."""
     a, b = ogen.config(name), inputs.config(name)

@@ -48,6 +48,24 @@ def test_core_matches_upstream_transformers_fixtures():
                     assert _rel_l2(out[t, h], exp[t, h]) <= 1e-12, (key, t, h)
 
 
+def test_split_kv_b_matches_the_reference_split_of_the_fixture_weights():
+    """The oracle's split of each fixture's packed kv_b weight equals the reference's split
+    (w_uk, w_uv stored by make_golden.py from reference/src/tq_reference/mla_attention.py:87-107),
+    and the packing checks of :95-101 reject a wrong row count."""
+    g = np.load(GOLDEN / "mla_upstream.npz")
+    keys = sorted(k[: -len("__w_kv_b")] for k in g.keys() if k.endswith("__w_kv_b"))
+    assert len(keys) >= 5
+    for key in keys:
+        heads, dn, dv = (int(x) for x in g[f"{key}__kv_b_dims"])
+        w_uk, w_uv = omla.split_kv_b(g[f"{key}__w_kv_b"], num_heads=heads, qk_nope_head_dim=dn,
+                                     v_head_dim=dv)
+        np.testing.assert_array_equal(w_uk, g[f"{key}__w_uk"], err_msg=key)
+        np.testing.assert_array_equal(w_uv, g[f"{key}__w_uv"], err_msg=key)
+        with pytest.raises(omla.MlaError):
+            omla.split_kv_b(g[f"{key}__w_kv_b"][:-1], num_heads=heads, qk_nope_head_dim=dn,
+                            v_head_dim=dv)
+
+
 def test_identity_core_equals_general_core_with_identity_weights():
     rng = np.random.default_rng(0)
     h, d, n = 4, 576, 37
