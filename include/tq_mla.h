@@ -14,6 +14,10 @@
  *                            mla_attention.py:135-169
  *   tq_mla_prefill           SMLA-PF launcher           docs/TEST-PLAN.md:410-413 (planned)
  *   tq_mla_combine           split-K merge              docs/TEST-PLAN.md:206-207,220,247
+ *   tq_comm_*                the planned NCCL Comm      docs/ARCHITECTURE.md:136-137, lifecycle
+ *                            (per GPU worker)           :242-254 (abort, never reuse a failed one)
+ *   tq_mla_context_merge     decode context parallelism docs/ARCHITECTURE.md:240-241,313 (planned
+ *                            "later option"): all-gather of per-device partials + LSE merge
  *   tq_philox_words          tq_testkit::philox::fill_words crates/tq-testkit/src/philox.rs:78-98
  *   tq_philox_block          tq_testkit::philox::block      crates/tq-testkit/src/philox.rs:57-70
  *   tq_philox_uniform_f32    tq_testkit::philox::uniform_f32 crates/tq-testkit/src/philox.rs:109-111
@@ -48,7 +52,9 @@ enum {
   TQ_ERR_WORKSPACE = 102,        /* workspace missing, misaligned or too small           */
   TQ_ERR_CUDA = 103,             /* a CUDA runtime/driver call failed                    */
   TQ_ERR_PARAMS = 104,           /* params not produced by a validate call, or altered   */
-  TQ_ERR_RANGE = 105             /* Philox word range exceeds u64 (philox.md:69-75)      */
+  TQ_ERR_RANGE = 105,            /* Philox word range exceeds u64 (philox.md:69-75)      */
+  TQ_ERR_COMM = 106              /* NCCL missing, or a collective failed: the communicator
+                                    is unusable from then on; abort it and make a new one  */
 };
 
 /* Device error flag bits, read back with tq_mla_read_device_error. */
@@ -172,6 +178,42 @@ int32_t tq_mla_decode(const TqMlaParams* params, void* workspace, uint64_t works
 int32_t tq_mla_prefill(const TqMlaParams* params, void* workspace, uint64_t workspace_bytes,
                        void* stream, TqContractError* err);
 int32_t tq_mla_combine(const TqCombineParams* params, void* stream);
+
+/* Communicator of one rank of a multi-GPU job (an NCCL communicator, one per GPU worker; NCCL
+ * is loaded at run time as libnccl.so.2, so the library has no link-time NCCL dependency and
+ * shares the NCCL already loaded into the process, if any).
+ *   tq_comm_unique_id   on one rank; the caller sends the 128 bytes to every rank (host side)
+ *   tq_comm_init        on every rank, with its GPU current; collective over all ranks
+ *   tq_comm_abort       after a failed or timed-out collective (TQ_ERR_COMM): frees it at once
+ *   tq_comm_destroy     normal teardown; destroy CUDA graphs holding its collectives first
+ * A communicator that reported TQ_ERR_COMM refuses further collectives (TQ_ERR_COMM). */
+typedef struct { char internal[128]; } TqCommId;
+typedef struct TqComm TqComm;
+int32_t tq_comm_unique_id(TqCommId* id);
+int32_t tq_comm_init(const TqCommId* id, int32_t nranks, int32_t rank, TqComm** comm);
+int32_t tq_comm_abort(TqComm* comm);
+int32_t tq_comm_destroy(TqComm* comm);
+int32_t tq_comm_rank(const TqComm* comm, int32_t* rank, int32_t* nranks);
+
+/* Cross-device merge of a context split: each of the G ranks holds the partial result of the
+ * same T query tokens over its own page range (f32 out normalised over that range and its
+ * natural-log lse, e.g. a tq_mla_decode with f32 out). The partials of all ranks are
+ * all-gathered into gather_out f32 [G, T, H, 512] and gather_lse f32 [G, T, H] (caller-owned,
+ * packed, at least gather_*_bytes long), then merged by log-sum-exp into out (bf16 or f32
+ * [T, H, 512], padded outer strides allowed) and lse f32 [T, H] on every rank, as
+ * tq_mla_combine does. part_out and part_lse are packed [T, H, 512] / [T, H]. Every rank makes
+ * the same call with the same T and H, in the same order as its other collectives on `comm`.
+ * Device addresses and strides must be 16-byte aligned. */
+typedef struct {
+  uint64_t tokens, heads;
+  uint64_t part_out, part_lse;              /* this rank's partials (device)       */
+  uint64_t gather_out, gather_lse;          /* receive buffers (device)            */
+  uint64_t gather_out_bytes, gather_lse_bytes;
+  uint64_t out, lse;                        /* merged result (device)              */
+  uint64_t out_stride_token, out_stride_head; /* bytes                             */
+  int32_t out_dtype;
+} TqContextMergeParams;
+int32_t tq_mla_context_merge(const TqContextMergeParams* params, TqComm* comm, void* stream);
 
 /* Device error flag of the last launch that used `workspace` (synchronises `stream`). */
 int32_t tq_mla_read_device_error(const void* workspace, void* stream, int32_t* flags);

@@ -432,6 +432,7 @@ const char* tq_mla_status_string(int32_t status) {
     case TQ_ERR_CUDA: return "CUDA error";
     case TQ_ERR_PARAMS: return "params not produced by validation";
     case TQ_ERR_RANGE: return "word range exceeds u64";
+    case TQ_ERR_COMM: return "NCCL unavailable or a collective failed";
     default: return "unknown status";
   }
 }

@@ -18,7 +18,7 @@ STATUS = {
     0: "ok", 1: "Shape", 2: "Dtype", 3: "Dimension", 4: "Stride", 5: "Alignment", 6: "Address",
     7: "Capacity", 8: "Overflow", 9: "QueryCount", 10: "Scale", 11: "Group", 12: "Alias",
     100: "InvalidArgument", 101: "Unsupported", 102: "Workspace", 103: "Cuda", 104: "Params",
-    105: "Range",
+    105: "Range", 106: "Comm",
 }
 DEV_WAIT_TIMEOUT, DEV_PAGE_RANGE, DEV_SEQ_RANGE, DEV_TABLE_SHORT, DEV_WORK_OVERFLOW = 1, 2, 4, 8, 16
 
@@ -72,6 +72,17 @@ class TqCombineParams(ctypes.Structure):
     ]
 
 
+class TqCommId(ctypes.Structure):
+    _fields_ = [("internal", ctypes.c_char * 128)]
+
+
+class TqContextMergeParams(ctypes.Structure):
+    _fields_ = [(name, ctypes.c_uint64) for name in (
+        "tokens", "heads", "part_out", "part_lse", "gather_out", "gather_lse", "gather_out_bytes",
+        "gather_lse_bytes", "out", "lse", "out_stride_token", "out_stride_head")] + [
+        ("out_dtype", ctypes.c_int32)]
+
+
 class TqWorkspaceLayout(ctypes.Structure):
     _fields_ = [(name, ctypes.c_uint64) for name in (
         "total_bytes", "header", "unit_n", "unit_pages", "unit_gstart", "unit_first",
@@ -102,6 +113,12 @@ PROTOTYPES = {
     "tq_mla_prefill": (_I32, [_P(TqMlaParams), _VP, _U64, _VP, _P(TqContractError)]),
     "tq_mla_combine": (_I32, [_P(TqCombineParams), _VP]),
     "tq_mla_read_device_error": (_I32, [_VP, _VP, _P(_I32)]),
+    "tq_comm_unique_id": (_I32, [_P(TqCommId)]),
+    "tq_comm_init": (_I32, [_P(TqCommId), _I32, _I32, _P(_VP)]),
+    "tq_comm_abort": (_I32, [_VP]),
+    "tq_comm_destroy": (_I32, [_VP]),
+    "tq_comm_rank": (_I32, [_VP, _P(_I32), _P(_I32)]),
+    "tq_mla_context_merge": (_I32, [_P(TqContextMergeParams), _VP, _VP]),
     "tq_mla_set_kernel_timer": (_I32, [_VP, _VP]),
     "tq_mla_decode_no_alloc": (_I32, [_P(TqMlaParams), _VP, _P(TqContractError)]),
     "tq_kv_write_validate": (_I32, [_P(TqKvWriteSpec), _P(TqContractError)]),

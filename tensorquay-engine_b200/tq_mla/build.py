@@ -8,7 +8,7 @@ from pathlib import Path
 
 PKG = Path(__file__).resolve().parent
 CSRC = PKG.parent / "csrc"
-SOURCES = ["tq_mla_kernels.cu", "tq_kv_write.cu", "tq_contracts.cpp"]
+SOURCES = ["tq_mla_kernels.cu", "tq_kv_write.cu", "tq_contracts.cpp", "tq_comm.cpp"]
 HEADERS = ["tq_ptx.cuh", "tq_mla_layout.h", "tq_contracts.h"]
 TARGET = PKG / "libtq_mla.so"
 NVCC_FLAGS = [
@@ -37,7 +37,7 @@ def up_to_date():
 def build(force=False, verbose=False):
     if not force and up_to_date():
         return TARGET
-    cmd = [nvcc(), *NVCC_FLAGS, "-o", str(TARGET), *[str(CSRC / s) for s in SOURCES]]
+    cmd = [nvcc(), *NVCC_FLAGS, "-o", str(TARGET), *[str(CSRC / s) for s in SOURCES], "-ldl"]
     if verbose:
         cmd.insert(1, "-Xptxas=-v")
         print(" ".join(cmd))

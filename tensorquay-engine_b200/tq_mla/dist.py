@@ -4,13 +4,19 @@ Two strategies, one process per GPU:
   - request sharding (``inputs.shard``): whole sequences are assigned to devices by token count;
     each device owns the pages of its sequences and runs the kernel on them; no collective is
     on the data path.
-  - context split (``context_split`` + ``gather_merge``): for very long single-token decodes,
+  - context split (``context_split`` + ``context_merge``): for very long single-token decodes,
     every device holds a contiguous, page-aligned range of each sequence's positions and
     computes a partial result (f32 output normalised over its range, natural-log lse); the
-    partials are all-gathered (``torch.distributed`` over NCCL) and merged by log-sum-exp with
-    ``tq_mla_combine``. The reference plans this as decode context parallelism
-    (docs/ARCHITECTURE.md:240-241,313).
+    library's ``tq_mla_context_merge`` all-gathers the partials over its own NCCL communicator
+    and merges them by log-sum-exp on every device. The reference plans this as decode context
+    parallelism (docs/ARCHITECTURE.md:240-241,313) behind a per-worker ``Comm``
+    (docs/ARCHITECTURE.md:136-137, lifecycle :242-254).
+Python only sets things up: it carries the communicator's 128-byte id from rank 0 to the other
+ranks (any ``torch.distributed`` group, gloo included) and holds the device buffers; the
+collective and the merge run in libtq_mla.so.
 """
+
+import ctypes
 
 import numpy as np
 
@@ -50,24 +56,98 @@ def context_split(w: inputs.Workload, world: int, rank: int) -> inputs.Workload:
     return inputs._finish(sub)
 
 
-def gather_merge(part_out, part_lse, group=None, out=None, lse=None):
-    """All-gather per-device partials (``f32 [T,H,512]``, ``f32 [T,H]``) and merge them.
+class Comm:
+    """This rank's communicator (``tq_comm_*``): an NCCL communicator over the GPUs of the job.
 
-    On GPUs the merge runs in ``tq_mla_combine``; on CPU tensors (gloo) it is left to the caller
-    (returns the gathered stacks), since there is no CPU compute path.
+    Created collectively by every rank with its GPU current. A communicator whose collective
+    failed (``TqError`` with status 106) must be aborted (``abort``) and never reused.
     """
+
+    def __init__(self, comm_id: bytes, world: int, rank: int):
+        from . import _abi
+
+        cid = _abi.TqCommId()
+        ctypes.memmove(ctypes.addressof(cid), comm_id, 128)
+        handle = ctypes.c_void_p()
+        _abi.raise_for(_abi.lib.tq_comm_init(ctypes.byref(cid), world, rank, ctypes.byref(handle)))
+        self.handle, self.world, self.rank = handle, world, rank
+        self._gather = {}
+
+    @staticmethod
+    def new_id() -> bytes:
+        from . import _abi
+
+        cid = _abi.TqCommId()
+        _abi.raise_for(_abi.lib.tq_comm_unique_id(ctypes.byref(cid)))
+        return ctypes.string_at(ctypes.addressof(cid), 128)
+
+    @classmethod
+    def from_process_group(cls, group=None):
+        """All ranks of ``group`` call this; rank 0's id reaches the others through the group."""
+        import torch.distributed as dist
+
+        rank, world = dist.get_rank(group), dist.get_world_size(group)
+        box = [cls.new_id() if rank == 0 else None]
+        dist.broadcast_object_list(box, src=0, group=group)
+        return cls(box[0], world, rank)
+
+    def destroy(self):
+        from . import _abi
+
+        if self.handle:
+            self._gather.clear()
+            st = _abi.lib.tq_comm_destroy(self.handle)
+            self.handle = None
+            _abi.raise_for(st)
+
+    def abort(self):
+        from . import _abi
+
+        if self.handle:
+            self._gather.clear()
+            st = _abi.lib.tq_comm_abort(self.handle)
+            self.handle = None
+            _abi.raise_for(st)
+
+    def gather_buffers(self, tokens, heads, device):
+        import torch
+
+        key = (tokens, heads, str(device))
+        if key not in self._gather:
+            self._gather[key] = (
+                torch.empty((self.world, tokens, heads, 512), dtype=torch.float32, device=device),
+                torch.empty((self.world, tokens, heads), dtype=torch.float32, device=device))
+        return self._gather[key]
+
+
+def context_merge(comm: Comm, part_out, part_lse, out=None, lse=None, stream=None):
+    """Merge this rank's partial (``f32 [T,H,512]``, ``f32 [T,H]``) with every other rank's:
+    returns ``(out [T,H,512], lse [T,H])``, identical on all ranks. One call of
+    ``tq_mla_context_merge`` (NCCL all-gather, then the LSE merge kernel) on ``stream``."""
     import torch
-    import torch.distributed as dist
 
-    world = dist.get_world_size(group)
-    g_out = torch.empty((world, *part_out.shape), dtype=part_out.dtype, device=part_out.device)
-    g_lse = torch.empty((world, *part_lse.shape), dtype=part_lse.dtype, device=part_lse.device)
-    if part_out.is_cuda:
-        dist.all_gather_into_tensor(g_out, part_out.contiguous(), group=group)
-        dist.all_gather_into_tensor(g_lse, part_lse.contiguous(), group=group)
-        from .ops import combine_parts
+    from . import _abi
+    from .ops import _TORCH_DTYPE, _stream_handle
 
-        return combine_parts(g_out, g_lse, out=out, lse=lse)
-    dist.all_gather(list(g_out.unbind(0)), part_out.contiguous(), group=group)
-    dist.all_gather(list(g_lse.unbind(0)), part_lse.contiguous(), group=group)
-    return g_out, g_lse
+    t, h, d = part_out.shape
+    if d != 512 or part_out.dtype != torch.float32 or part_lse.shape != (t, h):
+        raise ValueError("partials must be f32 [T, H, 512] and f32 [T, H]")
+    part_out, part_lse = part_out.contiguous(), part_lse.contiguous()
+    if out is None:
+        out = torch.empty((t, h, 512), dtype=torch.bfloat16, device=part_out.device)
+    if lse is None:
+        lse = torch.empty((t, h), dtype=torch.float32, device=part_out.device)
+    g_out, g_lse = comm.gather_buffers(t, h, part_out.device)
+    p = _abi.TqContextMergeParams()
+    p.tokens, p.heads = t, h
+    p.part_out, p.part_lse = part_out.data_ptr(), part_lse.data_ptr()
+    p.gather_out, p.gather_lse = g_out.data_ptr(), g_lse.data_ptr()
+    p.gather_out_bytes = g_out.numel() * 4
+    p.gather_lse_bytes = g_lse.numel() * 4
+    p.out, p.lse = out.data_ptr(), lse.data_ptr()
+    p.out_stride_token = out.stride(0) * out.element_size()
+    p.out_stride_head = out.stride(1) * out.element_size()
+    p.out_dtype = _TORCH_DTYPE[out.dtype]
+    _abi.raise_for(_abi.lib.tq_mla_context_merge(ctypes.byref(p), comm.handle,
+                                                 _stream_handle(stream)))
+    return out, lse

@@ -47,6 +47,9 @@ STRUCTS = {
     "TqWorkspaceLayout": (_abi.TqWorkspaceLayout, ["total_bytes", "part_out", "sparse_rows",
                                                    "sparse_count", "pairs"]),
     "TqContractError": (_abi.TqContractError, ["field", "kind"]),
+    "TqCommId": (_abi.TqCommId, ["internal"]),
+    "TqContextMergeParams": (_abi.TqContextMergeParams, ["tokens", "gather_out_bytes", "out",
+                                                         "out_stride_head", "out_dtype"]),
     "TqKvWriteSpec": (_abi.TqKvWriteSpec, ["src", "kv", "page_table", "seq_id", "pos",
                                            "kv_format", "norm_weight", "norm_eps"]),
 }

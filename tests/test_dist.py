@@ -4,6 +4,7 @@
 - The context split of a long decode covers every position exactly once, page-aligned; each
   rank's partial (computed by the oracle) gathered over gloo and merged by log-sum-exp equals
   the single-device result.
+- The communicator id travels from rank 0 to every rank through a gloo group unchanged.
 """
 
 import os
@@ -81,8 +82,12 @@ def _rank_main(rank, world, port, result_path):
         q = ogen.bf16_to_f64(ogen.queries(full.seed, full.tokens, full.heads, 576))
         out, lse = omla.paged_attention(q, rows, part.extra["page_table"], part.seq_id(),
                                         part.q_pos(), part.kv_len, scale=part.scale)
-        g_out, g_lse = tdist.gather_merge(torch.from_numpy(out), torch.from_numpy(lse))
-        merged = omla.combine_partials(g_out.numpy(), g_lse.numpy())
+        # Host-side stand-in for the device all-gather: each rank's partial reaches every rank.
+        g_out = [torch.empty(out.shape, dtype=torch.float64) for _ in range(world)]
+        g_lse = [torch.empty(lse.shape, dtype=torch.float64) for _ in range(world)]
+        dist.all_gather(g_out, torch.from_numpy(out))
+        dist.all_gather(g_lse, torch.from_numpy(lse))
+        merged = omla.combine_partials(torch.stack(g_out).numpy(), torch.stack(g_lse).numpy())
         if rank == 0:
             np.savez(result_path, out=merged[0], lse=merged[1])
     finally:
@@ -103,3 +108,44 @@ def test_context_split_gather_merge_equals_single_device(tmp_path, world):
                                             scale=192 ** -0.5)
     np.testing.assert_allclose(got["out"], ref_out, rtol=0, atol=1e-12)
     np.testing.assert_allclose(got["lse"], ref_lse, rtol=0, atol=1e-12)
+
+
+def _id_rank_main(rank, world, port, result_path):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    import datetime
+
+    import torch.distributed as dist
+
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60))
+    try:
+        # The id that tdist.Comm.from_process_group sends (raw bytes, NUL bytes included).
+        box = [bytes(range(128)) if rank == 0 else None]
+        dist.broadcast_object_list(box, src=0)
+        assert box[0] == bytes(range(128))
+        if rank == world - 1:
+            open(result_path, "w").write("ok")
+    finally:
+        dist.destroy_process_group()
+
+
+def test_communicator_id_reaches_every_rank(tmp_path):
+    result = tmp_path / "id.txt"
+    tmp.start_processes(_id_rank_main, args=(2, _free_port(), str(result)), nprocs=2, join=True,
+                        start_method="spawn")
+    assert result.read_text() == "ok"
+
+
+def test_comm_entry_points_refuse_bad_arguments():
+    """Argument checks of the C entry points need no GPU and no NCCL."""
+    import ctypes
+
+    from tq_mla import _abi
+
+    assert _abi.lib.tq_comm_unique_id(None) == 100
+    cid = _abi.TqCommId()
+    h = ctypes.c_void_p()
+    assert _abi.lib.tq_comm_init(ctypes.byref(cid), 2, 2, ctypes.byref(h)) == 100
+    assert _abi.lib.tq_comm_init(ctypes.byref(cid), 0, 0, ctypes.byref(h)) == 100
+    assert _abi.lib.tq_mla_context_merge(None, None, None) == 100
+    assert _abi.lib.tq_comm_destroy(None) == 100 and _abi.lib.tq_comm_abort(None) == 100
