@@ -30,6 +30,7 @@ all host cores, on a bounded sample of the same workload, on rank 0 only.
 """
 
 import argparse
+import contextlib
 import json
 import math
 import multiprocessing as mp
@@ -65,21 +66,29 @@ SHARD_BASE = {"decode": 64, "decode_fp8": 64, "mtp": 512, "prefill": 8, "longctx
               "sparse": 64, "sparse_fp8": 64}
 
 
-def workload_for(name, world, rank):
+def job_batch(name, world, strong):
+    """Sequences of the whole job: the configuration's batch (one GPU, or strong scaling) or
+    N times it (weak scaling over N ranks)."""
+    return None if (world == 1 or strong or name == "cpu") else SHARD_BASE[name] * world
+
+
+def workload_for(name, world, rank, strong=False):
+    """This rank's share of the job: whole sequences, balanced by token count."""
     from tq_mla import inputs
 
-    if world == 1 or name == "cpu":
-        return inputs.config(name)
-    full = inputs.config(name, batch=SHARD_BASE[name] * world)
-    return inputs.shard(full, world, rank)
+    full = inputs.config(name, batch=job_batch(name, world, strong))
+    return full if world == 1 else inputs.shard(full, world, rank)
 
 
-def config_block(name, world, sequences, tokens, heads, width, pool_bytes, parallelism=None):
+def config_block(name, world, sequences, tokens, heads, width, pool_bytes, parallelism=None,
+                 strong=False):
     """The line's ``config``: the workload's fixed description (no measured values), the same
     for the GPU arm and the reference arm of one configuration and rank count. ``sequences``,
     ``tokens`` and ``pool_bytes`` are the whole job's."""
     return {
-        "workload": name if world == 1 else f"{name} x{world} ranks (token-sharded)",
+        "workload": name if world == 1 else (
+            f"{name} over {world} ranks (fixed batch)" if strong
+            else f"{name} x{world} ranks (token-sharded)"),
         "sequences": int(sequences), "query_tokens": int(tokens), "heads": int(heads),
         "row_width": int(width), "value_width": 512, "page_rows": 64,
         "parallelism": parallelism or f"sequence-shard x{world}",
@@ -254,13 +263,13 @@ class CpuTeam:
             p.join(timeout=30)
 
 
-def cpu_sample(name, world):
+def cpu_sample(name, world, strong=False):
     """The sequences a CPU step covers: the whole batch for the decode batches, else a fixed
     spread of sequences of the (unsharded) job, so a step stays within about a second."""
     sys.path.insert(0, str(ROOT))
     from oracle import generate as ogen
 
-    batch = None if world == 1 else SHARD_BASE[name] * world
+    batch = job_batch(name, world, strong)
     w = ogen.config(name, batch=batch)
     cap = {"decode": 64, "decode_fp8": 64, "cpu": 4, "mtp": 16, "prefill": 1,
            "longctx": 1}.get(name, 8)
@@ -308,10 +317,10 @@ def kv_format_of(w):
     return _abi.KV_FP8_E4M3 if w.extra.get("kv_format") == "fp8_e4m3" else None
 
 
-def cpu_measure(name, world, steps, warmup, single_seqs=8):
+def cpu_measure(name, world, steps, warmup, single_seqs=8, strong=False):
     """Times the CPU path: ``steps`` steps of the sample over one process per host core, plus
     one pass over a few of its sequences in a single process with default BLAS threads."""
-    w, batch, picks = cpu_sample(name, world)
+    w, batch, picks = cpu_sample(name, world, strong)
     cores = os.cpu_count() or 1
     team = CpuTeam(name, batch, picks, cores)
     try:
@@ -684,15 +693,16 @@ def run_reference(args, world, rank):
         return
     # Dense configurations: the oracle's float64 restatement of mla_attention_core over the same
     # seeded inputs, one spawned process per host core; no product library is loaded.
-    base = cpu_measure(args.config, world, steps=args.steps, warmup=args.warmup)
-    w, _, _ = cpu_sample(args.config, world)
+    strong = args.scaling == "strong"
+    base = cpu_measure(args.config, world, steps=args.steps, warmup=args.warmup, strong=strong)
+    w, _, _ = cpu_sample(args.config, world, strong)
     dtype = "f64" + (" (FP8 E4M3 rows decoded to f64)" if _fp8_note(w) else "")
     line = {
         "impl": "reference", "metric": METRIC, "value": base["value"], "unit": UNIT,
         "n_gpus": world, "steps": base["steps"], "warmup": base["warmup"],
         "ms_per_step": base["ms_per_step"], "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": dtype, "data": "synthetic",
-        "config": job_config(args.config, world, w),
+        "scaling": args.scaling, "vs_baseline": None, "dtype": dtype, "data": "synthetic",
+        "config": job_config(args.config, world, w, strong),
         "cpu_baseline": base,
         "e2e": {"value": base["value"], "unit": UNIT, "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
@@ -700,13 +710,18 @@ def run_reference(args, world, rank):
     print(json.dumps(line), flush=True)
 
 
-def job_config(name, world, w):
+def job_config(name, world, w, strong=False):
     """``config`` of a dense configuration from its whole-job workload (product or oracle)."""
     fp8 = getattr(w, "kv_format", None) == "fp8_e4m3" or \
         getattr(w, "extra", {}).get("kv_format") == "fp8_e4m3"
     row_stride = 544 if fp8 else 2 * w.width
+    par = None
+    if strong and world > 1:
+        par = (f"context split x{world} (each sequence's pages over the ranks, NCCL all-gather "
+               f"+ LSE merge)" if name == "longctx"
+               else f"sequence-shard x{world} of the fixed batch (token-balanced)")
     return config_block(w.name, world, w.sequences, w.tokens, w.heads, w.width,
-                        w.pool_pages * 64 * row_stride)
+                        w.pool_pages * 64 * row_stride, parallelism=par, strong=strong)
 
 
 # ------------------------------------------------------------------------- our arm
@@ -829,6 +844,32 @@ def traffic_from_profiles(workload_name):
     return None
 
 
+NATIVE_CONFIGS = ("decode", "prefill", "longctx", "mtp", "cpu")
+
+
+def native_binary():
+    """Path of the native benchmark binary (built next to libtq_mla.so), or None."""
+    path = ROOT / "tensorquay-engine_b200" / "tq_mla" / "tq_bench"
+    return path if path.exists() and os.access(path, os.X_OK) else None
+
+
+def run_native(args, world, rank, local_rank, strong, dump_path):
+    """Times the step with the native binary (C ABI only, no Python on the timed path) on this
+    rank's GPU and share of the job; returns its JSON result."""
+    cmd = [str(native_binary()), "--config", args.config, "--steps", str(args.steps),
+           "--warmup", str(args.warmup), "--world", str(world), "--rank", str(rank),
+           "--device", str(local_rank), "--graph", "--dump-out", dump_path]
+    if strong:
+        cmd.append("--strong")
+    env = dict(os.environ, CUDA_VISIBLE_DEVICES=os.environ.get("CUDA_VISIBLE_DEVICES", ""))
+    if not env["CUDA_VISIBLE_DEVICES"]:
+        env.pop("CUDA_VISIBLE_DEVICES")
+    r = subprocess.run(cmd, capture_output=True, text=True, timeout=900, env=env)
+    if r.returncode != 0:
+        raise SystemExit(f"tq_bench failed ({r.returncode}): {r.stderr[-2000:]}")
+    return json.loads(r.stdout.strip().splitlines()[-1])
+
+
 def run_ours(args, world, rank, local_rank):
     import torch
     import torch.distributed as dist
@@ -836,7 +877,24 @@ def run_ours(args, world, rank, local_rank):
 
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
-    w = workload_for(args.config, world, rank)
+    strong = args.scaling == "strong"
+    w = workload_for(args.config, world, rank, strong)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    # ---- the timed step, from the native binary (C ABI only) when it is built for this
+    # configuration: K steps back to back on this rank's GPU, bracketed by barriers.
+    native, dump = None, None
+    clock = ClockSampler(local_rank, clock_log_path(args, rank))
+    if native_binary() is not None and args.config in NATIVE_CONFIGS:
+        dump = os.path.join(tempfile.gettempdir(), f"tq_bench_out_rank{rank}_{os.getpid()}.bin")
+        barrier()
+        torch.cuda.synchronize(dev)
+        with clock:
+            native = run_native(args, world, rank, local_rank, strong, dump)
+        barrier()
     batch = inputs.materialize(w, dev)
     out = torch.empty((w.tokens, w.heads, 512), dtype=torch.bfloat16, device=dev)
     lse = torch.empty((w.tokens, w.heads), dtype=torch.float32, device=dev)
@@ -862,10 +920,6 @@ def run_ours(args, world, rank, local_rank):
     h2d = h_q.numel() * 2 + h_meta.numel() * 4
     d2h = h_out.numel() * 2 + h_lse.numel() * 4
 
-    def barrier():
-        if world > 1:
-            dist.barrier()
-
     def max_over_ranks(x):
         if world == 1:
             return x
@@ -885,12 +939,11 @@ def run_ours(args, world, rank, local_rank):
     torch.cuda.synchronize(dev)
     assert launch.device_error() == 0, "device error flag set during warm-up"
 
-    # ---- device-resident timing
+    # ---- device-resident timing through the Python front end (ctypes -> C ABI)
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    clock = ClockSampler(local_rank, clock_log_path(args, rank))
     barrier()
     torch.cuda.synchronize(dev)
-    with clock:
+    with (clock if native is None else contextlib.nullcontext()):
         ev0.record(stream)
         for _ in range(args.steps):
             launch(stream)
@@ -988,7 +1041,30 @@ def run_ours(args, world, rank, local_rank):
     # Parity of the timed output with the oracle (after every timed region; all ranks check
     # their own tokens, then the verdict is combined).
     check = self_check(w, batch, out, lse, fp8=kv_format_of(w) is not None)
-    ok_all = max_over_ranks(0.0 if (check["pass"] and e2e_same and err == 0) else 1.0) == 0.0
+    native_same = True
+    if native is not None:
+        # The binary's last output: bitwise equal to this front end's (same seeded inputs,
+        # deterministic kernels), hence also checked against the oracle above.
+        raw = np.fromfile(dump, dtype=np.uint8)
+        os.remove(dump)
+        n_out = out.numel() * 2
+        nat_out = torch.from_numpy(raw[:n_out].copy()).view(torch.bfloat16).view(out.shape)
+        nat_lse = torch.from_numpy(raw[n_out:].copy()).view(torch.float32).view(lse.shape)
+        native_same = bool(torch.equal(nat_out, out.cpu()) and torch.equal(nat_lse, lse.cpu()))
+        native_same = native_same and native["e2e"]["results_equal_resident_run"] and \
+            native["device_error_flags"] == 0
+        check["native_output_equal"] = native_same
+    ok_all = max_over_ranks(0.0 if (check["pass"] and e2e_same and err == 0 and native_same)
+                            else 1.0) == 0.0
+    py = {"ms_per_step": ms_step, "kernel_ms_per_launch": kernel_ms, "e2e_ms_per_step": e2e_ms,
+          "step_stats": stats}
+    if native is not None:
+        ms = max_over_ranks(native["ms_per_step"]) * args.steps
+        ms_step = ms / args.steps
+        kernel_ms = max_over_ranks(native["kernel_ms_per_launch"])
+        e2e_ms = max_over_ranks(native["e2e"]["ms_per_step"])
+        stats = native["step_stats"]
+        h2d, d2h = native["e2e"]["h2d_bytes_per_step"], native["e2e"]["d2h_bytes_per_step"]
 
     tokens_all = sum_over_ranks(float(w.tokens))
     flops_all = sum_over_ranks(w.flops())
@@ -1024,17 +1100,21 @@ def run_ours(args, world, rank, local_rank):
     result = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None,
+        "scaling": args.scaling, "vs_baseline": None,
         "dtype": "fp8_e4m3 rows, bf16 operands" if kv_format_of(w) is not None else "bf16",
         "data": "synthetic",
         "config": job_config(args.config, world, inputs.config(
-            args.config, batch=None if world == 1 else SHARD_BASE[args.config] * world)),
+            args.config, batch=job_batch(args.config, world, strong)), strong),
         "tflops_total": flops_all / (ms_step * 1e-3) / 1e12,
         "step_stats": stats,
+        "timed_by": ("tq_bench (native binary, C ABI only)" if native is not None
+                     else "bench.py through the C ABI (ctypes)"),
+        "graph_stats": native.get("graph_stats") if native is not None else None,
+        "python_front_end": py,
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": int(h2d),
                 "d2h_bytes_per_step": int(d2h), "ms_per_step": e2e_ms,
                 "pipeline": "copy-in, compute and copy-out streams, two buffer sets",
-                "results_equal_resident_run": bool(e2e_same),
+                "results_equal_resident_run": bool(e2e_same and native_same),
                 "host_link": link,
                 "ceiling_tokens_per_s": float(w.tokens) * world / (1e-3 * max(
                     link["both_ms"], ms_step))},
@@ -1053,6 +1133,171 @@ def run_ours(args, world, rank, local_rank):
                          f"(rank {rank}: {check}, e2e equal {e2e_same}, device flags {err})")
 
 
+def run_context(args, world, rank, local_rank):
+    """The long-context batch as configured: every sequence's 131072 cached positions are split
+    over the ranks by page range. Per step each rank decodes its range into f32 partials, then
+    ``tq_mla_context_merge`` (NCCL all-gather of the partials + the LSE merge kernel) leaves the
+    merged output on every rank. ``value`` = the batch's query tokens / the slowest rank's step
+    time (strong scaling: the work is fixed, the ranks share it)."""
+    import torch
+    import torch.distributed as dist
+    from tq_mla import dist as tdist, inputs, ops
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    full = inputs.config(args.config)
+    part = tdist.context_split(full, world, rank)
+    batch = inputs.materialize(part, dev)
+    T, H = part.tokens, part.heads
+    p_out = torch.empty((T, H, 512), dtype=torch.float32, device=dev)
+    p_lse = torch.empty((T, H), dtype=torch.float32, device=dev)
+    out = torch.empty((T, H, 512), dtype=torch.bfloat16, device=dev)
+    lse = torch.empty((T, H), dtype=torch.float32, device=dev)
+    launch = ops.MlaLaunch(batch.q, batch.kv, batch.page_table, batch.seq_id, batch.q_pos,
+                           batch.kv_len, p_out, p_lse, scale=part.scale,
+                           query_counts=batch.query_counts)
+    comm = tdist.Comm.from_process_group()
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        launch(stream)
+        tdist.context_merge(comm, p_out, p_lse, out, lse, stream)
+
+    def max_over_ranks(x):
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    try:
+        for _ in range(args.warmup):
+            step()
+        torch.cuda.synchronize(dev)
+        assert launch.device_error() == 0
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        clock = ClockSampler(local_rank, clock_log_path(args, rank))
+        dist.barrier()
+        torch.cuda.synchronize(dev)
+        with clock:
+            ev0.record(stream)
+            for _ in range(args.steps):
+                step()
+            ev1.record(stream)
+            torch.cuda.synchronize(dev)
+        dist.barrier()
+        ms_step = max_over_ranks(ev0.elapsed_time(ev1)) / args.steps
+        # The merge alone (all-gather + merge kernel), then the attention kernel alone.
+        dist.barrier()
+        torch.cuda.synchronize(dev)
+        ev0.record(stream)
+        for _ in range(args.steps):
+            tdist.context_merge(comm, p_out, p_lse, out, lse, stream)
+        ev1.record(stream)
+        torch.cuda.synchronize(dev)
+        merge_ms = max_over_ranks(ev0.elapsed_time(ev1)) / args.steps
+        k_steps = min(args.steps, 300)
+        kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+               for _ in range(k_steps)]
+        for b_, e_ in kev:
+            b_.record(stream)
+            e_.record(stream)
+        torch.cuda.synchronize(dev)
+        for b_, e_ in kev:
+            ops.set_kernel_timer(b_, e_)
+            launch(stream)
+        torch.cuda.synchronize(dev)
+        ops.set_kernel_timer()
+        kernel_ms = max_over_ranks(sum(b_.elapsed_time(e_) for b_, e_ in kev) / k_steps)
+        # End to end: the step's queries from pinned host memory on every rank, the merged
+        # output and lse back to the host, one stream.
+        h_q = batch.q.cpu().pin_memory()
+        h_out = torch.empty_like(out, device="cpu").pin_memory()
+        h_lse = torch.empty_like(lse, device="cpu").pin_memory()
+        dist.barrier()
+        torch.cuda.synchronize(dev)
+        ev0.record(stream)
+        for _ in range(args.steps):
+            batch.q.copy_(h_q, non_blocking=True)
+            step()
+            h_out.copy_(out, non_blocking=True)
+            h_lse.copy_(lse, non_blocking=True)
+        ev1.record(stream)
+        torch.cuda.synchronize(dev)
+        e2e_ms = max_over_ranks(ev0.elapsed_time(ev1)) / args.steps
+        err = launch.device_error()
+        # Parity: every rank's partial against the oracle of its own range; rank 0 merges the
+        # oracle partials of all ranks and compares the merged device output with that.
+        from oracle import mla as omla
+
+        step()
+        torch.cuda.synchronize(dev)
+        part_check = self_check(part, batch, p_out, p_lse, count=T)
+        table = part.extra["page_table"]
+        ref_o, ref_l = [], []
+        for t in range(T):
+            n = int(part.kv_len[t])
+            pages = torch.from_numpy(table[t, : (n + 63) // 64].astype(np.int64)).to(dev)
+            rows = batch.kv[pages].reshape(-1, batch.kv.shape[-1])[:n].double().cpu().numpy()
+            o, l_ = omla.identity_core(batch.q[t].double().cpu().numpy(), rows, part.scale, 512)
+            ref_o.append(o)
+            ref_l.append(l_)
+        gathered = [None] * world
+        dist.all_gather_object(gathered, (np.stack(ref_o), np.stack(ref_l)))
+        m_o, m_l = omla.combine_partials(np.stack([g[0] for g in gathered]),
+                                         np.stack([g[1] for g in gathered]))
+        go, gl = out.double().cpu().numpy(), lse.double().cpu().numpy()
+        merged_check = {
+            "out_max_abs": float(np.abs(go - m_o).max()),
+            "out_rel_l2": float(np.linalg.norm(go - m_o) / np.linalg.norm(m_o)),
+            "lse_max_abs": float(np.abs(gl - m_l).max()),
+        }
+        merged_check["pass"] = bool(merged_check["out_max_abs"] <= 2e-2 and
+                                    merged_check["out_rel_l2"] <= 1e-2 and
+                                    merged_check["lse_max_abs"] <= 1e-3)
+        ok_all = max_over_ranks(0.0 if (part_check["pass"] and merged_check["pass"] and
+                                        err == 0) else 1.0) == 0.0
+    finally:
+        comm.destroy()
+
+    hbm, tc_burst, tc_sus, src = peaks()
+    bytes_rank, flops_rank = part.bytes(), part.flops()
+    ach = bytes_rank / (kernel_ms * 1e-3) / 1e9
+    tokens = full.tokens
+    gather_bytes = (world - 1) * T * H * (512 + 1) * 4
+    result = {
+        "metric": METRIC, "value": tokens / (ms_step * 1e-3), "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic",
+        "config": job_config(args.config, world, full, strong=True),
+        "e2e": {"value": tokens / (e2e_ms * 1e-3), "unit": UNIT,
+                "h2d_bytes_per_step": int(h_q.numel() * 2),
+                "d2h_bytes_per_step": int(h_out.numel() * 2 + h_lse.numel() * 4),
+                "ms_per_step": e2e_ms, "per_rank": "each rank copies the queries in and the "
+                                                 "merged result out"},
+        "gpu_launches": (LAUNCHES_PER_STEP + 1) * args.steps,
+        "merge": {"ms": merge_ms, "received_bytes_per_rank": gather_bytes,
+                  "what": "tq_mla_context_merge: NCCL all-gather of f32 partials + lse, then "
+                          "the LSE merge kernel", "kernel_ms": kernel_ms},
+        "roofline": {"bound": "hbm", "achieved": ach, "peak": hbm, "unit": "GB/s",
+                     "frac": ach / hbm, "traffic": None, "kernel": "mla_paged_kernel",
+                     "kernel_ms_per_launch": kernel_ms,
+                     "peak_source": f"{src} (MEASURED_PEAKS.json)",
+                     "algorithmic_bytes_per_launch": bytes_rank,
+                     "flops_per_launch": flops_rank,
+                     "tflops": flops_rank / (kernel_ms * 1e-3) / 1e12,
+                     "step_roofline_frac": max(full.bytes() / (hbm * 1e9),
+                                               full.flops() / (tc_burst * 1e12))
+                     / world / (ms_step * 1e-3)},
+        "clocks": clock.summary(),
+        "device_error_flags": err,
+        "self_check": {"partial": part_check, "merged": merged_check},
+    }
+    if rank == 0:
+        print(json.dumps(result), flush=True)
+    if not ok_all:
+        raise SystemExit(f"self-check failed on rank {rank}: {result['self_check']}")
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -1062,6 +1307,10 @@ def main():
     ap.add_argument("--config", default="decode",
                     choices=["decode", "decode_fp8", "mtp", "prefill", "longctx", "cpu",
                              "kv_write", "kv_write_fp8", "sparse", "sparse_fp8"])
+    ap.add_argument("--scaling", choices=["weak", "strong"], default="weak",
+                    help="weak: N ranks hold N times the one-GPU batch; strong: the batch stays "
+                         "fixed and is shared (longctx: each sequence's pages split over the "
+                         "ranks, merged over NCCL)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--clock-log", default=None,
                     help="file for the nvidia-smi clock samples ({rank} is replaced)")
@@ -1086,6 +1335,8 @@ def main():
             run_writer(args, world, rank, local_rank)
         elif args.config.startswith("sparse"):
             run_sparse(args, world, rank, local_rank)
+        elif args.config == "longctx" and args.scaling == "strong" and world > 1:
+            run_context(args, world, rank, local_rank)
         else:
             run_ours(args, world, rank, local_rank)
     finally:

@@ -34,14 +34,31 @@ def up_to_date():
     return all(d.stat().st_mtime <= built for d in deps)
 
 
-def build(force=False, verbose=False):
-    if not force and up_to_date():
-        return TARGET
-    cmd = [nvcc(), *NVCC_FLAGS, "-o", str(TARGET), *[str(CSRC / s) for s in SOURCES], "-ldl"]
-    if verbose:
-        cmd.insert(1, "-Xptxas=-v")
-        print(" ".join(cmd))
+BENCH = PKG / "tq_bench"
+BENCH_SOURCE = CSRC / "tq_bench.cpp"
+
+
+def build_bench(force=False):
+    """The native benchmark binary: links libtq_mla.so (found next to it) and the CUDA runtime."""
+    deps = [BENCH_SOURCE, PKG.parent.parent / "include" / "tq_mla.h", TARGET]
+    if not force and BENCH.exists() and all(d.stat().st_mtime <= BENCH.stat().st_mtime
+                                            for d in deps):
+        return BENCH
+    cmd = [nvcc(), "-O2", "-std=c++17", "-Wno-deprecated-gpu-targets", "-Xcompiler", "-O2", "-o",
+           str(BENCH), str(BENCH_SOURCE),
+           f"-L{PKG}", "-ltq_mla", "-Xlinker", "-rpath,$ORIGIN"]
     subprocess.run(cmd, check=True)
+    return BENCH
+
+
+def build(force=False, verbose=False):
+    if force or not up_to_date():
+        cmd = [nvcc(), *NVCC_FLAGS, "-o", str(TARGET), *[str(CSRC / s) for s in SOURCES], "-ldl"]
+        if verbose:
+            cmd.insert(1, "-Xptxas=-v")
+            print(" ".join(cmd))
+        subprocess.run(cmd, check=True)
+    build_bench(force=force)
     return TARGET
 
 
