@@ -224,13 +224,18 @@ int32_t tq_mla_read_device_error(const void* workspace, void* stream, int32_t* f
  * Same plan, inputs, outputs and results as tq_mla_decode, but the workspace is a fixed array
  * inside this library of TQ_MLA_NO_ALLOC_WORKSPACE_BYTES (42 MiB), which every GPU that loads the
  * library keeps until the process exits. A plan whose tq_mla_workspace_bytes exceeds that size
- * returns TQ_ERR_WORKSPACE with field "no_alloc_workspace" (on a B200 that means more than about
- * 160 000 query tokens). The first call on each device looks up the array's device address, so
- * make it before capturing any stream. All calls share the one array: calls that may overlap on
- * the GPU (other streams, other threads) race and must be serialised by the caller. Device error
- * flags of these calls cannot be read back (tq_mla_read_device_error needs the workspace). */
+ * returns TQ_ERR_WORKSPACE with field "no_alloc_workspace". On a B200 about 39 MB of the array
+ * hold the split partials and the rest 32 bytes per query token, so dense plans fit up to about
+ * 160 000 query tokens; a sparse plan also keeps 4 K + 4 bytes per token for its compacted
+ * entries, so it fits about 5.1 MB / (4 K + 36) tokens: about 620 at K = 2051. The first call
+ * on each device (and the first after that device's context changed) looks up the array's
+ * device address, so make it before capturing any stream. All calls share the one array: calls
+ * that may overlap on the GPU (other streams, other threads) race and must be serialised by the
+ * caller. tq_mla_no_alloc_read_device_error reads the device error flags of the last call on
+ * the current device (it synchronises `stream`). */
 #define TQ_MLA_NO_ALLOC_WORKSPACE_BYTES (42ull << 20)
 int32_t tq_mla_decode_no_alloc(const TqMlaParams* params, void* stream, TqContractError* err);
+int32_t tq_mla_no_alloc_read_device_error(void* stream, int32_t* flags);
 
 /* KV cache writer: the planned "latent -> 528 B KV writer" (docs/DEV-PLAN.md:116) over the row
  * formats of docs/HOST-CONTRACTS.md:122-123 and the paged addressing of contracts.rs:182-209.

@@ -1661,20 +1661,44 @@ int32_t launch(const TqMlaParams* params, void* workspace, uint64_t workspace_by
 
 static __device__ __align__(256) uint8_t g_no_alloc_workspace[TQ_MLA_NO_ALLOC_WORKSPACE_BYTES];
 
-// Device address of g_no_alloc_workspace on `device`, looked up once per device with that
-// device current (in host code the array's name is only a host-side stand-in).
+typedef CUresult (*CtxGetCurrentFn)(CUcontext*);
+
+CtxGetCurrentFn ctx_get_current_fn() {
+  static CtxGetCurrentFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<CtxGetCurrentFn>(p);
+  });
+  return fn;
+}
+
+// Device address of g_no_alloc_workspace on `device` in the current context, looked up with
+// that device current (in host code the array's name is only a host-side stand-in). The
+// address is cached per device together with the context it was found in, and found again when
+// the current context differs (a device reset, or a driver-API context other than the primary
+// one), so a cached address is never used in another context.
 void* no_alloc_workspace(int device) {
   static std::mutex mu;
   static void* cache[128] = {nullptr};
+  static CUcontext cache_ctx[128] = {nullptr};
   std::lock_guard<std::mutex> lock(mu);
   if (device < 0 || device >= 128) return nullptr;
-  if (!cache[device]) {
+  CUcontext ctx = nullptr;
+  CtxGetCurrentFn get = ctx_get_current_fn();
+  if (!get || get(&ctx) != CUDA_SUCCESS) ctx = nullptr;
+  if (!cache[device] || !ctx || cache_ctx[device] != ctx) {
     void* ptr = nullptr;
     if (cudaGetSymbolAddress(&ptr, g_no_alloc_workspace) != cudaSuccess) {
       cudaGetLastError();
       return nullptr;
     }
+    if (!ctx && get && get(&ctx) != CUDA_SUCCESS) ctx = nullptr;  // made current by the lookup
     cache[device] = ptr;
+    cache_ctx[device] = ctx;
   }
   return cache[device];
 }
@@ -1729,6 +1753,16 @@ int32_t tq_mla_decode_no_alloc(const TqMlaParams* params, void* stream, TqContra
   // The scheduler kernel rewrites every workspace word the later kernels read, so the previous
   // call's contents need no clearing.
   return launch(params, ws, TQ_MLA_NO_ALLOC_WORKSPACE_BYTES, stream, err);
+}
+
+int32_t tq_mla_no_alloc_read_device_error(void* stream, int32_t* flags) {
+  if (!flags) return TQ_ERR_INVALID_ARGUMENT;
+  int device = 0;
+  if (cudaGetDevice(&device) != cudaSuccess) return TQ_ERR_CUDA;
+  void* ws = no_alloc_workspace(device);
+  if (!ws) return TQ_ERR_CUDA;
+  // The header sits at offset 0 of every workspace layout.
+  return tq_mla_read_device_error(ws, stream, flags);
 }
 
 int32_t tq_mla_prefill(const TqMlaParams* params, void* workspace, uint64_t workspace_bytes,

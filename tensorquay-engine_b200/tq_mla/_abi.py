@@ -121,6 +121,7 @@ PROTOTYPES = {
     "tq_mla_context_merge": (_I32, [_P(TqContextMergeParams), _VP, _VP]),
     "tq_mla_set_kernel_timer": (_I32, [_VP, _VP]),
     "tq_mla_decode_no_alloc": (_I32, [_P(TqMlaParams), _VP, _P(TqContractError)]),
+    "tq_mla_no_alloc_read_device_error": (_I32, [_VP, _P(_I32)]),
     "tq_kv_write_validate": (_I32, [_P(TqKvWriteSpec), _P(TqContractError)]),
     "tq_kv_write": (_I32, [_P(TqKvWriteSpec), _VP, _VP, _P(TqContractError)]),
     "tq_philox_block": (None, [_P(ctypes.c_uint32), _P(ctypes.c_uint32), _P(ctypes.c_uint32)]),

@@ -94,6 +94,7 @@ def _rank_main(rank, world, port, result_path):
         dist.destroy_process_group()
 
 
+@pytest.mark.timeout(300)
 @pytest.mark.parametrize("world", [2])
 def test_context_split_gather_merge_equals_single_device(tmp_path, world):
     result = tmp_path / "merged.npz"
@@ -129,6 +130,7 @@ def _id_rank_main(rank, world, port, result_path):
         dist.destroy_process_group()
 
 
+@pytest.mark.timeout(300)
 def test_communicator_id_reaches_every_rank(tmp_path):
     result = tmp_path / "id.txt"
     tmp.start_processes(_id_rank_main, args=(2, _free_port(), str(result)), nprocs=2, join=True,

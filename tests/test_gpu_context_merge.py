@@ -100,6 +100,7 @@ def _rank_main(rank, world, port, result_path):
         dist.destroy_process_group()
 
 
+@pytest.mark.timeout(600)
 def test_two_rank_context_merge(cuda_device, tmp_path):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs on this box")
