@@ -257,9 +257,11 @@ int32_t tq_mla_no_alloc_read_device_error(void* stream, int32_t* flags);
  * Optional RMSNorm of each row's 512 latent values before the write (the norm of the planned
  * "kv_a -> norm -> cache write" prologue; docs/DEV-PLAN.md:116): with norm_weight a bf16 [512]
  * tensor (rank 0 switches it off) and norm_eps finite and > 0, each latent value becomes
- * bf16(x * r * w) with r = 1 / sqrt(sum(x^2) / 512 + eps). All f32 operations are IEEE
- * round-to-nearest (no fused multiply-add); the sum adds each 16-value run in order, then
- * combines the 32 runs pairwise at distances 16, 8, 4, 2, 1. The 64 RoPE values of a 576-wide
+ * bf16(bf16(x * r) * w) with r = 1 / sqrt(sum(x^2) / 512 + eps): the normalised value rounded to
+ * bf16 before the weight multiplies it, the rounding points of the model's RMSNorm
+ * (weight * hidden.to(bf16); docs/reviews/2026-09-19-design-review.md:13). All f32 operations
+ * are IEEE round-to-nearest (no fused multiply-add); the sum adds each 16-value run in order,
+ * then combines the 32 runs pairwise at distances 16, 8, 4, 2, 1. The 64 RoPE values of a 576-wide
  * row are copied unchanged; FP8 rows quantize the normalised bf16 values. */
 typedef struct {
   TqTensorSpec src, kv, page_table, seq_id, pos;
@@ -270,6 +272,46 @@ typedef struct {
 int32_t tq_kv_write_validate(const TqKvWriteSpec* spec, TqContractError* err);
 int32_t tq_kv_write(const TqKvWriteSpec* spec, int32_t* device_flags, void* stream,
                     TqContractError* err);
+
+/* MLA prologue: the planned "q_a -> norm -> q_b -> absorb; kv_a -> norm -> cache write"
+ * (docs/DEV-PLAN.md:116). Two row forms: rope_dim 0, the no-RoPE model of
+ * docs/research/glm-5.md:163-167 (q 512 wide; kv_format TQ_KV_BF16 or TQ_KV_FP8_E4M3), and
+ * rope_dim 64 with 576-wide rows (kv_format TQ_KV_BF16_ROPE576). With Dr = rope_dim and
+ * W = 512 + Dr, for every token t:
+ *   cq      = bf16(x[t] . w_qa^T)                                   [Rq]
+ *   cqn     = bf16(bf16(rms(cq)) * q_norm)                          [Rq]
+ *   qf      = bf16(cqn . w_qb^T)                  per head h:       [Dn | Dr]
+ *   q[t, h] = [ bf16(qf[h][:Dn] . w_uk[h]) (the key absorption of mla_attention.py:150)
+ *             | bf16(rope(qf[h][Dn:], pos[t])) ]                    [512 | Dr]
+ *   kvf     = bf16(x[t] . w_kva^T)                                  [512 | Dr]
+ *   row     = [ bf16(bf16(rms(kvf[:512])) * kv_norm) | bf16(rope(kvf[512:], pos[t])) ]
+ * and `row` is written (as tq_kv_write writes it, FP8 rows quantized) to pool row
+ * page_table[seq_id[t]][pos[t] / 64] * 64 + pos[t] % 64.
+ * rms(v) = v / sqrt(mean(v^2) + eps), computed in f32. rope rotates pairs (2i, 2i + 1) by the
+ * angle pos * theta^(-2i / Dr) (angle reduced in f64). The projections are plain bf16 GEMMs with
+ * f32 accumulation (cuBLAS, opened at run time as libcublas.so.12); the norms, RoPE, the
+ * assembly of q and the row writes are this library's kernels.
+ *   x        bf16 [T, Dm]              w_qa  bf16 [Rq, Dm]          q_norm  bf16 [Rq]
+ *   w_qb     bf16 [H * (Dn + Dr), Rq]  w_uk  bf16 [H, Dn, 512]      w_kva   bf16 [W, Dm]
+ *   kv_norm  bf16 [512]                pos, seq_id i32 [T]          page_table i32 [S, L]
+ *   kv       u8 [P, 64, row bytes] pool of `kv_format` rows        q  bf16 [T, H, W] (out)
+ * All matrices are packed row-major with 16-byte aligned bases; Dm, Rq and Dn are multiples of
+ * 8. A row whose seq_id, pos or page entry is out of range is not written and sets
+ * TQ_DEV_SEQ_RANGE, TQ_DEV_TABLE_SHORT or TQ_DEV_PAGE_RANGE in `device_flags` (a device int32,
+ * may be null); its q is still produced. The workspace (tq_mla_prologue_workspace_bytes, 256-byte
+ * aligned) holds the intermediates and cuBLAS's scratch; the first call on a device creates
+ * that device's cuBLAS handle, so make it before capturing a stream. Calls are serialised on
+ * the host (one cuBLAS handle per device). No reference counterpart exists beyond the plan
+ * line above. */
+typedef struct {
+  TqTensorSpec x, w_qa, q_norm, w_qb, w_uk, w_kva, kv_norm, pos, seq_id, page_table, kv, q;
+  int32_t heads, nope_dim, rope_dim, kv_format;
+  float q_eps, kv_eps, rope_theta;
+} TqPrologueSpec;
+int32_t tq_mla_prologue_validate(const TqPrologueSpec* spec, TqContractError* err);
+int32_t tq_mla_prologue_workspace_bytes(const TqPrologueSpec* spec, uint64_t* bytes);
+int32_t tq_mla_prologue(const TqPrologueSpec* spec, void* workspace, uint64_t workspace_bytes,
+                        int32_t* device_flags, void* stream, TqContractError* err);
 
 /* Measurement hook, no reference counterpart. Makes later tq_mla_decode / tq_mla_prefill calls
  * on the calling thread record `begin_event` right before and `end_event` right after the

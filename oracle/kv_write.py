@@ -71,9 +71,12 @@ def quantize_rows(x):
 def rms_norm_rows(src_bf16_bits, weight_bf16_bits, eps):
     """RMSNorm of each row's 512 latent values with the writer's f32 arithmetic, bit for bit:
     per 16-value run the squares are added in dim order, the 32 run sums are combined pairwise at
-    distances 16, 8, 4, 2, 1, mean = sum / 512, r = 1 / sqrt(mean + eps), y = bf16((x * r) * w),
-    every operation an IEEE round-to-nearest f32 operation (no fused multiply-add). Returns the
-    new bf16 bits (uint16 ``[R, 512]``)."""
+    distances 16, 8, 4, 2, 1, mean = sum / 512, r = 1 / sqrt(mean + eps),
+    y = bf16(bf16(x * r) * w), every operation an IEEE round-to-nearest f32 operation (no fused
+    multiply-add). The normalised value is rounded to bf16 before the weight multiplies it, as in
+    the model's RMSNorm (``self.weight * hidden_states.to(input_dtype)``, the Transformers
+    ``modeling_glm5_next.py`` lines 77-81 cited by docs/reviews/2026-09-19-design-review.md:13).
+    Returns the new bf16 bits (uint16 ``[R, 512]``)."""
     from oracle.fp8 import bf16_round
 
     f32 = np.float32
@@ -89,7 +92,8 @@ def rms_norm_rows(src_bf16_bits, weight_bf16_bits, eps):
             acc = (acc + acc[:, lanes ^ o]).astype(f32)
         total = acc[:, 0]
         r = (f32(1.0) / np.sqrt(((total / f32(512.0)).astype(f32) + f32(eps)).astype(f32))).astype(f32)
-        y = ((x * r[:, None]).astype(f32) * w[None, :]).astype(f32)
+        n = bf16_round((x * r[:, None]).astype(f32)).astype(f32)
+        y = (n * w[None, :]).astype(f32)
     bits = (bf16_round(y).astype(np.float32).view(np.uint32) >> 16).astype(np.uint16)
     nan = np.isnan(y)
     bits[nan] = 0x7FC0

@@ -319,7 +319,77 @@ int32_t kv_write_validate_impl(const TqKvWriteSpec* spec, TqContractError* err) 
   return TQ_OK;
 }
 
+// MLA prologue: the same tensor-declaration rules (shape, dtype, packed strides, spans, null,
+// alignment, capacity; outputs never alias inputs), plus 16-byte aligned rows for the GEMMs.
+int32_t prologue_validate_impl(const TqPrologueSpec* spec, TqContractError* err) {
+  Failure f{nullptr, TQ_OK};
+  auto fail = [&](const char* field, int32_t kind) {
+    if (err) { err->field = field; err->kind = kind; }
+    return kind;
+  };
+  if (!spec) return fail("spec", TQ_ERR_INVALID_ARGUMENT);
+  const TqPrologueSpec& s = *spec;
+  if (s.x.rank != 2) return fail("x", TQ_SHAPE);
+  if (s.w_qa.rank != 2) return fail("w_qa", TQ_SHAPE);
+  if (s.page_table.rank != 2) return fail("page_table", TQ_SHAPE);
+  if (s.heads <= 0 || s.heads > 128) return fail("heads", TQ_SHAPE);
+  if (s.nope_dim <= 0 || s.nope_dim > 512 || s.nope_dim % 8) return fail("nope_dim", TQ_SHAPE);
+  if (s.rope_dim != 0 && s.rope_dim != 64) return fail("rope_dim", TQ_SHAPE);
+  uint64_t payload = 0;
+  switch (s.kv_format) {
+    case TQ_KV_BF16: payload = 1024; break;
+    case TQ_KV_FP8_E4M3: payload = 528; break;
+    case TQ_KV_BF16_ROPE576: payload = 1152; break;
+    default: return fail("kv_format", TQ_SHAPE);
+  }
+  if ((s.kv_format == TQ_KV_BF16_ROPE576) != (s.rope_dim == 64)) return fail("kv_format", TQ_SHAPE);
+  const uint64_t T = s.x.shape[0], dm = s.x.shape[1], rq = s.w_qa.shape[0];
+  const uint64_t H = uint64_t(s.heads), dn = uint64_t(s.nope_dim), dr = uint64_t(s.rope_dim);
+  if (dm == 0 || dm % 8 || dm > (1u << 20)) return fail("x", TQ_SHAPE);
+  if (rq == 0 || rq % 8 || rq > (1u << 16)) return fail("w_qa", TQ_SHAPE);
+  if (T > (1u << 24)) return fail("x", TQ_SHAPE);
+  const bool launching = T != 0;
+  if (!check_kv_strides(s.kv, payload, &f)) return fail(f.field, f.kind);
+  const uint64_t x_shape[2] = {T, dm}, wqa[2] = {rq, dm}, qn[1] = {rq};
+  const uint64_t wqb[2] = {H * (dn + dr), rq}, wuk[3] = {H, dn, 512}, wkva[2] = {512 + dr, dm};
+  const uint64_t kvn[1] = {512}, tok[1] = {T};
+  const uint64_t table[2] = {s.page_table.shape[0], s.page_table.shape[1]};
+  const uint64_t pool[3] = {s.kv.shape[0], kPageRows, payload}, q_shape[3] = {T, H, 512 + dr};
+  Extent in[10], out[2];
+  if (!check("x", s.x, x_shape, 2, TQ_DTYPE_BF16, Layout::Packed, launching, &in[0], &f) ||
+      !check("w_qa", s.w_qa, wqa, 2, TQ_DTYPE_BF16, Layout::Packed, launching, &in[1], &f) ||
+      !check("q_norm", s.q_norm, qn, 1, TQ_DTYPE_BF16, Layout::Packed, launching, &in[2], &f) ||
+      !check("w_qb", s.w_qb, wqb, 2, TQ_DTYPE_BF16, Layout::Packed, launching, &in[3], &f) ||
+      !check("w_uk", s.w_uk, wuk, 3, TQ_DTYPE_BF16, Layout::Packed, launching, &in[4], &f) ||
+      !check("w_kva", s.w_kva, wkva, 2, TQ_DTYPE_BF16, Layout::Packed, launching, &in[5], &f) ||
+      !check("kv_norm", s.kv_norm, kvn, 1, TQ_DTYPE_BF16, Layout::Packed, launching, &in[6], &f) ||
+      !check("pos", s.pos, tok, 1, TQ_DTYPE_I32, Layout::Packed, launching, &in[7], &f) ||
+      !check("seq_id", s.seq_id, tok, 1, TQ_DTYPE_I32, Layout::Packed, launching, &in[8], &f) ||
+      !check("page_table", s.page_table, table, 2, TQ_DTYPE_I32, Layout::Packed, launching,
+             &in[9], &f) ||
+      !check("kv", s.kv, pool, 3, TQ_DTYPE_U8, Layout::Checked, launching, &out[0], &f) ||
+      !check("q", s.q, q_shape, 3, TQ_DTYPE_BF16, Layout::Packed, launching, &out[1], &f))
+    return fail(f.field, f.kind);
+  if (launching) {
+    const TqTensorSpec* mats[8] = {&s.x, &s.w_qa, &s.q_norm, &s.w_qb, &s.w_uk, &s.w_kva,
+                                   &s.kv_norm, &s.q};
+    const char* names[8] = {"x", "w_qa", "q_norm", "w_qb", "w_uk", "w_kva", "kv_norm", "q"};
+    for (int i = 0; i < 8; ++i)
+      if (mats[i]->device_address % 16) return fail(names[i], TQ_ALIGNMENT);
+  }
+  if (!(std::isfinite(s.q_eps) && s.q_eps > 0.f)) return fail("q_eps", TQ_SCALE);
+  if (!(std::isfinite(s.kv_eps) && s.kv_eps > 0.f)) return fail("kv_eps", TQ_SCALE);
+  if (!(std::isfinite(s.rope_theta) && s.rope_theta > 1.f)) return fail("rope_theta", TQ_SCALE);
+  if (!check_aliases(in, 10, out, 2, &f)) return fail(f.field, f.kind);
+  if (err) { err->field = nullptr; err->kind = TQ_OK; }
+  return TQ_OK;
+}
+
 }  // namespace
+
+int32_t prologue_validate(const TqPrologueSpec* spec, TqContractError* err) {
+  return prologue_validate_impl(spec, err);
+}
 
 bool params_intact(const TqMlaParams* p) { return p && p->digest == digest_of(*p); }
 
@@ -394,6 +464,10 @@ int32_t tq_mla_sparse_validate(const TqMlaSpec* spec, const TqTensorSpec* idx,
 
 int32_t tq_kv_write_validate(const TqKvWriteSpec* spec, TqContractError* err) {
   return tq::kv_write_validate_impl(spec, err);
+}
+
+int32_t tq_mla_prologue_validate(const TqPrologueSpec* spec, TqContractError* err) {
+  return tq::prologue_validate(spec, err);
 }
 
 int32_t tq_mla_should_launch(const TqMlaParams* params) {

@@ -20,6 +20,7 @@
 namespace tq {
 
 bool params_intact(const TqMlaParams* p);
+int32_t prologue_validate(const TqPrologueSpec* spec, TqContractError* err);
 void philox_block(const uint32_t counter[4], const uint32_t key[2], uint32_t out[4]);
 int32_t philox_words(uint64_t seed, uint64_t stream, uint64_t start, uint32_t* out,
                      uint64_t count);

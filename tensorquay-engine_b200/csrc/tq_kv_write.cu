@@ -137,7 +137,9 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
 // two 16-byte words of bf16 (in place). Only IEEE round-to-nearest f32 operations, in a fixed
 // order: the lane's squares added in dim order, the 32 lane sums combined pairwise at distances
 // 16, 8, 4, 2, 1 (both lanes of a pair get the same sum), mean = sum / 512, r = 1 / sqrt(mean +
-// eps), y = bf16((x * r) * w). All 32 lanes take part.
+// eps), y = bf16(bf16(x * r) * w): the normalised value is rounded to bf16 before the weight
+// multiplies it, as the model's RMSNorm does (weight * hidden.to(bf16), modeling_glm5_next.py
+// lines 77-81). All 32 lanes take part.
 __device__ __forceinline__ void rms_norm_16(uint4& w0, uint4& w1, const uint16_t* nw, float eps,
                                             int lane) {
   uint32_t words[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
@@ -158,7 +160,9 @@ __device__ __forceinline__ void rms_norm_16(uint4& w0, uint4& w1, const uint16_t
   for (int i = 0; i < 8; ++i) {
     const float lo = __uint_as_float(words[i] << 16), hi = __uint_as_float(words[i] & 0xFFFF0000u);
     const float wl = __uint_as_float(gw[i] << 16), wh = __uint_as_float(gw[i] & 0xFFFF0000u);
-    words[i] = pack_bf16x2(__fmul_rn(__fmul_rn(lo, r), wl), __fmul_rn(__fmul_rn(hi, r), wh));
+    const uint32_t n = pack_bf16x2(__fmul_rn(lo, r), __fmul_rn(hi, r));
+    words[i] = pack_bf16x2(__fmul_rn(__uint_as_float(n << 16), wl),
+                           __fmul_rn(__uint_as_float(n & 0xFFFF0000u), wh));
   }
   w0 = make_uint4(words[0], words[1], words[2], words[3]);
   w1 = make_uint4(words[4], words[5], words[6], words[7]);

@@ -1,0 +1,318 @@
+// MLA prologue: "q_a -> norm -> q_b -> absorb; kv_a -> norm -> cache write" (planned as one
+// fused step in docs/DEV-PLAN.md:116; the key absorption is the q_abs = w_uk^T q of
+// reference/src/tq_reference/mla_attention.py:150), for the no-RoPE rows of the reference's model
+// (rope_dim 0, docs/research/glm-5.md:163-167) and for 576-wide rows (rope_dim 64).
+//
+// Per call (T tokens, Dr = rope_dim, W = 512 + Dr):
+//   1. cq  = x . w_qa^T                 plain GEMM, bf16 in, f32 accumulate, bf16 out
+//   2. cq <- bf16(rms(cq)) * q_norm     rms_rows_kernel (in place)
+//   3. qf  = cq . w_qb^T                plain GEMM                       [T, H, Dn + Dr]
+//   4. q[:, :, :512] = qf[:, :, :Dn] . w_uk[h]   one strided-batched GEMM over the heads, written
+//                                       straight into q's row layout (ldc = H * W)
+//   5. q[:, :, 512:] = rope(qf[:, :, Dn:]) and kvf[:, 512:] rotated in place (rope_rows_kernel)
+//   6. kvf = x . w_kva^T                plain GEMM                       [T, W]
+//   7. tq_kv_write: bf16(rms(kvf[:512])) * kv_norm and the row written (FP8 rows quantized) to the
+//      token's pool slot through the page table
+// The GEMMs are cuBLAS (opened at run time as libcublas.so.12: a process that already has it,
+// e.g. through PyTorch, shares that copy); everything else is this library's kernels. At decode
+// sizes the step is HBM-bound on the weights (w_qb and w_uk dominate). The q norm accumulates
+// squares in f32; RoPE reduces its angle pos * theta^(-2i/64) in f64 before the sine and cosine,
+// so positions up to 2^31 keep full precision.
+
+#include <cublas_v2.h>
+#include <cuda_runtime.h>
+#include <dlfcn.h>
+
+#include <cmath>
+#include <cstdint>
+#include <cstring>
+#include <mutex>
+
+#include "tq_contracts.h"
+
+namespace tq {
+namespace prologue {
+
+constexpr int kRopeDim = 64;
+constexpr int kLatent = 512;
+constexpr uint64_t kCublasScratch = 32ull << 20;
+
+// ------------------------------------------------------------------------------ cuBLAS, opened
+struct Blas {
+  cublasStatus_t (*create)(cublasHandle_t*);
+  cublasStatus_t (*set_stream)(cublasHandle_t, cudaStream_t);
+  cublasStatus_t (*set_workspace)(cublasHandle_t, void*, size_t);
+  cublasStatus_t (*gemm)(cublasHandle_t, cublasOperation_t, cublasOperation_t, int, int, int,
+                         const void*, const void*, cudaDataType, int, const void*, cudaDataType,
+                         int, const void*, void*, cudaDataType, int, cublasComputeType_t,
+                         cublasGemmAlgo_t);
+  cublasStatus_t (*gemm_batched)(cublasHandle_t, cublasOperation_t, cublasOperation_t, int, int,
+                                 int, const void*, const void*, cudaDataType, int, long long,
+                                 const void*, cudaDataType, int, long long, const void*, void*,
+                                 cudaDataType, int, long long, int, cublasComputeType_t,
+                                 cublasGemmAlgo_t);
+  bool ok = false;
+};
+
+const Blas* blas() {
+  static Blas b;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* h = dlopen("libcublas.so.12", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) h = dlopen("libcublas.so", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) return;
+    b.create = reinterpret_cast<decltype(b.create)>(dlsym(h, "cublasCreate_v2"));
+    b.set_stream = reinterpret_cast<decltype(b.set_stream)>(dlsym(h, "cublasSetStream_v2"));
+    b.set_workspace = reinterpret_cast<decltype(b.set_workspace)>(dlsym(h, "cublasSetWorkspace_v2"));
+    b.gemm = reinterpret_cast<decltype(b.gemm)>(dlsym(h, "cublasGemmEx"));
+    b.gemm_batched =
+        reinterpret_cast<decltype(b.gemm_batched)>(dlsym(h, "cublasGemmStridedBatchedEx"));
+    b.ok = b.create && b.set_stream && b.set_workspace && b.gemm && b.gemm_batched;
+  });
+  return b.ok ? &b : nullptr;
+}
+
+// One handle per device, created on the first call with that device current.
+cublasHandle_t handle_for(int device) {
+  static std::mutex mu;
+  static cublasHandle_t cache[128] = {nullptr};
+  const Blas* b = blas();
+  if (!b || device < 0 || device >= 128) return nullptr;
+  std::lock_guard<std::mutex> lock(mu);
+  if (!cache[device]) {
+    cublasHandle_t h = nullptr;
+    if (b->create(&h) != CUBLAS_STATUS_SUCCESS) return nullptr;
+    cache[device] = h;
+  }
+  return cache[device];
+}
+
+// ------------------------------------------------------------------------------ kernels
+__device__ __forceinline__ float bf16_to_f32(uint16_t v) { return __uint_as_float(uint32_t(v) << 16); }
+
+__device__ __forceinline__ uint16_t f32_to_bf16(float x) {
+  uint16_t r;
+  asm("cvt.rn.bf16.f32 %0, %1;" : "=h"(r) : "f"(x));
+  return r;
+}
+
+// Rows of `width` bf16 values (packed, `rows` of them): x <- bf16(bf16(x * r) * w), r = 1 /
+// sqrt(mean of squares + eps), squares summed in f32; the normalised value is rounded to bf16
+// before the weight multiplies it, as in the model's RMSNorm (weight * hidden.to(bf16)). One
+// 256-thread block per row, grid-stride.
+__global__ void __launch_bounds__(256) rms_rows_kernel(uint16_t* x, int width, long long rows,
+                                                       const uint16_t* __restrict__ w, float eps) {
+  __shared__ float part[8];
+  __shared__ float s_r;
+  for (long long row = blockIdx.x; row < rows; row += gridDim.x) {
+    uint16_t* v = x + row * width;
+    float sq = 0.f;
+    for (int i = threadIdx.x; i < width; i += 256) {
+      const float f = bf16_to_f32(v[i]);
+      sq += f * f;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xFFFFFFFFu, sq, o);
+    if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = sq;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      float t = 0.f;
+      for (int k = 0; k < 8; ++k) t += part[k];
+      s_r = 1.f / sqrtf(t / float(width) + eps);
+    }
+    __syncthreads();
+    const float r = s_r;
+    for (int i = threadIdx.x; i < width; i += 256)
+      v[i] = f32_to_bf16(bf16_to_f32(f32_to_bf16(bf16_to_f32(v[i]) * r)) * bf16_to_f32(w[i]));
+    __syncthreads();  // part / s_r are reused by the next row
+  }
+}
+
+// Rotation of pair i of the 64 RoPE values at position `pos`: angle pos * theta^(-2i/64),
+// reduced modulo 2 pi in f64.
+__device__ __forceinline__ void rope_pair(float x0, float x1, int i, int pos, double log2_theta,
+                                          float* y0, float* y1) {
+  const double freq = exp2(-double(2 * i) / double(kRopeDim) * log2_theta);
+  const double angle = fmod(double(pos) * freq, 6.283185307179586476925286766559);
+  double s, c;
+  sincos(angle, &s, &c);
+  const float cf = float(c), sf = float(s);
+  *y0 = x0 * cf - x1 * sf;
+  *y1 = x0 * sf + x1 * cf;
+}
+
+// dst[r, 2i .. 2i + 1] = rope(src[r, 2i .. 2i + 1]) at pos[r / per_token], for `rows` rows of 64
+// values at the given element offsets and row strides: one warp per row, lane i one pair. Each
+// lane reads its pair before writing it, so src may equal dst (the kv RoPE slice is rotated in
+// place). q: rows (t, h), src qf + Dn, dst q + 512; kv: rows t, src = dst = kvf + 512.
+__global__ void __launch_bounds__(256) rope_rows_kernel(const uint16_t* src, long long src_stride,
+                                                        uint16_t* dst, long long dst_stride,
+                                                        long long rows, int per_token,
+                                                        const int* __restrict__ pos,
+                                                        double log2_theta) {
+  const int lane = threadIdx.x & 31;
+  for (long long r = (blockIdx.x * 256ll + threadIdx.x) >> 5; r < rows;
+       r += (gridDim.x * 256ll) >> 5) {
+    const uint32_t in = *reinterpret_cast<const uint32_t*>(src + r * src_stride + 2 * lane);
+    float y0, y1;
+    rope_pair(bf16_to_f32(uint16_t(in & 0xFFFF)), bf16_to_f32(uint16_t(in >> 16)), lane,
+              pos[r / per_token], log2_theta, &y0, &y1);
+    *reinterpret_cast<uint32_t*>(dst + r * dst_stride + 2 * lane) =
+        uint32_t(f32_to_bf16(y0)) | (uint32_t(f32_to_bf16(y1)) << 16);
+  }
+}
+
+// ------------------------------------------------------------------------------ host
+struct Layout {
+  uint64_t cq, qf, kvf, scratch, total;  // byte offsets into the workspace, and its size
+};
+
+uint64_t round256(uint64_t v) { return (v + 255) & ~uint64_t(255); }
+
+Layout layout_of(const TqPrologueSpec& s) {
+  const uint64_t T = s.x.shape[0], rq = s.w_qa.shape[0], H = uint64_t(s.heads);
+  const uint64_t dn = uint64_t(s.nope_dim), dr = uint64_t(s.rope_dim);
+  Layout l;
+  l.cq = 0;
+  l.qf = l.cq + round256(T * rq * 2);
+  l.kvf = l.qf + round256(T * H * (dn + dr) * 2);
+  l.scratch = l.kvf + round256(T * (kLatent + dr) * 2);
+  l.total = l.scratch + kCublasScratch;
+  return l;
+}
+
+int sm_count(int device) {
+  static std::mutex mu;
+  static int cached[128] = {0};
+  if (device < 0 || device >= 128) return 0;
+  std::lock_guard<std::mutex> lock(mu);
+  if (cached[device]) return cached[device];
+  int n = 0;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device) != cudaSuccess) return 0;
+  cached[device] = n;
+  return n;
+}
+
+// Row-major C[M, N] = A[M, K] . B[N, K]^T with A, B, C packed: cuBLAS sees the column-major
+// C^T = B . A^T (op(B) = T).
+cublasStatus_t gemm_nt(const Blas* b, cublasHandle_t h, const void* A, const void* B, void* C,
+                       int M, int N, int K) {
+  const float one = 1.f, zero = 0.f;
+  return b->gemm(h, CUBLAS_OP_T, CUBLAS_OP_N, N, M, K, &one, B, CUDA_R_16BF, K, A, CUDA_R_16BF, K,
+                 &zero, C, CUDA_R_16BF, N, CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT);
+}
+
+std::mutex& blas_mutex() {
+  static std::mutex mu;
+  return mu;
+}
+
+}  // namespace prologue
+}  // namespace tq
+
+extern "C" int32_t tq_mla_prologue_workspace_bytes(const TqPrologueSpec* spec, uint64_t* bytes) {
+  TqContractError e{nullptr, TQ_OK};
+  const int32_t st = tq::prologue_validate(spec, &e);
+  if (st != TQ_OK) return st;
+  if (!bytes) return TQ_ERR_INVALID_ARGUMENT;
+  *bytes = tq::prologue::layout_of(*spec).total;
+  return TQ_OK;
+}
+
+extern "C" int32_t tq_mla_prologue(const TqPrologueSpec* spec, void* workspace,
+                                   uint64_t workspace_bytes, int32_t* device_flags, void* stream,
+                                   TqContractError* err) {
+  using namespace tq::prologue;
+  auto fail = [&](const char* field, int32_t kind) {
+    if (err) { err->field = field; err->kind = kind; }
+    return kind;
+  };
+  const int32_t st = tq::prologue_validate(spec, err);
+  if (st != TQ_OK) return st;
+  const TqPrologueSpec& s = *spec;
+  const Layout l = layout_of(s);
+  const uint64_t T64 = s.x.shape[0];
+  if (T64 == 0) return fail(nullptr, TQ_OK);
+  if (!workspace || reinterpret_cast<uintptr_t>(workspace) % 256 || workspace_bytes < l.total)
+    return fail("workspace", TQ_ERR_WORKSPACE);
+  const Blas* b = blas();
+  if (!b) return fail("libcublas", TQ_ERR_UNSUPPORTED);
+  int device = 0;
+  if (cudaGetDevice(&device) != cudaSuccess) return fail("device", TQ_ERR_CUDA);
+  const int sms = sm_count(device);
+  if (sms <= 0) return fail("device", TQ_ERR_CUDA);
+  cudaStream_t cs = reinterpret_cast<cudaStream_t>(stream);
+
+  const int T = int(T64), dm = int(s.x.shape[1]), rq = int(s.w_qa.shape[0]), H = s.heads;
+  const int dn = s.nope_dim, dr = s.rope_dim, width = kLatent + dr;
+  char* ws = static_cast<char*>(workspace);
+  uint16_t* cq = reinterpret_cast<uint16_t*>(ws + l.cq);
+  uint16_t* qf = reinterpret_cast<uint16_t*>(ws + l.qf);
+  uint16_t* kvf = reinterpret_cast<uint16_t*>(ws + l.kvf);
+  const void* x = reinterpret_cast<const void*>(s.x.device_address);
+  uint16_t* q = reinterpret_cast<uint16_t*>(s.q.device_address);
+  const int* pos = reinterpret_cast<const int*>(s.pos.device_address);
+  const double log2_theta = std::log2(double(s.rope_theta));
+  const long long cap = 8ll * sms;
+  {
+    std::lock_guard<std::mutex> lock(blas_mutex());
+    cublasHandle_t h = handle_for(device);
+    if (!h) return fail("cublas_handle", TQ_ERR_CUDA);
+    if (b->set_stream(h, cs) != CUBLAS_STATUS_SUCCESS ||
+        b->set_workspace(h, ws + l.scratch, kCublasScratch) != CUBLAS_STATUS_SUCCESS)
+      return fail("cublas_setup", TQ_ERR_CUDA);
+    // 1-2: cq = rms(x . w_qa^T) * q_norm
+    if (gemm_nt(b, h, x, reinterpret_cast<const void*>(s.w_qa.device_address), cq, T, rq, dm) !=
+        CUBLAS_STATUS_SUCCESS)
+      return fail("gemm_q_a", TQ_ERR_CUDA);
+    rms_rows_kernel<<<int(T < cap ? T : cap), 256, 0, cs>>>(
+        cq, rq, T, reinterpret_cast<const uint16_t*>(s.q_norm.device_address), s.q_eps);
+    // 3: qf = cq . w_qb^T
+    if (gemm_nt(b, h, cq, reinterpret_cast<const void*>(s.w_qb.device_address), qf, T,
+                H * (dn + dr), rq) != CUBLAS_STATUS_SUCCESS)
+      return fail("gemm_q_b", TQ_ERR_CUDA);
+    // 4: per head h, row-major q[:, h, :512] = qf[:, h, :Dn] . w_uk[h]; column-major that is
+    // q^T = w_uk[h]^T . qf^T with w_uk[h] seen as a 512 x Dn matrix (ld 512), qf[:, h] as
+    // Dn x T (ld H (Dn + Dr)) and q[:, h] as 512 x T (ld H W).
+    const float one = 1.f, zero = 0.f;
+    if (b->gemm_batched(h, CUBLAS_OP_N, CUBLAS_OP_N, kLatent, T, dn, &one,
+                        reinterpret_cast<const void*>(s.w_uk.device_address), CUDA_R_16BF, kLatent,
+                        (long long)dn * kLatent, qf, CUDA_R_16BF, H * (dn + dr), dn + dr, &zero, q,
+                        CUDA_R_16BF, H * width, width, H, CUBLAS_COMPUTE_32F,
+                        CUBLAS_GEMM_DEFAULT) != CUBLAS_STATUS_SUCCESS)
+      return fail("gemm_absorb", TQ_ERR_CUDA);
+    // 6: kvf = x . w_kva^T
+    if (gemm_nt(b, h, x, reinterpret_cast<const void*>(s.w_kva.device_address), kvf, T, width,
+                dm) != CUBLAS_STATUS_SUCCESS)
+      return fail("gemm_kv_a", TQ_ERR_CUDA);
+  }
+  if (dr) {
+    // 5: the RoPE slices of q, and of kvf in place
+    const long long qrows = (long long)T * H, qblocks = (qrows + 7) / 8;
+    rope_rows_kernel<<<int(qblocks < cap ? qblocks : cap), 256, 0, cs>>>(
+        qf + dn, dn + dr, q + kLatent, width, qrows, H, pos, log2_theta);
+    const long long kblocks = ((long long)T + 7) / 8;
+    rope_rows_kernel<<<int(kblocks < cap ? kblocks : cap), 256, 0, cs>>>(
+        kvf + kLatent, width, kvf + kLatent, width, T, 1, pos, log2_theta);
+  }
+  if (cudaGetLastError() != cudaSuccess) return fail("launch", TQ_ERR_CUDA);
+  // 7: norm of the latent part and the paged write (FP8 rows quantized), by the cache writer
+  TqKvWriteSpec w;
+  std::memset(&w, 0, sizeof(w));
+  w.src.shape[0] = T64;
+  w.src.shape[1] = uint64_t(width);
+  w.src.strides_bytes[0] = uint64_t(width) * 2;
+  w.src.strides_bytes[1] = 2;
+  w.src.rank = 2;
+  w.src.dtype = TQ_DTYPE_BF16;
+  w.src.device_address = reinterpret_cast<uint64_t>(kvf);
+  w.src.buffer_bytes = T64 * uint64_t(width) * 2;
+  w.kv = s.kv;
+  w.page_table = s.page_table;
+  w.seq_id = s.seq_id;
+  w.pos = s.pos;
+  w.kv_format = s.kv_format;
+  w.norm_weight = s.kv_norm;
+  w.norm_eps = s.kv_eps;
+  return tq_kv_write(&w, device_flags, stream, err);
+}

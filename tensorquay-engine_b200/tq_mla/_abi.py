@@ -95,6 +95,14 @@ class TqKvWriteSpec(ctypes.Structure):
         ("kv_format", ctypes.c_int32), ("norm_weight", TqTensorSpec), ("norm_eps", ctypes.c_float)]
 
 
+class TqPrologueSpec(ctypes.Structure):
+    _fields_ = [(name, TqTensorSpec) for name in (
+        "x", "w_qa", "q_norm", "w_qb", "w_uk", "w_kva", "kv_norm", "pos", "seq_id", "page_table",
+        "kv", "q")] + [(name, ctypes.c_int32) for name in (
+            "heads", "nope_dim", "rope_dim", "kv_format")] + [(name, ctypes.c_float) for name in (
+                "q_eps", "kv_eps", "rope_theta")]
+
+
 # Every exported symbol of include/tq_mla.h, with its ctypes prototype.
 _P = ctypes.POINTER
 _U64, _I32, _VP = ctypes.c_uint64, ctypes.c_int32, ctypes.c_void_p
@@ -124,6 +132,9 @@ PROTOTYPES = {
     "tq_mla_no_alloc_read_device_error": (_I32, [_VP, _P(_I32)]),
     "tq_kv_write_validate": (_I32, [_P(TqKvWriteSpec), _P(TqContractError)]),
     "tq_kv_write": (_I32, [_P(TqKvWriteSpec), _VP, _VP, _P(TqContractError)]),
+    "tq_mla_prologue_validate": (_I32, [_P(TqPrologueSpec), _P(TqContractError)]),
+    "tq_mla_prologue_workspace_bytes": (_I32, [_P(TqPrologueSpec), _P(_U64)]),
+    "tq_mla_prologue": (_I32, [_P(TqPrologueSpec), _VP, _U64, _VP, _VP, _P(TqContractError)]),
     "tq_philox_block": (None, [_P(ctypes.c_uint32), _P(ctypes.c_uint32), _P(ctypes.c_uint32)]),
     "tq_philox_words": (_I32, [_U64, _U64, _U64, _P(ctypes.c_uint32), _U64]),
     "tq_philox_uniform_f32": (ctypes.c_float, [ctypes.c_uint32]),

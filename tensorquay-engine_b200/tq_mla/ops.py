@@ -243,6 +243,64 @@ def kv_write(src, kv, page_table, seq_id, pos, *, kv_format=None, flags=None, st
     return kv
 
 
+def prologue_spec(x, w_qa, q_norm, w_qb, w_uk, w_kva, kv_norm, pos, seq_id, page_table, kv, q, *,
+                  heads, nope_dim, rope_dim, kv_format=None, q_eps=1e-6, kv_eps=1e-6,
+                  rope_theta=10000.0):
+    """Declaration of an MLA prologue call (``tq_mla_prologue``)."""
+    if kv_format is None:
+        kv_format = _abi.KV_BF16_ROPE576 if rope_dim else _abi.KV_BF16
+    s = _abi.TqPrologueSpec()
+    for name, t in (("x", x), ("w_qa", w_qa), ("q_norm", q_norm), ("w_qb", w_qb), ("w_uk", w_uk),
+                    ("w_kva", w_kva), ("kv_norm", kv_norm), ("pos", pos), ("seq_id", seq_id),
+                    ("page_table", page_table), ("q", q)):
+        setattr(s, name, spec_of(t))
+    s.kv = pool_spec(kv, kv_format)
+    s.heads, s.nope_dim, s.rope_dim, s.kv_format = int(heads), int(nope_dim), int(rope_dim), kv_format
+    s.q_eps, s.kv_eps, s.rope_theta = float(q_eps), float(kv_eps), float(rope_theta)
+    return s
+
+
+class MlaPrologue:
+    """A validated prologue: token activations ``x`` to absorbed queries ``q`` and cache rows.
+
+    ``x`` bf16 ``[T, Dm]``; weights ``w_qa [Rq, Dm]``, ``q_norm [Rq]``, ``w_qb [H (Dn + Dr), Rq]``,
+    ``w_uk [H, Dn, 512]``, ``w_kva [512 + Dr, Dm]``, ``kv_norm [512]``; ``pos``/``seq_id`` i32
+    ``[T]``. Writes ``q`` bf16 ``[T, H, 512 + Dr]`` and each token's row into the paged pool
+    ``kv`` at ``pos`` of sequence ``seq_id`` (``kv_format`` rows). Owns only its workspace.
+    """
+
+    def __init__(self, x, w_qa, q_norm, w_qb, w_uk, w_kva, kv_norm, pos, seq_id, page_table, kv,
+                 q, **kw):
+        self._keep = (x, w_qa, q_norm, w_qb, w_uk, w_kva, kv_norm, pos, seq_id, page_table, kv, q)
+        self.spec = prologue_spec(x, w_qa, q_norm, w_qb, w_uk, w_kva, kv_norm, pos, seq_id,
+                                  page_table, kv, q, **kw)
+        err = _abi.TqContractError()
+        raise_for(lib.tq_mla_prologue_validate(ctypes.byref(self.spec), ctypes.byref(err)), err)
+        nbytes = ctypes.c_uint64()
+        raise_for(lib.tq_mla_prologue_workspace_bytes(ctypes.byref(self.spec),
+                                                      ctypes.byref(nbytes)))
+        self.workspace = torch.empty(int(nbytes.value), dtype=torch.uint8, device=x.device)
+        self.q = q
+
+    def __call__(self, flags=None, stream=None):
+        err = _abi.TqContractError()
+        fp = ctypes.c_void_p(flags.data_ptr()) if flags is not None else None
+        raise_for(lib.tq_mla_prologue(ctypes.byref(self.spec),
+                                      ctypes.c_void_p(self.workspace.data_ptr()),
+                                      self.workspace.numel(), fp, _stream_handle(stream),
+                                      ctypes.byref(err)), err)
+        return self.q
+
+
+def mla_prologue(x, w_qa, q_norm, w_qb, w_uk, w_kva, kv_norm, pos, seq_id, page_table, kv, *,
+                 heads, nope_dim, rope_dim, q=None, flags=None, stream=None, **kw):
+    """One prologue call (see ``MlaPrologue``); returns ``q``."""
+    if q is None:
+        q = torch.empty((x.shape[0], heads, 512 + rope_dim), dtype=torch.bfloat16, device=x.device)
+    return MlaPrologue(x, w_qa, q_norm, w_qb, w_uk, w_kva, kv_norm, pos, seq_id, page_table, kv, q,
+                       heads=heads, nope_dim=nope_dim, rope_dim=rope_dim, **kw)(flags, stream)
+
+
 def combine_parts(part_out, part_lse, out=None, lse=None, stream=None):
     """Merge ``G`` partial results (``part_out f32 [G,T,H,512]``, ``part_lse f32 [G,T,H]``)."""
     g, t, h, _ = part_out.shape

@@ -52,6 +52,9 @@ STRUCTS = {
                                                          "out_stride_head", "out_dtype"]),
     "TqKvWriteSpec": (_abi.TqKvWriteSpec, ["src", "kv", "page_table", "seq_id", "pos",
                                            "kv_format", "norm_weight", "norm_eps"]),
+    "TqPrologueSpec": (_abi.TqPrologueSpec, ["x", "w_qa", "w_uk", "kv", "q", "heads", "nope_dim",
+                                             "rope_dim", "kv_format", "q_eps", "kv_eps",
+                                             "rope_theta"]),
 }
 
 
