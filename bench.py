@@ -2,7 +2,7 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
                     [--config decode|decode_fp8|mtp|prefill|longctx|cpu|kv_write|kv_write_fp8|
-                              sparse|sparse_fp8]
+                              sparse|sparse_fp8|prologue|prologue_nope]
                     [--cpu-sample S]
 
 A step is one launch of the attention path (scheduler, tcgen05 attention kernel, combine) over
@@ -17,7 +17,8 @@ stride 544; or 576 wide, copied to 1152-byte rows) scattered into a permuted pag
 is rows written per second. ``--config sparse`` / ``sparse_fp8`` time sparse top-k decode: 64
 sequences x 1 token, 32 heads, 32K cached positions, 2051 index entries per token of which 2048
 are valid, bf16 or FP8 rows; four index sets rotate between steps so the rows read are not
-L2-resident.
+L2-resident. ``--config prologue`` / ``prologue_nope`` time the MLA prologue of one decode step
+(64 tokens: projections, norms, absorption, RoPE, cache write) with L2 flushed between steps.
 
 With N ranks (torchrun, one GPU each) the job holds N x 64 sequences drawn from the same seeded
 stream and sharded by token count (weak scaling); there is no collective on the data path.
@@ -485,6 +486,187 @@ def run_writer(args, world, rank, local_rank):
         print(json.dumps(result), flush=True)
 
 
+# ------------------------------------------------------------------------- MLA prologue
+
+# One decode step's prologue: every sequence's new token, x -> (absorbed q, cache row).
+# "prologue": the 576-wide form at the decode batch (128 heads of 128 + 64 RoPE, hidden 7168,
+# Q rank 1536); "prologue_nope": the reference's no-RoPE model (64 heads of 256, hidden 4096,
+# Q rank 1536) writing 528-byte FP8 rows.
+PROLOGUE = {
+    "prologue": dict(tokens=64, dm=7168, rq=1536, heads=128, dn=128, dr=64, fmt=2, row=1152),
+    "prologue_nope": dict(tokens=64, dm=4096, rq=1536, heads=64, dn=256, dr=0, fmt=1, row=544),
+}
+L2_FLUSH_BYTES = 256 << 20
+
+
+def prologue_host(name, seed=5):
+    """Seeded weights and one decode token per sequence (positions uniform in [4096, 8192)),
+    float32 arrays holding bf16-rounded values."""
+    import torch
+
+    c = PROLOGUE[name]
+    g = np.random.default_rng(seed)
+    dm, rq, h, dn, dr, t = c["dm"], c["rq"], c["heads"], c["dn"], c["dr"], c["tokens"]
+
+    def bf(a):
+        return torch.from_numpy(a.astype(np.float32)).to(torch.bfloat16).float().numpy()
+
+    w = dict(x=bf(g.standard_normal((t, dm))),
+             w_qa=bf(g.standard_normal((rq, dm)) / math.sqrt(dm)),
+             q_norm=bf(g.uniform(0.5, 1.5, rq)),
+             w_qb=bf(g.standard_normal((h * (dn + dr), rq)) / math.sqrt(rq)),
+             w_uk=bf(g.standard_normal((h, dn, 512)) / math.sqrt(dn)),
+             w_kva=bf(g.standard_normal((512 + dr, dm)) / math.sqrt(dm)),
+             kv_norm=bf(g.uniform(0.5, 1.5, 512)))
+    pos = g.integers(4096, 8192, t).astype(np.int32)
+    seq = np.arange(t, dtype=np.int32)
+    slots = 128
+    table = g.permutation(t * slots).astype(np.int32).reshape(t, slots)
+    return c, w, pos, seq, table
+
+
+def prologue_bytes(c):
+    """Algorithmic bytes of one step: the weights, x, q and the rows written (plus pos, seq_id)."""
+    dm, rq, h, dn, dr, t = c["dm"], c["rq"], c["heads"], c["dn"], c["dr"], c["tokens"]
+    payload = {0: 1024, 1: 528, 2: 1152}[c["fmt"]]
+    weights = 2 * (rq * dm + rq + h * (dn + dr) * rq + h * dn * 512 + (512 + dr) * dm + 512)
+    return weights + t * (2 * dm + 2 * h * (512 + dr) + payload + 8)
+
+
+def prologue_cpu_baseline(name, min_seconds=10.0):
+    """The oracle's float64 prologue of the whole step (numpy BLAS on every host thread), repeated
+    for at least ``min_seconds``, in tokens/s."""
+    from oracle import prologue as opro
+
+    c, w, pos, seq, table = prologue_host(name)
+    w = {k: v.astype(np.float64) for k, v in w.items()}
+    reps = 0
+    t0 = time.perf_counter()
+    while True:
+        opro.prologue(**w, pos=pos, heads=c["heads"], nope_dim=c["dn"], rope_dim=c["dr"],
+                      q_eps=1e-6, kv_eps=1e-6, rope_theta=10000.0)
+        reps += 1
+        sec = time.perf_counter() - t0
+        if sec >= min_seconds:
+            break
+    return {"value": reps * c["tokens"] / sec, "unit": UNIT, "cores": os.cpu_count(),
+            "kind": "port", "seconds": sec / reps,
+            "sample": f"{name}: the whole {c['tokens']}-token step through the oracle's float64 "
+                      f"prologue (numpy BLAS, all host threads), {reps} repetitions in "
+                      f"{sec:.1f} s; the reference ships no prologue of its own"}
+
+
+def run_prologue(args, world, rank, local_rank):
+    import torch
+    import torch.distributed as dist
+    from tq_mla import ops
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    c, w, pos, seq, table = prologue_host(args.config, seed=5 + rank)
+    d = {k: torch.from_numpy(v).to(torch.bfloat16).to(dev) for k, v in w.items()}
+    h_x = torch.from_numpy(w["x"]).to(torch.bfloat16).pin_memory()
+    h_ids = torch.from_numpy(np.stack([pos, seq])).pin_memory()
+    d_ids = h_ids.to(dev)
+    d_table = torch.from_numpy(table).to(dev)
+    pool = torch.zeros((table.size, 64, c["row"]), dtype=torch.uint8, device=dev)
+    q = torch.empty((c["tokens"], c["heads"], 512 + c["dr"]), dtype=torch.bfloat16, device=dev)
+    flags = torch.zeros(1, dtype=torch.int32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    pro = ops.MlaPrologue(d["x"], d["w_qa"], d["q_norm"], d["w_qb"], d["w_uk"], d["w_kva"],
+                          d["kv_norm"], d_ids[0], d_ids[1], d_table, pool, q, heads=c["heads"],
+                          nope_dim=c["dn"], rope_dim=c["dr"], kv_format=c["fmt"])
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    for _ in range(max(args.warmup, 3)):
+        pro(flags=flags, stream=stream)
+    torch.cuda.synchronize(dev)
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(args.steps)]
+    clock = ClockSampler(local_rank, clock_log_path(args, rank))
+    barrier()
+    torch.cuda.synchronize(dev)
+    with clock:
+        for a, b in evs:
+            flush.fill_(1)                        # L2 flushed between timed steps (256 MB write)
+            a.record(stream)
+            pro(flags=flags, stream=stream)
+            b.record(stream)
+        torch.cuda.synchronize(dev)
+    barrier()
+    times = [a.elapsed_time(b) for a, b in evs]
+    ms_step = max_over_ranks(sum(times) / len(times))
+    # End to end: x, positions and sequence ids copied in from pinned host memory, the device
+    # flags read back (q stays on the device for the attention step that consumes it).
+    h_flags = torch.zeros(1, dtype=torch.int32).pin_memory()
+    e2e = []
+    for _ in range(max(3, min(args.steps, 50))):
+        flush.fill_(1)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        d["x"].copy_(h_x, non_blocking=True)
+        d_ids.copy_(h_ids, non_blocking=True)
+        pro(flags=flags, stream=stream)
+        h_flags.copy_(flags, non_blocking=True)
+        b.record(stream)
+        e2e.append((a, b))
+    torch.cuda.synchronize(dev)
+    e2e_ms = max_over_ranks(sum(a.elapsed_time(b) for a, b in e2e) / len(e2e))
+    assert int(flags.item()) == 0, "prologue flagged rows"
+    # Self-check of the timed output against the oracle (q of every token).
+    from oracle import prologue as opro
+
+    q_ref, _ = opro.prologue(**{k: v.astype(np.float64) for k, v in w.items()}, pos=pos,
+                             heads=c["heads"], nope_dim=c["dn"], rope_dim=c["dr"], q_eps=1e-6,
+                             kv_eps=1e-6, rope_theta=10000.0)
+    got = q.float().cpu().numpy().astype(np.float64)
+    rms = np.sqrt(np.mean(q_ref ** 2, axis=-1, keepdims=True))
+    ok = bool(np.all(np.abs(got - q_ref) <= 2.0 ** -6 * np.abs(q_ref) + 2.0 ** -6 * rms) and
+              np.linalg.norm(got - q_ref) <= 2.0 ** -8 * np.linalg.norm(q_ref))
+    nbytes = prologue_bytes(c)
+    hbm, _, _, src_name = peaks()
+    ach = nbytes / (ms_step * 1e-3) / 1e9
+    ours = 2 + (2 if c["dr"] else 0)
+    t = c["tokens"]
+    result = {
+        "metric": "MLA prologue tokens/s", "value": world * t / (ms_step * 1e-3), "unit": UNIT,
+        "n_gpus": world, "steps": args.steps, "warmup": max(args.warmup, 3),
+        "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16 (f32 accumulate)", "data": "synthetic",
+        "config": {"workload": f"{args.config}: {t} decode tokens, hidden {c['dm']}, Q rank "
+                               f"{c['rq']}, {c['heads']} heads x ({c['dn']} + {c['dr']}), rows "
+                               f"{ {0: 1024, 1: 528, 2: 1152}[c['fmt']] } B",
+                   "l2": "flushed between timed steps (256 MB write outside the events)"},
+        "e2e": {"value": world * t / (e2e_ms * 1e-3), "unit": UNIT,
+                "h2d_bytes_per_step": t * c["dm"] * 2 + 8 * t, "d2h_bytes_per_step": 4,
+                "ms_per_step": e2e_ms},
+        "gpu_launches": ours * args.steps,
+        "library_launches_per_step": 4,
+        "roofline": {"bound": "hbm", "achieved": ach, "peak": hbm, "unit": "GB/s",
+                     "frac": ach / hbm, "traffic": None,
+                     "kernel": "whole prologue step (4 cuBLAS GEMMs + norm, RoPE, writer)",
+                     "peak_source": f"{src_name} (MEASURED_PEAKS.json)",
+                     "algorithmic_bytes_per_step": nbytes},
+        "self_check": {"q_within_tolerance": ok, "tokens": t},
+        "clocks": clock.summary(),
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        result["cpu_baseline"] = prologue_cpu_baseline(args.config)
+    if rank == 0:
+        print(json.dumps(result), flush=True)
+
+
 # ------------------------------------------------------------------------- sparse top-k
 
 SPARSE_K, SPARSE_VALID, SPARSE_SETS = 2051, 2048, 4
@@ -673,6 +855,17 @@ def run_reference(args, world, rank):
         base = sparse_cpu_baseline(args.config, tokens=16)
         line = {"impl": "reference", "metric": "MLA sparse top-k decode tokens/s",
                 "value": base["value"], "unit": UNIT, "n_gpus": world, "steps": 1, "warmup": 0,
+                "ms_per_step": 1e3 * base["seconds"], "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
+                "config": {"workload": args.config}, "cpu_baseline": base,
+                "e2e": {"value": base["value"], "unit": UNIT, "h2d_bytes_per_step": 0,
+                        "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
+        return
+    if args.config.startswith("prologue"):
+        base = prologue_cpu_baseline(args.config)
+        line = {"impl": "reference", "metric": "MLA prologue tokens/s", "value": base["value"],
+                "unit": UNIT, "n_gpus": world, "steps": 1, "warmup": 0,
                 "ms_per_step": 1e3 * base["seconds"], "higher_is_better": True,
                 "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
                 "config": {"workload": args.config}, "cpu_baseline": base,
@@ -1306,7 +1499,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", default="decode",
                     choices=["decode", "decode_fp8", "mtp", "prefill", "longctx", "cpu",
-                             "kv_write", "kv_write_fp8", "sparse", "sparse_fp8"])
+                             "kv_write", "kv_write_fp8", "sparse", "sparse_fp8", "prologue",
+                             "prologue_nope"])
     ap.add_argument("--scaling", choices=["weak", "strong"], default="weak",
                     help="weak: N ranks hold N times the one-GPU batch; strong: the batch stays "
                          "fixed and is shared (longctx: each sequence's pages split over the "
@@ -1333,6 +1527,8 @@ def main():
     try:
         if args.config.startswith("kv_write"):
             run_writer(args, world, rank, local_rank)
+        elif args.config.startswith("prologue"):
+            run_prologue(args, world, rank, local_rank)
         elif args.config.startswith("sparse"):
             run_sparse(args, world, rank, local_rank)
         elif args.config == "longctx" and args.scaling == "strong" and world > 1:

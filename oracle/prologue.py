@@ -84,7 +84,7 @@ def prologue(x, w_qa, q_norm, w_qb, w_uk, w_kva, kv_norm, pos, *, heads, nope_di
 
     Returns ``(q, kvf)``: ``q`` float64 ``[T, H, 512 + Dr]`` (bf16 values) and ``kvf`` float64
     ``[T, 512 + Dr]``, the projected cache row before its norm (RoPE part already rotated), which
-    ``rows`` turns into pool rows.
+    ``write_rows`` turns into pool rows.
     """
     x = np.asarray(x, np.float64)
     t = x.shape[0]
@@ -96,10 +96,16 @@ def prologue(x, w_qa, q_norm, w_qb, w_uk, w_kva, kv_norm, pos, *, heads, nope_di
     q[:, :, :LATENT] = bf16(absorb(qf[:, :, :dn], w_uk))
     if dr:
         q[:, :, LATENT:] = rope(qf[:, :, dn:], pos, rope_theta)
-    kvf = bf16(x @ np.asarray(w_kva, np.float64).T)
-    if dr:
+    return q, cache_rows(x, w_kva, pos, rope_dim=dr, rope_theta=rope_theta)
+
+
+def cache_rows(x, w_kva, pos, *, rope_dim, rope_theta):
+    """``kvf = bf16(x . w_kva^T)`` with its RoPE part rotated (``[T, 512 + Dr]``, bf16 values):
+    the cache half of the prologue before the writer's norm."""
+    kvf = bf16(np.asarray(x, np.float64) @ np.asarray(w_kva, np.float64).T)
+    if rope_dim:
         kvf[:, LATENT:] = rope(kvf[:, LATENT:], pos, rope_theta)
-    return q, kvf
+    return kvf
 
 
 def write_rows(pool_u8, kvf, kv_norm, page_table, seq_id, pos, *, kv_format, kv_eps):

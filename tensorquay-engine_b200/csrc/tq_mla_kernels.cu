@@ -435,11 +435,13 @@ __global__ void __launch_bounds__((kFp8 || kSparse) ? kThreadsGather : kThreads,
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
-      // FP8 / sparse: a page's stage is complete when the four convert warps have arrived; a query
-      // slot's TMA arrives once with its bytes plus three plain arrivals.
+      // FP8 / sparse: a page's stage is complete when the four convert warps have arrived (FP8:
+      // each arrival also expects the peer's 4 KB copy of its keys' value half); a query slot's
+      // TMA arrives once with its bytes plus three plain arrivals.
       ptx::mbar_init(bar(kBarKvFull + s), kGather ? kConvertWarps : 1);
       ptx::mbar_init(bar(kBarKvEmpty + s), 1);
       ptx::mbar_init(bar(kBarKvGrant + s), 1);
+      ptx::mbar_init(bar(kBarPeerGrant + s), 1);
     }
     ptx::mbar_init(bar(kBarQSmemFull), 1);
     ptx::mbar_init(bar(kBarQEmpty), 1);
@@ -556,6 +558,8 @@ __global__ void __launch_bounds__((kFp8 || kSparse) ? kThreadsGather : kThreads,
           }
           if constexpr (kGather) {
             ptx::mbar_arrive(bar(kBarKvGrant + stage));
+            // FP8: the peer's convert warps may now copy their keys' value half into this stage.
+            if constexpr (kFp8) ptx::mbar_arrive_cluster(ptx::map_peer(bar(kBarPeerGrant + stage), peer));
             continue;
           }
           long long row = (long long)page * kPageRows;
@@ -756,10 +760,150 @@ __global__ void __launch_bounds__((kFp8 || kSparse) ? kThreadsGather : kThreads,
     // Keys past the token's count (and rows of pages outside the pool) are written as zeros and
     // their rows are never read. A page's pool rows: page_table[seq][p] * 64 + key (dense), or
     // the token's compacted valid entries p * 64 + key (sparse).
-    // FP8 rows: all loads of a page are in flight together (registers), then each 16-byte group
-    // of codes is dequantized (code x tile scale, rounded once to bf16) and stored. Sparse bf16
-    // rows: cp.async copies straight into the stage after the grant, zero-filled past the count.
-    if constexpr (kGather) {
+    // FP8 rows: each 16-byte group of codes is dequantized (code x tile scale, rounded once to
+    // bf16) and stored. Sparse bf16 rows: cp.async copies straight into the stage after the
+    // grant, zero-filled past the count.
+    if constexpr (kFp8) {
+      // FP8 rows. Warp cw converts this CTA's keys key0 + 8 cw + [0, 8) across all 512 dims (lane:
+      // dims [16 lane, 16 lane + 16)) into its own group of the page's stage, then copies the
+      // group's four 64-dim chunks of the peer's value half (4 KB, already in the peer's layout)
+      // into the peer's stage with one bulk copy, once the peer's producer has granted that stage
+      // (kBarPeerGrant); the peer does the same for its keys, so each key is loaded and converted
+      // once per pair. Each warp's arrival on its own stage expects the peer's 4 KB.
+      // The next page's codes (cp.async, zero-filled past the token's keys or outside the pool)
+      // land in a per-warp buffer in the unused query chunk while this page converts: 8 keys x
+      // four 128-code tiles (tile t of key i at t KB + i * 128 B), scale quadruples at
+      // kSmFp8Scales. The page-table entry (dense) or the 8 row numbers (sparse) of the page after
+      // next are read one page ahead.
+      static_assert(kQSmemChunks + 1 <= int(kSmKv / kQChunkBytes), "no free query chunk for FP8 codes");
+      const int cw = warp - 6;
+      const uint32_t raw = base + kSmQ + kQSmemChunks * kQChunkBytes + cw * 4096;
+      const uint8_t* raw_p = sm + kSmQ + kQSmemChunks * kQChunkBytes + cw * 4096;
+      const uint32_t rsc = base + kSmFp8Scales + cw * 128;
+      const uint8_t* rsc_p = sm + kSmFp8Scales + cw * 128;
+      const uint32_t peer_chunk0 = uint32_t((kValueHalf - vdim0) / 64);  // the peer's value chunks
+      uint32_t it = 0;
+      uint32_t grant_parity = 0, peer_parity = 0;  // bit s: parity of stage s's next phase
+      Seg s;
+      bool ok = true;
+      while (ok && walker.next(meta, s)) {
+        const int n = meta.unit_n[s.u];
+        const int* pt = kSparse ? nullptr : a.page_table + (long long)a.seq_id[s.u] * a.slots;
+        const int* srows = kSparse ? meta.sparse_rows + (long long)s.u * meta.topk : nullptr;
+        // Row numbers of page p's 8 keys of this warp (-1: zero-filled), from `ent`: the page-table
+        // entry (dense, in ent[0]) or the 8 compacted rows (sparse).
+        auto fetch = [&](int p, int (&ent)[8]) {
+          const int valid = min(kPageRows, n - p * kPageRows);
+          if constexpr (kSparse) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              const int key = key0 + 8 * cw + i;
+              ent[i] = key < valid ? srows[p * kPageRows + key] : -1;
+            }
+          } else {
+            ent[0] = pt[p];
+          }
+        };
+        auto issue = [&](int p, const int (&ent)[8]) {
+          const int valid = min(kPageRows, n - p * kPageRows);
+          long long row0 = 0;
+          bool page_ok = true;
+          if constexpr (!kSparse) {
+            row0 = (long long)ent[0] * kPageRows;
+            page_ok = ent[0] >= 0 && row0 < a.pool_rows;
+            if (!page_ok && cw == 0 && lane == 0)
+              atomicOr(a.meta.header + kHdrError, TQ_DEV_PAGE_RANGE);
+          }
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const int key = key0 + 8 * cw + i;
+            bool live;
+            long long row;
+            if constexpr (kSparse) {
+              live = ent[i] >= 0;
+              row = ent[i];
+            } else {
+              live = page_ok && key < valid;
+              row = row0 + key;
+            }
+            const uint8_t* rp = live ? a.kv + row * a.kv_row_stride : a.kv;
+            ptx::cp_async_16(raw + (lane >> 3) * kAtomBytes + i * 128 + (lane & 7) * 16,
+                             rp + (live ? 16 * lane : 0), live ? 16u : 0u);
+            if (lane == i)
+              ptx::cp_async_16(rsc + i * 16, rp + (live ? kFp8RowCodes : 0), live ? 16u : 0u);
+          }
+          ptx::cp_async_commit();
+        };
+        it += 2;  // the segment's two query slots, filled by the TMA producer
+        int ent[8], nxt[8];
+        fetch(s.p0, ent);
+        issue(s.p0, ent);
+        if (s.np > 1) fetch(s.p0 + 1, nxt);
+        for (int j = 0; j < s.np; ++j, ++it) {
+          const uint32_t stage = it % kStages;
+          // This page's codes: landed, then read into registers.
+          ptx::cp_async_wait_all();
+          __syncwarp();
+          uint4 own[8];
+          float own_sc[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            own[i] = *reinterpret_cast<const uint4*>(raw_p + (lane >> 3) * kAtomBytes + i * 128 +
+                                                     (lane & 7) * 16);
+            own_sc[i] = *reinterpret_cast<const float*>(rsc_p + i * 16 + (lane >> 3) * 4);
+          }
+          __syncwarp();  // the buffer is read: the next page's copies may overwrite it
+          if (j + 1 < s.np) {
+            issue(s.p0 + j + 1, nxt);
+            if (j + 2 < s.np) fetch(s.p0 + j + 2, nxt);  // used one page from now
+          }
+          wt.where = (7 << 24) | int(it & 0xFFFFFF);
+          const bool got =
+              wt.wait<false>(bar(kBarKvGrant + stage), (grant_parity >> stage) & 1u);
+          if (!__all_sync(0xFFFFFFFFu, got)) { ok = false; break; }
+          grant_parity ^= 1u << stage;
+          uint8_t* own_g = sm + kSmKv + stage * kStageBytes + cw * kOwnGroupBytes;
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const uint4& c = own[i];
+            const float sc = own_sc[i];
+            uint4 lo, hi;
+            lo.x = ptx::e4m3x2_scaled_bf16x2(c.x, sc);
+            lo.y = ptx::e4m3x2_scaled_bf16x2(c.x >> 16, sc);
+            lo.z = ptx::e4m3x2_scaled_bf16x2(c.y, sc);
+            lo.w = ptx::e4m3x2_scaled_bf16x2(c.y >> 16, sc);
+            hi.x = ptx::e4m3x2_scaled_bf16x2(c.z, sc);
+            hi.y = ptx::e4m3x2_scaled_bf16x2(c.z >> 16, sc);
+            hi.z = ptx::e4m3x2_scaled_bf16x2(c.w, sc);
+            hi.w = ptx::e4m3x2_scaled_bf16x2(c.w >> 16, sc);
+            // 16-byte units 2 (lane % 4) and + 1 of chunk lane / 4, row i, 128B-swizzled
+            uint8_t* rowp = own_g + (lane >> 2) * kAtomBytes + i * 128;
+            const int u0 = 2 * (lane & 3);
+            *reinterpret_cast<uint4*>(rowp + ((u0 ^ i) << 4)) = lo;
+            *reinterpret_cast<uint4*>(rowp + (((u0 + 1) ^ i) << 4)) = hi;
+          }
+          ptx::fence_proxy_async_smem();  // the MMAs and the bulk copy read through the async proxy
+          __syncwarp();
+          if (lane == 0) ptx::mbar_expect_tx(bar(kBarKvFull + stage), kPeerGroupBytes);
+          wt.where = (8 << 24) | int(it & 0xFFFFFF);
+          const bool free_peer =
+              wt.wait<true>(bar(kBarPeerGrant + stage), (peer_parity >> stage) & 1u);
+          if (!__all_sync(0xFFFFFFFFu, free_peer)) { ok = false; break; }
+          peer_parity ^= 1u << stage;
+          if (lane == 0) {
+            const uint32_t src = base + kSmKv + stage * kStageBytes + cw * kOwnGroupBytes +
+                                 peer_chunk0 * kAtomBytes;
+            const uint32_t dst = ptx::map_peer(
+                base + kSmKv + stage * kStageBytes + kPvxOffset + cw * kPeerGroupBytes, peer);
+            ptx::bulk_copy_to_peer(dst, src, kPeerGroupBytes,
+                                   ptx::map_peer(bar(kBarKvFull + stage), peer));
+          }
+          __syncwarp();
+        }
+      }
+      ptx::cp_async_wait_all();  // no copy into this CTA stays in flight past this point
+      __syncwarp();
+    } else if constexpr (kSparse) {
       const int cw = warp - 6, hl = lane & 15;
       uint32_t it = 0;
       uint32_t grant_parity = 0;  // bit s: parity of the next grant phase of stage s
@@ -794,65 +938,7 @@ __global__ void __launch_bounds__((kFp8 || kSparse) ? kThreadsGather : kThreads,
             if constexpr (kSparse) return (long long)srows[p * kPageRows + k];
             else return row0 + k;
           };
-          if constexpr (kFp8) {
-            uint4 own[8], pr[4];
-            float own_sc[8], pr_sc[4];
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-              const int key = key0 + 8 * cw + i;
-              own[i] = make_uint4(0, 0, 0, 0);
-              own_sc[i] = 0.f;
-              if (page_ok && key < valid) {
-                const uint8_t* rp = a.kv + row_of(key) * a.kv_row_stride;
-                own[i] = __ldg(reinterpret_cast<const uint4*>(rp) + lane);
-                own_sc[i] = __ldg(reinterpret_cast<const float*>(rp + kFp8RowCodes) + (lane >> 3));
-              }
-            }
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              const int key = (kKeysPerCta - key0) + 8 * cw + 2 * q + (lane >> 4);
-              pr[q] = make_uint4(0, 0, 0, 0);
-              pr_sc[q] = 0.f;
-              if (page_ok && key < valid) {
-                const uint8_t* rp = a.kv + row_of(key) * a.kv_row_stride;
-                pr[q] = __ldg(reinterpret_cast<const uint4*>(rp + vdim0) + hl);
-                pr_sc[q] = __ldg(reinterpret_cast<const float*>(rp + kFp8RowCodes) +
-                                 ((vdim0 + 16 * hl) >> 7));
-              }
-            }
-            wt.where = (7 << 24) | int(it & 0xFFFFFF);
-            const bool got =
-                wt.wait<false>(bar(kBarKvGrant + stage), (grant_parity >> stage) & 1u);
-            if (!__all_sync(0xFFFFFFFFu, got)) { ok = false; break; }
-            grant_parity ^= 1u << stage;
-            uint8_t* st_ptr = sm + kSmKv + stage * kStageBytes;
-            auto put16 = [&](uint8_t* rowp, int u0, int r8, const uint4& c, float sc) {
-              uint4 lo, hi;
-              lo.x = ptx::e4m3x2_scaled_bf16x2(c.x, sc);
-              lo.y = ptx::e4m3x2_scaled_bf16x2(c.x >> 16, sc);
-              lo.z = ptx::e4m3x2_scaled_bf16x2(c.y, sc);
-              lo.w = ptx::e4m3x2_scaled_bf16x2(c.y >> 16, sc);
-              hi.x = ptx::e4m3x2_scaled_bf16x2(c.z, sc);
-              hi.y = ptx::e4m3x2_scaled_bf16x2(c.z >> 16, sc);
-              hi.z = ptx::e4m3x2_scaled_bf16x2(c.w, sc);
-              hi.w = ptx::e4m3x2_scaled_bf16x2(c.w >> 16, sc);
-              *reinterpret_cast<uint4*>(rowp + ((u0 ^ r8) << 4)) = lo;
-              *reinterpret_cast<uint4*>(rowp + (((u0 + 1) ^ r8) << 4)) = hi;
-            };
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-              const int r = 8 * cw + i;
-              put16(st_ptr + (r >> 3) * kOwnGroupBytes + (lane >> 2) * kAtomBytes + (r & 7) * 128,
-                    2 * (lane & 3), r & 7, own[i], own_sc[i]);
-            }
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              const int r = 8 * cw + 2 * q + (lane >> 4);
-              put16(st_ptr + kPvxOffset + (r >> 3) * kPeerGroupBytes + (hl >> 2) * kAtomBytes +
-                        (r & 7) * 128,
-                    2 * (hl & 3), r & 7, pr[q], pr_sc[q]);
-            }
-          } else {
+          {
             // Sparse bf16 rows: the page's row numbers (read while the previous page of the
             // segment was in flight, else now), then the grant, then the copies.
             int own_row[8], pr_row[4];

