@@ -771,7 +771,8 @@ __global__ void __launch_bounds__((kFp8 || kSparse) ? kThreadsGather : kThreads,
       // (kBarPeerGrant); the peer does the same for its keys, so each key is loaded and converted
       // once per pair. Each warp's arrival on its own stage expects the peer's 4 KB.
       // The next page's codes (cp.async, zero-filled past the token's keys or outside the pool)
-      // land in a per-warp buffer in the unused query chunk while this page converts: 8 keys x
+      // are copied into a per-warp buffer in the unused query chunk once this page's conversion
+      // has read it, and land while the pair works through the grants and copies: 8 keys x
       // four 128-code tiles (tile t of key i at t KB + i * 128 B), scale quadruples at
       // kSmFp8Scales. The page-table entry (dense) or the 8 row numbers (sparse) of the page after
       // next are read one page ahead.
@@ -841,32 +842,22 @@ __global__ void __launch_bounds__((kFp8 || kSparse) ? kThreadsGather : kThreads,
         if (s.np > 1) fetch(s.p0 + 1, nxt);
         for (int j = 0; j < s.np; ++j, ++it) {
           const uint32_t stage = it % kStages;
-          // This page's codes: landed, then read into registers.
-          ptx::cp_async_wait_all();
-          __syncwarp();
-          uint4 own[8];
-          float own_sc[8];
-#pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            own[i] = *reinterpret_cast<const uint4*>(raw_p + (lane >> 3) * kAtomBytes + i * 128 +
-                                                     (lane & 7) * 16);
-            own_sc[i] = *reinterpret_cast<const float*>(rsc_p + i * 16 + (lane >> 3) * 4);
-          }
-          __syncwarp();  // the buffer is read: the next page's copies may overwrite it
-          if (j + 1 < s.np) {
-            issue(s.p0 + j + 1, nxt);
-            if (j + 2 < s.np) fetch(s.p0 + j + 2, nxt);  // used one page from now
-          }
           wt.where = (7 << 24) | int(it & 0xFFFFFF);
           const bool got =
               wt.wait<false>(bar(kBarKvGrant + stage), (grant_parity >> stage) & 1u);
           if (!__all_sync(0xFFFFFFFFu, got)) { ok = false; break; }
           grant_parity ^= 1u << stage;
+          // This page's codes have landed; convert them key by key from the buffer. The loop is
+          // kept rolled: four code regions share each scheduler's instruction cache, and the
+          // unrolled conversion (~9 KB) made instruction fetch every role's top stall.
+          ptx::cp_async_wait_all();
+          __syncwarp();
           uint8_t* own_g = sm + kSmKv + stage * kStageBytes + cw * kOwnGroupBytes;
-#pragma unroll
+#pragma unroll 1
           for (int i = 0; i < 8; ++i) {
-            const uint4& c = own[i];
-            const float sc = own_sc[i];
+            const uint4 c = *reinterpret_cast<const uint4*>(raw_p + (lane >> 3) * kAtomBytes +
+                                                            i * 128 + (lane & 7) * 16);
+            const float sc = *reinterpret_cast<const float*>(rsc_p + i * 16 + (lane >> 3) * 4);
             uint4 lo, hi;
             lo.x = ptx::e4m3x2_scaled_bf16x2(c.x, sc);
             lo.y = ptx::e4m3x2_scaled_bf16x2(c.x >> 16, sc);
@@ -881,6 +872,11 @@ __global__ void __launch_bounds__((kFp8 || kSparse) ? kThreadsGather : kThreads,
             const int u0 = 2 * (lane & 3);
             *reinterpret_cast<uint4*>(rowp + ((u0 ^ i) << 4)) = lo;
             *reinterpret_cast<uint4*>(rowp + (((u0 + 1) ^ i) << 4)) = hi;
+          }
+          __syncwarp();  // the buffer is read: the next page's copies may overwrite it
+          if (j + 1 < s.np) {
+            issue(s.p0 + j + 1, nxt);
+            if (j + 2 < s.np) fetch(s.p0 + j + 2, nxt);  // used one page from now
           }
           ptx::fence_proxy_async_smem();  // the MMAs and the bulk copy read through the async proxy
           __syncwarp();
