@@ -122,7 +122,8 @@ def _check_rows(r):
         want = (ref[named, :pay].copy().view(np.uint16).astype(np.uint32) << 16).view(np.float32)
         got, want = got.reshape(-1, w).astype(np.float64), want.reshape(-1, w).astype(np.float64)
         rms = np.sqrt(np.mean(want ** 2, axis=-1, keepdims=True))
-        assert np.all(np.abs(got - want) <= 2.0 ** -7 * np.abs(want) + 2.0 ** -9 * rms)
+        # a projected value one bf16 step away is two steps away after the norm's two roundings
+        assert np.all(np.abs(got - want) <= 2.0 ** -6 * np.abs(want) + 2.0 ** -9 * rms)
         assert np.mean(got == want) > 0.97
 
 
