@@ -41,8 +41,12 @@ OUT_REL_L2 = 1e-2
 LSE_ABS = 1e-3
 
 
-def assert_parity(out, lse, ref_out, ref_lse, *, label="", lse_abs=LSE_ABS):
-    """Compare a kernel result (float64 arrays) with the oracle: north-star tolerances."""
+def assert_parity(out, lse, ref_out, ref_lse, *, label="", lse_abs=LSE_ABS,
+                  out_abs=None, out_rel=None):
+    """Compare a kernel result (float64 arrays) with the oracle: north-star tolerances, unless a
+    caller whose inputs differ from the oracle's by a stated amount passes wider ones."""
+    out_abs = OUT_MAX_ABS if out_abs is None else out_abs
+    out_rel = OUT_REL_L2 if out_rel is None else out_rel
     out = np.asarray(out, dtype=np.float64)
     lse = np.asarray(lse, dtype=np.float64)
     assert out.shape == ref_out.shape and lse.shape == ref_lse.shape, label
@@ -54,8 +58,8 @@ def assert_parity(out, lse, ref_out, ref_lse, *, label="", lse_abs=LSE_ABS):
         assert err <= lse_abs, f"{label}: lse max abs err {err:.3e}"
     assert (out[ninf] == 0).all(), f"{label}: empty rows must be exact zeros"
     diff = np.abs(out - ref_out).max() if out.size else 0.0
-    assert diff <= OUT_MAX_ABS, f"{label}: out max abs err {diff:.3e}"
+    assert diff <= out_abs, f"{label}: out max abs err {diff:.3e}"
     denom = np.linalg.norm(ref_out)
     if denom > 0:
         rel = np.linalg.norm(out - ref_out) / denom
-        assert rel <= OUT_REL_L2, f"{label}: out rel L2 {rel:.3e}"
+        assert rel <= out_rel, f"{label}: out rel L2 {rel:.3e}"

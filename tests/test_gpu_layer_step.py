@@ -4,8 +4,9 @@ oracle's chain (prologue oracle, writer oracle, paged attention oracle).
 Every token of each sequence goes through ``tq_mla_prologue`` (its row lands in the paged pool),
 then the last token of each sequence attends over its whole sequence with ``tq_mla_decode``.
 The reference's no-RoPE model sizes (hidden 4096, Q rank 1536, 64 heads of 256, scale 256^-0.5)
-with bf16 and FP8 rows; the 576-wide RoPE form with 128 heads. The output tolerances are the
-attention path's (``assert_parity``)."""
+with bf16 and FP8 rows; the 576-wide RoPE form with 128 heads. The attention step is checked on
+the prologue's own output at the attention path's tolerances, and the whole chain against the
+oracle chain with an lse bound that covers the spread of q (``assert_parity``)."""
 
 import numpy as np
 import pytest
@@ -80,7 +81,26 @@ def test_prologue_then_decode_matches_the_oracle_chain(cuda_device, fmt, heads, 
         rows = ofp8.operand_rows(flat)
     else:
         rows = (flat.copy().view(np.uint16).astype(np.uint32) << 16).view(np.float32).astype(np.float64)
+    got_out, got_lse = out.double().cpu().numpy(), lse.double().cpu().numpy()
+    # 1. the attention step on exactly what the prologue produced (its q, the pool it wrote):
+    #    the attention path's own tolerances
+    pool_np = pool.cpu().numpy().reshape(-1, ROW[fmt])
+    if fmt == _abi.KV_FP8_E4M3:
+        own_rows = ofp8.operand_rows(pool_np)
+    else:
+        own_rows = (pool_np.copy().view(np.uint16).astype(np.uint32) << 16).view(
+            np.float32).astype(np.float64)
+    own_out, own_lse = omla.paged_attention(q.double().cpu().numpy(), own_rows, table,
+                                            np.arange(seqs), kv_len - 1, kv_len, scale=scale,
+                                            value_dim=512)
+    assert_parity(got_out, got_lse, own_out, own_lse, label=f"decode on the prologue's output ({fmt})")
+    # 2. the whole chain against the oracle chain: q differs from the float64 oracle's by bf16
+    #    rounding propagated through the projections (relative L2 ~2^-8), which moves the scores
+    #    and so lse by up to a few 1e-3. FP8 rows: a projected value one bf16 step away can land
+    #    one E4M3 step away (up to 12.5% of the value; 1-3% of the codes), so the outputs get
+    #    3x the attention path's bounds there.
     ref_out, ref_lse = omla.paged_attention(q_ref, rows, table, np.arange(seqs), kv_len - 1,
                                             kv_len, scale=scale, value_dim=512)
-    assert_parity(out.double().cpu().numpy(), lse.double().cpu().numpy(), ref_out, ref_lse,
-                  label=f"prologue -> decode (format {fmt})")
+    wide = 3.0 if fmt == _abi.KV_FP8_E4M3 else 1.0
+    assert_parity(got_out, got_lse, ref_out, ref_lse, label=f"prologue -> decode ({fmt})",
+                  lse_abs=5e-3, out_abs=wide * 2e-2, out_rel=wide * 1e-2)
