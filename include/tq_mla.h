@@ -300,7 +300,9 @@ int32_t tq_kv_write(const TqKvWriteSpec* spec, int32_t* device_flags, void* stre
  * TQ_DEV_SEQ_RANGE, TQ_DEV_TABLE_SHORT or TQ_DEV_PAGE_RANGE in `device_flags` (a device int32,
  * may be null); its q is still produced. The workspace (tq_mla_prologue_workspace_bytes, 256-byte
  * aligned) holds the intermediates and cuBLAS's scratch; the first call on a device creates
- * that device's cuBLAS handle, so make it before capturing a stream. Calls are serialised on
+ * that device's cuBLAS handle and the side stream on which the cache branch (kv_a projection,
+ * RoPE, write) runs beside the query branch (forked from and joined back into `stream` with
+ * events), so make it before capturing a stream. Calls are serialised on
  * the host (one cuBLAS handle per device). No reference counterpart exists beyond the plan
  * line above. */
 typedef struct {

@@ -13,6 +13,9 @@
 //   6. kvf = x . w_kva^T                plain GEMM                       [T, W]
 //   7. tq_kv_write: bf16(rms(kvf[:512])) * kv_norm and the row written (FP8 rows quantized) to the
 //      token's pool slot through the page table
+// Steps 6-7 (the cache branch) run on a per-device side stream, forked from the caller's stream
+// by an event and joined back into it before the call returns, beside steps 1-5 (the query
+// branch) on the caller's stream; the pattern is graph-capturable.
 // The GEMMs are cuBLAS (opened at run time as libcublas.so.12: a process that already has it,
 // e.g. through PyTorch, shares that copy); everything else is this library's kernels. At decode
 // sizes the step is HBM-bound on the weights (w_qb and w_uk dominate). The q norm accumulates
@@ -193,6 +196,30 @@ int sm_count(int device) {
   return n;
 }
 
+// Per device: a non-blocking side stream and the fork / join events of the two branches, created
+// on the first call with that device current.
+struct Side {
+  cudaStream_t stream = nullptr;
+  cudaEvent_t fork = nullptr, join = nullptr;
+};
+
+Side* side_for(int device) {
+  static std::mutex mu;
+  static Side cache[128];
+  if (device < 0 || device >= 128) return nullptr;
+  std::lock_guard<std::mutex> lock(mu);
+  Side& sd = cache[device];
+  if (!sd.stream) {
+    Side made;
+    if (cudaStreamCreateWithFlags(&made.stream, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaEventCreateWithFlags(&made.fork, cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventCreateWithFlags(&made.join, cudaEventDisableTiming) != cudaSuccess)
+      return nullptr;
+    sd = made;
+  }
+  return &sd;
+}
+
 // Row-major C[M, N] = A[M, K] . B[N, K]^T with A, B, C packed: cuBLAS sees the column-major
 // C^T = B . A^T (op(B) = T).
 cublasStatus_t gemm_nt(const Blas* b, cublasHandle_t h, const void* A, const void* B, void* C,
@@ -254,49 +281,9 @@ extern "C" int32_t tq_mla_prologue(const TqPrologueSpec* spec, void* workspace,
   const int* pos = reinterpret_cast<const int*>(s.pos.device_address);
   const double log2_theta = std::log2(double(s.rope_theta));
   const long long cap = 8ll * sms;
-  {
-    std::lock_guard<std::mutex> lock(blas_mutex());
-    cublasHandle_t h = handle_for(device);
-    if (!h) return fail("cublas_handle", TQ_ERR_CUDA);
-    if (b->set_stream(h, cs) != CUBLAS_STATUS_SUCCESS ||
-        b->set_workspace(h, ws + l.scratch, kCublasScratch) != CUBLAS_STATUS_SUCCESS)
-      return fail("cublas_setup", TQ_ERR_CUDA);
-    // 1-2: cq = rms(x . w_qa^T) * q_norm
-    if (gemm_nt(b, h, x, reinterpret_cast<const void*>(s.w_qa.device_address), cq, T, rq, dm) !=
-        CUBLAS_STATUS_SUCCESS)
-      return fail("gemm_q_a", TQ_ERR_CUDA);
-    rms_rows_kernel<<<int(T < cap ? T : cap), 256, 0, cs>>>(
-        cq, rq, T, reinterpret_cast<const uint16_t*>(s.q_norm.device_address), s.q_eps);
-    // 3: qf = cq . w_qb^T
-    if (gemm_nt(b, h, cq, reinterpret_cast<const void*>(s.w_qb.device_address), qf, T,
-                H * (dn + dr), rq) != CUBLAS_STATUS_SUCCESS)
-      return fail("gemm_q_b", TQ_ERR_CUDA);
-    // 4: per head h, row-major q[:, h, :512] = qf[:, h, :Dn] . w_uk[h]; column-major that is
-    // q^T = w_uk[h]^T . qf^T with w_uk[h] seen as a 512 x Dn matrix (ld 512), qf[:, h] as
-    // Dn x T (ld H (Dn + Dr)) and q[:, h] as 512 x T (ld H W).
-    const float one = 1.f, zero = 0.f;
-    if (b->gemm_batched(h, CUBLAS_OP_N, CUBLAS_OP_N, kLatent, T, dn, &one,
-                        reinterpret_cast<const void*>(s.w_uk.device_address), CUDA_R_16BF, kLatent,
-                        (long long)dn * kLatent, qf, CUDA_R_16BF, H * (dn + dr), dn + dr, &zero, q,
-                        CUDA_R_16BF, H * width, width, H, CUBLAS_COMPUTE_32F,
-                        CUBLAS_GEMM_DEFAULT) != CUBLAS_STATUS_SUCCESS)
-      return fail("gemm_absorb", TQ_ERR_CUDA);
-    // 6: kvf = x . w_kva^T
-    if (gemm_nt(b, h, x, reinterpret_cast<const void*>(s.w_kva.device_address), kvf, T, width,
-                dm) != CUBLAS_STATUS_SUCCESS)
-      return fail("gemm_kv_a", TQ_ERR_CUDA);
-  }
-  if (dr) {
-    // 5: the RoPE slices of q, and of kvf in place
-    const long long qrows = (long long)T * H, qblocks = (qrows + 7) / 8;
-    rope_rows_kernel<<<int(qblocks < cap ? qblocks : cap), 256, 0, cs>>>(
-        qf + dn, dn + dr, q + kLatent, width, qrows, H, pos, log2_theta);
-    const long long kblocks = ((long long)T + 7) / 8;
-    rope_rows_kernel<<<int(kblocks < cap ? kblocks : cap), 256, 0, cs>>>(
-        kvf + kLatent, width, kvf + kLatent, width, T, 1, pos, log2_theta);
-  }
-  if (cudaGetLastError() != cudaSuccess) return fail("launch", TQ_ERR_CUDA);
-  // 7: norm of the latent part and the paged write (FP8 rows quantized), by the cache writer
+  Side* sd = side_for(device);
+  if (!sd) return fail("side_stream", TQ_ERR_CUDA);
+  // The cache half of the step, fed to the writer: kvf viewed as bf16 [T, W] rows.
   TqKvWriteSpec w;
   std::memset(&w, 0, sizeof(w));
   w.src.shape[0] = T64;
@@ -314,5 +301,72 @@ extern "C" int32_t tq_mla_prologue(const TqPrologueSpec* spec, void* workspace,
   w.kv_format = s.kv_format;
   w.norm_weight = s.kv_norm;
   w.norm_eps = s.kv_eps;
-  return tq_kv_write(&w, device_flags, stream, err);
+  {
+    std::lock_guard<std::mutex> lock(blas_mutex());
+    cublasHandle_t h = handle_for(device);
+    if (!h) return fail("cublas_handle", TQ_ERR_CUDA);
+    // Fork: the cache branch (steps 6-7) runs on this device's side stream beside the query
+    // branch (steps 1-5) on the caller's stream; each branch has its own half of the cuBLAS
+    // scratch. Both are joined back into the caller's stream before returning, also on errors.
+    if (cudaEventRecord(sd->fork, cs) != cudaSuccess ||
+        cudaStreamWaitEvent(sd->stream, sd->fork, 0) != cudaSuccess)
+      return fail("fork", TQ_ERR_CUDA);
+    const char* bad = nullptr;
+    int32_t status = TQ_OK;
+    constexpr uint64_t kHalf = kCublasScratch / 2;
+    // 6: kvf = x . w_kva^T, its RoPE slice rotated in place; 7: norm and paged write.
+    if (b->set_stream(h, sd->stream) != CUBLAS_STATUS_SUCCESS ||
+        b->set_workspace(h, ws + l.scratch + kHalf, kHalf) != CUBLAS_STATUS_SUCCESS)
+      bad = "cublas_setup";
+    else if (gemm_nt(b, h, x, reinterpret_cast<const void*>(s.w_kva.device_address), kvf, T,
+                     width, dm) != CUBLAS_STATUS_SUCCESS)
+      bad = "gemm_kv_a";
+    if (!bad && dr) {
+      const long long kblocks = ((long long)T + 7) / 8;
+      rope_rows_kernel<<<int(kblocks < cap ? kblocks : cap), 256, 0, sd->stream>>>(
+          kvf + kLatent, width, kvf + kLatent, width, T, 1, pos, log2_theta);
+      if (cudaGetLastError() != cudaSuccess) bad = "launch";
+    }
+    if (!bad) {
+      status = tq_kv_write(&w, device_flags, sd->stream, err);
+      if (status != TQ_OK) bad = "kv_write";
+    }
+    // 1-2: cq = rms(x . w_qa^T) * q_norm; 3: qf = cq . w_qb^T
+    if (!bad && (b->set_stream(h, cs) != CUBLAS_STATUS_SUCCESS ||
+                 b->set_workspace(h, ws + l.scratch, kHalf) != CUBLAS_STATUS_SUCCESS))
+      bad = "cublas_setup";
+    if (!bad && gemm_nt(b, h, x, reinterpret_cast<const void*>(s.w_qa.device_address), cq, T,
+                        rq, dm) != CUBLAS_STATUS_SUCCESS)
+      bad = "gemm_q_a";
+    if (!bad) {
+      rms_rows_kernel<<<int(T < cap ? T : cap), 256, 0, cs>>>(
+          cq, rq, T, reinterpret_cast<const uint16_t*>(s.q_norm.device_address), s.q_eps);
+      if (gemm_nt(b, h, cq, reinterpret_cast<const void*>(s.w_qb.device_address), qf, T,
+                  H * (dn + dr), rq) != CUBLAS_STATUS_SUCCESS)
+        bad = "gemm_q_b";
+    }
+    // 4: per head h, row-major q[:, h, :512] = qf[:, h, :Dn] . w_uk[h]; column-major that is
+    // q^T = w_uk[h]^T . qf^T with w_uk[h] seen as a 512 x Dn matrix (ld 512), qf[:, h] as
+    // Dn x T (ld H (Dn + Dr)) and q[:, h] as 512 x T (ld H W).
+    const float one = 1.f, zero = 0.f;
+    if (!bad && b->gemm_batched(h, CUBLAS_OP_N, CUBLAS_OP_N, kLatent, T, dn, &one,
+                                reinterpret_cast<const void*>(s.w_uk.device_address), CUDA_R_16BF,
+                                kLatent, (long long)dn * kLatent, qf, CUDA_R_16BF, H * (dn + dr),
+                                dn + dr, &zero, q, CUDA_R_16BF, H * width, width, H,
+                                CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT) != CUBLAS_STATUS_SUCCESS)
+      bad = "gemm_absorb";
+    // 5: the RoPE slices of q
+    if (!bad && dr) {
+      const long long qrows = (long long)T * H, qblocks = (qrows + 7) / 8;
+      rope_rows_kernel<<<int(qblocks < cap ? qblocks : cap), 256, 0, cs>>>(
+          qf + dn, dn + dr, q + kLatent, width, qrows, H, pos, log2_theta);
+    }
+    if (!bad && cudaGetLastError() != cudaSuccess) bad = "launch";
+    // Join.
+    if (cudaEventRecord(sd->join, sd->stream) != cudaSuccess ||
+        cudaStreamWaitEvent(cs, sd->join, 0) != cudaSuccess)
+      return fail("join", TQ_ERR_CUDA);
+    if (bad) return status != TQ_OK ? status : fail(bad, TQ_ERR_CUDA);
+  }
+  return fail(nullptr, TQ_OK);
 }
