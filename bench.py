@@ -1329,7 +1329,8 @@ def run_ours(args, world, rank, local_rank):
 def run_context(args, world, rank, local_rank):
     """The long-context batch as configured: every sequence's 131072 cached positions are split
     over the ranks by page range. Per step each rank decodes its range into f32 partials, then
-    ``tq_mla_context_merge`` (NCCL all-gather of the partials + the LSE merge kernel) leaves the
+    ``tq_mla_context_merge`` (NCCL all-gather of the partials + the LSE merge kernel; with
+    ``--merge peer`` one kernel reading the peers' partials over NVLink) leaves the
     merged output on every rank. ``value`` = the batch's query tokens / the slowest rank's step
     time (strong scaling: the work is fixed, the ranks share it)."""
     import torch
@@ -1342,19 +1343,30 @@ def run_context(args, world, rank, local_rank):
     part = tdist.context_split(full, world, rank)
     batch = inputs.materialize(part, dev)
     T, H = part.tokens, part.heads
-    p_out = torch.empty((T, H, 512), dtype=torch.float32, device=dev)
-    p_lse = torch.empty((T, H), dtype=torch.float32, device=dev)
+    comm = tdist.Comm.from_process_group()
+    peer = args.merge == "peer"
+    pm = tdist.PeerMerge(comm, T, H) if peer else None
+    if peer:  # the partials are decoded straight into this rank's exchange region
+        p_out, p_lse = pm.part_out, pm.part_lse
+    else:
+        p_out = torch.empty((T, H, 512), dtype=torch.float32, device=dev)
+        p_lse = torch.empty((T, H), dtype=torch.float32, device=dev)
     out = torch.empty((T, H, 512), dtype=torch.bfloat16, device=dev)
     lse = torch.empty((T, H), dtype=torch.float32, device=dev)
     launch = ops.MlaLaunch(batch.q, batch.kv, batch.page_table, batch.seq_id, batch.q_pos,
                            batch.kv_len, p_out, p_lse, scale=part.scale,
                            query_counts=batch.query_counts)
-    comm = tdist.Comm.from_process_group()
     stream = torch.cuda.current_stream(dev)
+
+    def merge():
+        if peer:
+            pm.merge(out, lse, stream)
+        else:
+            tdist.context_merge(comm, p_out, p_lse, out, lse, stream)
 
     def step():
         launch(stream)
-        tdist.context_merge(comm, p_out, p_lse, out, lse, stream)
+        merge()
 
     def max_over_ranks(x):
         t = torch.tensor([x], dtype=torch.float64, device=dev)
@@ -1383,7 +1395,7 @@ def run_context(args, world, rank, local_rank):
         torch.cuda.synchronize(dev)
         ev0.record(stream)
         for _ in range(args.steps):
-            tdist.context_merge(comm, p_out, p_lse, out, lse, stream)
+            merge()
         ev1.record(stream)
         torch.cuda.synchronize(dev)
         merge_ms = max_over_ranks(ev0.elapsed_time(ev1)) / args.steps
@@ -1446,9 +1458,12 @@ def run_context(args, world, rank, local_rank):
         merged_check["pass"] = bool(merged_check["out_max_abs"] <= 2e-2 and
                                     merged_check["out_rel_l2"] <= 1e-2 and
                                     merged_check["lse_max_abs"] <= 1e-3)
+        merge_err = pm.device_error(stream) if peer else 0
         ok_all = max_over_ranks(0.0 if (part_check["pass"] and merged_check["pass"] and
-                                        err == 0) else 1.0) == 0.0
+                                        err == 0 and merge_err == 0) else 1.0) == 0.0
     finally:
+        if pm is not None:
+            pm.destroy()
         comm.destroy()
 
     hbm, tc_burst, tc_sus, src = peaks()
@@ -1469,8 +1484,10 @@ def run_context(args, world, rank, local_rank):
                                                  "merged result out"},
         "gpu_launches": (LAUNCHES_PER_STEP + 1) * args.steps,
         "merge": {"ms": merge_ms, "received_bytes_per_rank": gather_bytes,
-                  "what": "tq_mla_context_merge: NCCL all-gather of f32 partials + lse, then "
-                          "the LSE merge kernel", "kernel_ms": kernel_ms},
+                  "what": ("tq_peer_merge: one kernel per rank reads the peers' f32 partials and "
+                           "lse over NVLink (CUDA IPC mappings) and merges them" if peer else
+                           "tq_mla_context_merge: NCCL all-gather of f32 partials + lse, then "
+                           "the LSE merge kernel"), "kernel_ms": kernel_ms},
         "roofline": {"bound": "hbm", "achieved": ach, "peak": hbm, "unit": "GB/s",
                      "frac": ach / hbm, "traffic": None, "kernel": "mla_paged_kernel",
                      "kernel_ms_per_launch": kernel_ms,
@@ -1505,6 +1522,10 @@ def main():
                     help="weak: N ranks hold N times the one-GPU batch; strong: the batch stays "
                          "fixed and is shared (longctx: each sequence's pages split over the "
                          "ranks, merged over NCCL)")
+    ap.add_argument("--merge", choices=["nccl", "peer"], default="nccl",
+                    help="long-context split (--config longctx --scaling strong, N > 1): merge "
+                         "the ranks' partials by an NCCL all-gather + merge kernel, or by one "
+                         "kernel reading the peers' partials over NVLink")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--clock-log", default=None,
                     help="file for the nvidia-smi clock samples ({rank} is replaced)")

@@ -215,6 +215,37 @@ typedef struct {
 } TqContextMergeParams;
 int32_t tq_mla_context_merge(const TqContextMergeParams* params, TqComm* comm, void* stream);
 
+/* The same merge over NVLink peer memory, with no collective on the step (the planned "NVLink
+ * LSE merge" of decode context parallelism, docs/ARCHITECTURE.md:240-241,313):
+ *   tq_peer_merge_create     collective over `comm` (all ranks, same tokens and heads, each with
+ *                            its GPU current): allocates this rank's exchange region (a 256-byte
+ *                            header, f32 partial out [T, H, 512], f32 lse [T, H]), exports it
+ *                            with CUDA IPC and opens every peer's (handles all-gathered once
+ *                            over NCCL). Up to 8 ranks.
+ *   tq_peer_merge_partials   device addresses of this rank's partials in its region: decode
+ *                            into them (tq_mla_decode with f32 out, packed [T, H, 512] and lse)
+ *   tq_peer_merge            one kernel on `stream`, after that decode: tells every peer this
+ *                            rank's partials are ready, waits for theirs, merges all ranks' rows
+ *                            by log-sum-exp reading the peers' partials over NVLink into out
+ *                            (bf16 or f32 [T, H, 512], strides in bytes, 16-byte aligned) and lse
+ *                            f32 [T, H], then waits until every peer has read this rank's
+ *                            partials, so the next decode may overwrite them. Every rank calls it
+ *                            once per step, in the same order; the step counter lives on the
+ *                            device, so a captured decode + merge replays.
+ *   tq_peer_merge_read_error the region's device error flags (synchronises `stream`): a wait
+ *                            that gave up after ~2 s (a peer that never arrived) sets
+ *                            TQ_DEV_WAIT_TIMEOUT, and every later merge on the plan returns at
+ *                            once; destroy it (and the communicator) then.
+ *   tq_peer_merge_destroy    collective: waits for the device, closes the peers' mappings and
+ *                            frees the region (two small NCCL barriers). */
+typedef struct TqPeerMerge TqPeerMerge;
+int32_t tq_peer_merge_create(TqComm* comm, uint64_t tokens, uint64_t heads, TqPeerMerge** pm);
+int32_t tq_peer_merge_partials(const TqPeerMerge* pm, uint64_t* part_out, uint64_t* part_lse);
+int32_t tq_peer_merge(TqPeerMerge* pm, uint64_t out, uint64_t lse, uint64_t out_stride_token,
+                      uint64_t out_stride_head, int32_t out_dtype, void* stream);
+int32_t tq_peer_merge_read_error(const TqPeerMerge* pm, void* stream, int32_t* flags);
+int32_t tq_peer_merge_destroy(TqPeerMerge* pm);
+
 /* Device error flag of the last launch that used `workspace` (synchronises `stream`). */
 int32_t tq_mla_read_device_error(const void* workspace, void* stream, int32_t* flags);
 

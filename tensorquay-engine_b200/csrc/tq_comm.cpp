@@ -12,7 +12,12 @@
 //
 // tq_mla_context_merge = one grouped NCCL all-gather of the f32 partial outputs and their lse
 // into caller-owned receive buffers on the caller's stream, then tq_mla_combine (the LSE merge
-// kernel) over the G gathered parts. Nothing here reads another GPU's memory directly.
+// kernel) over the G gathered parts.
+//
+// tq_peer_merge_* = the same merge without a collective on the step: every rank's partials live
+// in an exchange region exported with CUDA IPC; the handles are all-gathered once over NCCL at
+// creation, and each step one kernel per rank reads its peers' partials over NVLink
+// (tq_peer_merge.cu). Plain peer loads and stores only: no multicast of any kind.
 
 #include <cuda_runtime.h>
 #include <dlfcn.h>
@@ -70,6 +75,48 @@ struct TqComm {
   int32_t device;
   int32_t failed;  // a collective failed: only abort/destroy remain
 };
+
+struct TqPeerMerge {
+  TqComm* comm;
+  int32_t nranks, rank, device;
+  uint64_t tokens, heads, bytes;
+  uint8_t* own;                             // this rank's exchange region (cudaMalloc)
+  uint8_t* mapped[tq::kPeerMaxRanks];       // every rank's region as mapped on this device
+};
+
+namespace {
+
+// A small all-gather over `comm` on a private stream, waited for: `bytes` from this rank, the
+// ranks' contributions in rank order in `host_out`.
+int32_t gather_bytes(TqComm* comm, const void* mine, uint64_t bytes, void* host_out) {
+  const NcclApi* api = nccl();
+  if (!api || comm->failed) return TQ_ERR_COMM;
+  uint8_t* d = nullptr;
+  cudaStream_t st = nullptr;
+  int32_t rc = TQ_OK;
+  if (cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking) != cudaSuccess) return TQ_ERR_CUDA;
+  if (cudaMalloc(&d, bytes * uint64_t(comm->nranks)) != cudaSuccess) {
+    cudaStreamDestroy(st);
+    return TQ_ERR_CUDA;
+  }
+  if (cudaMemcpyAsync(d + bytes * uint64_t(comm->rank), mine, bytes, cudaMemcpyHostToDevice,
+                      st) != cudaSuccess)
+    rc = TQ_ERR_CUDA;
+  if (rc == TQ_OK && api->all_gather(d + bytes * uint64_t(comm->rank), d, size_t(bytes), ncclInt8,
+                                     comm->comm, st) != ncclSuccess) {
+    comm->failed = 1;
+    rc = TQ_ERR_COMM;
+  }
+  if (rc == TQ_OK && (cudaMemcpyAsync(host_out, d, bytes * uint64_t(comm->nranks),
+                                      cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+                      cudaStreamSynchronize(st) != cudaSuccess))
+    rc = TQ_ERR_CUDA;
+  cudaFree(d);
+  cudaStreamDestroy(st);
+  return rc;
+}
+
+}  // namespace
 
 extern "C" {
 
@@ -180,6 +227,133 @@ int32_t tq_mla_context_merge(const TqContextMergeParams* p, TqComm* comm, void* 
   cp.out_stride_head = p->out_stride_head;
   cp.out_dtype = p->out_dtype;
   return tq_mla_combine(&cp, stream);
+}
+
+int32_t tq_peer_merge_create(TqComm* comm, uint64_t tokens, uint64_t heads, TqPeerMerge** out) {
+  if (!comm || !out) return TQ_ERR_INVALID_ARGUMENT;
+  *out = nullptr;
+  if (comm->failed) return TQ_ERR_COMM;
+  if (comm->nranks < 1 || comm->nranks > tq::kPeerMaxRanks) return TQ_ERR_UNSUPPORTED;
+  const uint64_t rows = tokens * heads;
+  if (tokens == 0 || heads == 0 || heads > (uint64_t(1) << 31) || rows / heads != tokens ||
+      rows > (uint64_t(1) << 32))
+    return TQ_ERR_INVALID_ARGUMENT;
+  int device = 0;
+  if (cudaGetDevice(&device) != cudaSuccess) return TQ_ERR_CUDA;
+  if (device != comm->device) return TQ_ERR_INVALID_ARGUMENT;
+  TqPeerMerge* pm = new (std::nothrow) TqPeerMerge;
+  if (!pm) return TQ_ERR_INVALID_ARGUMENT;
+  std::memset(pm, 0, sizeof(*pm));
+  pm->comm = comm;
+  pm->nranks = comm->nranks;
+  pm->rank = comm->rank;
+  pm->device = device;
+  pm->tokens = tokens;
+  pm->heads = heads;
+  pm->bytes = (tq::kPeerHeaderBytes + rows * 2048 + rows * 4 + 255) & ~uint64_t(255);
+  if (cudaMalloc(&pm->own, pm->bytes) != cudaSuccess) {
+    delete pm;
+    return TQ_ERR_CUDA;
+  }
+  // The header is zero before any peer can learn the region exists.
+  if (cudaMemset(pm->own, 0, tq::kPeerHeaderBytes) != cudaSuccess ||
+      cudaDeviceSynchronize() != cudaSuccess) {
+    cudaFree(pm->own);
+    delete pm;
+    return TQ_ERR_CUDA;
+  }
+  pm->mapped[pm->rank] = pm->own;
+  cudaIpcMemHandle_t mine;
+  cudaIpcMemHandle_t all[tq::kPeerMaxRanks];
+  int32_t rc = TQ_OK;
+  if (pm->nranks > 1) {
+    if (cudaIpcGetMemHandle(&mine, pm->own) != cudaSuccess) rc = TQ_ERR_CUDA;
+    if (rc == TQ_OK) rc = gather_bytes(comm, &mine, sizeof(mine), all);
+    for (int r = 0; rc == TQ_OK && r < pm->nranks; ++r) {
+      if (r == pm->rank) continue;
+      void* p = nullptr;
+      if (cudaIpcOpenMemHandle(&p, all[r], cudaIpcMemLazyEnablePeerAccess) != cudaSuccess)
+        rc = TQ_ERR_CUDA;
+      else
+        pm->mapped[r] = static_cast<uint8_t*>(p);
+    }
+  }
+  if (rc != TQ_OK) {
+    for (int r = 0; r < pm->nranks; ++r)
+      if (r != pm->rank && pm->mapped[r]) cudaIpcCloseMemHandle(pm->mapped[r]);
+    cudaFree(pm->own);
+    delete pm;
+    return rc;
+  }
+  *out = pm;
+  return TQ_OK;
+}
+
+int32_t tq_peer_merge_partials(const TqPeerMerge* pm, uint64_t* part_out, uint64_t* part_lse) {
+  if (!pm || !part_out || !part_lse) return TQ_ERR_INVALID_ARGUMENT;
+  const uint64_t rows = pm->tokens * pm->heads;
+  *part_out = reinterpret_cast<uint64_t>(pm->own) + tq::kPeerHeaderBytes;
+  *part_lse = *part_out + rows * 2048;
+  return TQ_OK;
+}
+
+int32_t tq_peer_merge(TqPeerMerge* pm, uint64_t out, uint64_t lse, uint64_t out_stride_token,
+                      uint64_t out_stride_head, int32_t out_dtype, void* stream) {
+  if (!pm || !out || !lse) return TQ_ERR_INVALID_ARGUMENT;
+  if (out_dtype != TQ_DTYPE_BF16 && out_dtype != TQ_DTYPE_F32) return TQ_ERR_INVALID_ARGUMENT;
+  if ((out | out_stride_token | out_stride_head) % 16 || lse % 4) return TQ_ALIGNMENT;
+  if (out_stride_head < (out_dtype == TQ_DTYPE_F32 ? 2048u : 1024u) ||
+      out_stride_token < out_stride_head * pm->heads)
+    return TQ_STRIDE;
+  int device = 0;
+  if (cudaGetDevice(&device) != cudaSuccess) return TQ_ERR_CUDA;
+  if (device != pm->device) return TQ_ERR_INVALID_ARGUMENT;
+  tq::PeerMergeLaunch L;
+  std::memset(&L, 0, sizeof(L));
+  for (int r = 0; r < pm->nranks; ++r) L.regions[r] = pm->mapped[r];
+  L.nranks = pm->nranks;
+  L.rank = pm->rank;
+  L.tokens = pm->tokens;
+  L.heads = pm->heads;
+  L.out = reinterpret_cast<uint8_t*>(out);
+  L.lse = reinterpret_cast<float*>(lse);
+  L.out_stride_token = out_stride_token;
+  L.out_stride_head = out_stride_head;
+  L.out_bf16 = out_dtype == TQ_DTYPE_BF16;
+  return tq::peer_merge_launch(L, stream);
+}
+
+int32_t tq_peer_merge_read_error(const TqPeerMerge* pm, void* stream, int32_t* flags) {
+  if (!pm || !flags) return TQ_ERR_INVALID_ARGUMENT;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int32_t v = 0;
+  if (cudaMemcpyAsync(&v, pm->own + 4 * tq::kPeerHdrError, sizeof(v), cudaMemcpyDeviceToHost,
+                      st) != cudaSuccess ||
+      cudaStreamSynchronize(st) != cudaSuccess)
+    return TQ_ERR_CUDA;
+  *flags = v;
+  return TQ_OK;
+}
+
+int32_t tq_peer_merge_destroy(TqPeerMerge* pm) {
+  if (!pm) return TQ_ERR_INVALID_ARGUMENT;
+  int32_t rc = TQ_OK;
+  if (cudaDeviceSynchronize() != cudaSuccess) rc = TQ_ERR_CUDA;
+  uint8_t token = 0, tokens[tq::kPeerMaxRanks];
+  // Every rank has stopped touching the others' regions before any mapping goes away, and every
+  // mapping of a region is closed before its owner frees it.
+  if (pm->nranks > 1 && !pm->comm->failed) {
+    if (gather_bytes(pm->comm, &token, 1, tokens) != TQ_OK) rc = TQ_ERR_COMM;
+  }
+  for (int r = 0; r < pm->nranks; ++r)
+    if (r != pm->rank && pm->mapped[r] && cudaIpcCloseMemHandle(pm->mapped[r]) != cudaSuccess)
+      rc = TQ_ERR_CUDA;
+  if (pm->nranks > 1 && !pm->comm->failed) {
+    if (gather_bytes(pm->comm, &token, 1, tokens) != TQ_OK) rc = TQ_ERR_COMM;
+  }
+  if (cudaFree(pm->own) != cudaSuccess) rc = TQ_ERR_CUDA;
+  delete pm;
+  return rc;
 }
 
 }  // extern "C"

@@ -26,4 +26,25 @@ int32_t philox_words(uint64_t seed, uint64_t stream, uint64_t start, uint32_t* o
                      uint64_t count);
 float philox_uniform_f32(uint32_t word);
 
+// Exchange region of the peer-memory context merge (tq_peer_merge.cu): a 256-byte header of u32
+// words, then f32 partial out [T, H, 512] and f32 lse [T, H].
+constexpr int kPeerMaxRanks = 8;
+constexpr int kPeerHdrStep = 0;     // this rank's merge counter (device-side, graph-replayable)
+constexpr int kPeerHdrError = 1;    // sticky device error flags (TQ_DEV_WAIT_TIMEOUT)
+constexpr int kPeerHdrBlocks = 2;   // blocks of the running merge that have finished
+constexpr int kPeerHdrReady = 16;   // [kPeerMaxRanks] rank r's partials of step k: k + 1
+constexpr int kPeerHdrDone = 32;    // [kPeerMaxRanks] rank r has read them: k + 1
+constexpr uint64_t kPeerHeaderBytes = 256;
+
+struct PeerMergeLaunch {
+  const uint8_t* regions[kPeerMaxRanks];  // every rank's region as mapped on this device
+  int nranks, rank;
+  uint64_t tokens, heads;
+  uint8_t* out;
+  float* lse;
+  uint64_t out_stride_token, out_stride_head;
+  int out_bf16;
+};
+int32_t peer_merge_launch(const PeerMergeLaunch& launch, void* stream);
+
 }  // namespace tq

@@ -127,6 +127,11 @@ PROTOTYPES = {
     "tq_comm_destroy": (_I32, [_VP]),
     "tq_comm_rank": (_I32, [_VP, _P(_I32), _P(_I32)]),
     "tq_mla_context_merge": (_I32, [_P(TqContextMergeParams), _VP, _VP]),
+    "tq_peer_merge_create": (_I32, [_VP, _U64, _U64, _P(_VP)]),
+    "tq_peer_merge_partials": (_I32, [_VP, _P(_U64), _P(_U64)]),
+    "tq_peer_merge": (_I32, [_VP, _U64, _U64, _U64, _U64, _I32, _VP]),
+    "tq_peer_merge_read_error": (_I32, [_VP, _VP, _P(_I32)]),
+    "tq_peer_merge_destroy": (_I32, [_VP]),
     "tq_mla_set_kernel_timer": (_I32, [_VP, _VP]),
     "tq_mla_decode_no_alloc": (_I32, [_P(TqMlaParams), _VP, _P(TqContractError)]),
     "tq_mla_no_alloc_read_device_error": (_I32, [_VP, _P(_I32)]),

@@ -151,3 +151,62 @@ def context_merge(comm: Comm, part_out, part_lse, out=None, lse=None, stream=Non
     _abi.raise_for(_abi.lib.tq_mla_context_merge(ctypes.byref(p), comm.handle,
                                                  _stream_handle(stream)))
     return out, lse
+
+
+class _DeviceArray:
+    """Exposes a device address range to torch (``__cuda_array_interface__``, no copy)."""
+
+    def __init__(self, address, shape, typestr):
+        self.__cuda_array_interface__ = {"data": (int(address), False), "shape": tuple(shape),
+                                         "typestr": typestr, "version": 3}
+
+
+class PeerMerge:
+    """The context merge over NVLink peer memory (``tq_peer_merge_*``): created collectively on
+    ``comm`` for ``tokens`` x ``heads`` rows. ``part_out`` (f32 ``[T, H, 512]``) and ``part_lse``
+    (f32 ``[T, H]``) view this rank's exchange region: decode into them, then call ``merge``.
+    Every rank calls ``merge`` once per step, in the same order."""
+
+    def __init__(self, comm: Comm, tokens: int, heads: int):
+        import torch
+
+        from . import _abi
+
+        self.comm = comm
+        self.handle = ctypes.c_void_p()
+        _abi.raise_for(_abi.lib.tq_peer_merge_create(comm.handle, tokens, heads,
+                                                     ctypes.byref(self.handle)))
+        po, pl = ctypes.c_uint64(), ctypes.c_uint64()
+        _abi.raise_for(_abi.lib.tq_peer_merge_partials(self.handle, ctypes.byref(po),
+                                                       ctypes.byref(pl)))
+        self.part_out = torch.as_tensor(_DeviceArray(po.value, (tokens, heads, 512), "<f4"),
+                                        device="cuda")
+        self.part_lse = torch.as_tensor(_DeviceArray(pl.value, (tokens, heads), "<f4"),
+                                        device="cuda")
+
+    def merge(self, out, lse, stream=None):
+        """The merged ``out`` (bf16 or f32 ``[T, H, 512]``) and ``lse`` (f32 ``[T, H]``)."""
+        from . import _abi
+        from .ops import _TORCH_DTYPE, _stream_handle
+
+        _abi.raise_for(_abi.lib.tq_peer_merge(
+            self.handle, out.data_ptr(), lse.data_ptr(), out.stride(0) * out.element_size(),
+            out.stride(1) * out.element_size(), _TORCH_DTYPE[out.dtype], _stream_handle(stream)))
+        return out, lse
+
+    def device_error(self, stream=None):
+        from . import _abi
+        from .ops import _stream_handle
+
+        flags = ctypes.c_int32()
+        _abi.raise_for(_abi.lib.tq_peer_merge_read_error(self.handle, _stream_handle(stream),
+                                                         ctypes.byref(flags)))
+        return flags.value
+
+    def destroy(self):
+        from . import _abi
+
+        if self.handle:
+            self.part_out = self.part_lse = None
+            _abi.raise_for(_abi.lib.tq_peer_merge_destroy(self.handle))
+            self.handle = ctypes.c_void_p()
