@@ -1476,7 +1476,11 @@ def run_context(args, world, rank, local_rank):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic",
-        "config": job_config(args.config, world, full, strong=True),
+        "config": dict(job_config(args.config, world, full, strong=True),
+                       parallelism=f"context split x{world} (each sequence's pages over the "
+                                   "ranks; " + ("partials read over NVLink by one merge kernel "
+                                                "per rank" if peer else "NCCL all-gather + LSE "
+                                                "merge") + ")"),
         "e2e": {"value": tokens / (e2e_ms * 1e-3), "unit": UNIT,
                 "h2d_bytes_per_step": int(h_q.numel() * 2),
                 "d2h_bytes_per_step": int(h_out.numel() * 2 + h_lse.numel() * 4),
@@ -1522,7 +1526,7 @@ def main():
                     help="weak: N ranks hold N times the one-GPU batch; strong: the batch stays "
                          "fixed and is shared (longctx: each sequence's pages split over the "
                          "ranks, merged over NCCL)")
-    ap.add_argument("--merge", choices=["nccl", "peer"], default="nccl",
+    ap.add_argument("--merge", choices=["nccl", "peer"], default="peer",
                     help="long-context split (--config longctx --scaling strong, N > 1): merge "
                          "the ranks' partials by an NCCL all-gather + merge kernel, or by one "
                          "kernel reading the peers' partials over NVLink")
