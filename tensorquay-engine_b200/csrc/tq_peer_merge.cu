@@ -77,6 +77,9 @@ struct Args {
 };
 
 __global__ void __launch_bounds__(128) peer_merge_kernel(Args a) {
+  // Launched as a programmatic dependent of the decode's last kernel: nothing is read or
+  // published before that kernel's results are complete and visible.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   uint32_t* h = a.header;
   __shared__ uint32_t s_step;
   __shared__ int s_ok;
@@ -183,7 +186,17 @@ int32_t peer_merge_launch(const PeerMergeLaunch& L, void* stream_handle) {
       cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
     return TQ_ERR_CUDA;
   const uint64_t want = a.rows < uint64_t(4 * sms) ? a.rows : uint64_t(4 * sms);
-  peer::peer_merge_kernel<<<unsigned(want ? want : 1), 128, 0, stream>>>(a);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(unsigned(want ? want : 1), 1, 1);
+  cfg.blockDim = dim3(128, 1, 1);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, peer::peer_merge_kernel, a) != cudaSuccess) return TQ_ERR_CUDA;
   return cudaGetLastError() == cudaSuccess ? TQ_OK : TQ_ERR_CUDA;
 }
 
