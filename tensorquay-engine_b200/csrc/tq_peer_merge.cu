@@ -9,10 +9,11 @@
 //                   ready[r] and done[r] (u32 per rank, written by rank r over NVLink)
 //   partials:       f32 out [T, H, 512], then f32 lse [T, H]
 // Merge k (every rank calls it in the same order; k is this rank's device-side step counter):
-//   1. block 0 publishes ready = k + 1 into every peer's header (release at system scope, after
-//      a system fence, so the decode kernel's partials are visible to a peer that sees it);
+//   1. block 0 publishes ready = k + 1 into every peer's header (a release store at system
+//      scope, after griddepcontrol.wait, so the decode kernel's partials are visible to a peer
+//      that acquires it);
 //   2. every block waits until all peers' ready in its own header reach k + 1 (bounded);
-//   3. blocks merge rows (t, h): m = max lse, w_r = exp(lse_r - m), out = sum_r w_r o_r / sum w,
+//   3. blocks merge rows (t, h), four at a time: m = max lse, w_r = exp(lse_r - m), out = sum_r w_r o_r / sum w,
 //      lse = m + ln sum w, reading the peers' rows over NVLink (L2-only loads);
 //   4. the last block to finish publishes done = k + 1 into every peer's header, waits until
 //      all peers' done reach k + 1 (they have read this rank's partials), and advances the step.
@@ -76,7 +77,7 @@ struct Args {
   int out_bf16;
 };
 
-__global__ void __launch_bounds__(128) peer_merge_kernel(Args a) {
+__global__ void __launch_bounds__(512) peer_merge_kernel(Args a) {
   // Launched as a programmatic dependent of the decode's last kernel: nothing is read or
   // published before that kernel's results are complete and visible.
   asm volatile("griddepcontrol.wait;" ::: "memory");
@@ -91,7 +92,8 @@ __global__ void __launch_bounds__(128) peer_merge_kernel(Args a) {
   const uint32_t k = s_step;
   if (!s_ok) return;  // an earlier timeout: the plan is unusable
   if (blockIdx.x == 0 && threadIdx.x == 0) {
-    __threadfence_system();  // the decode kernel's partials, before the flag
+    // The decode's partials are complete and visible here (griddepcontrol.wait); the release
+    // store orders them before the flag for a peer that acquires it.
     for (int r = 0; r < a.nranks; ++r)
       if (r != a.rank) st_release_sys(a.peer_headers[r] + kPeerHdrReady + a.rank, k + 1);
   }
@@ -103,26 +105,37 @@ __global__ void __launch_bounds__(128) peer_merge_kernel(Args a) {
   }
   __syncthreads();
   if (s_ok) {
-    const int c = threadIdx.x * 4;  // this thread's 4 of the row's 512 values
-    for (uint64_t row = blockIdx.x; row < a.rows; row += gridDim.x) {
+    // Four rows at a time per block: 128 threads per row, 4 of its 512 values per thread.
+    const int tr = threadIdx.x & 127, c = tr * 4;
+    for (uint64_t row = blockIdx.x * 4ull + (threadIdx.x >> 7); row < a.rows;
+         row += gridDim.x * 4ull) {
+      // Every rank's lse and this thread's 4 values of the row, all loads in flight together.
       float lr[kPeerMaxRanks];
-      float m = -INFINITY;
-      for (int r = 0; r < a.nranks; ++r) {
-        lr[r] = __ldcg(reinterpret_cast<const float*>(a.regions[r] + a.lse_offset) + row);
-        m = fmaxf(m, lr[r]);
+      float4 o[kPeerMaxRanks];
+#pragma unroll
+      for (int r = 0; r < kPeerMaxRanks; ++r) {
+        if (r < a.nranks) {
+          lr[r] = __ldcg(reinterpret_cast<const float*>(a.regions[r] + a.lse_offset) + row);
+          o[r] = __ldcg(reinterpret_cast<const float4*>(a.regions[r] + a.out_offset +
+                                                        row * 2048) + tr);
+        }
       }
+      float m = -INFINITY;
+#pragma unroll
+      for (int r = 0; r < kPeerMaxRanks; ++r)
+        if (r < a.nranks) m = fmaxf(m, lr[r]);
       float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
       float wsum = 0.f;
       if (m != -INFINITY) {
-        for (int r = 0; r < a.nranks; ++r) {
+#pragma unroll
+        for (int r = 0; r < kPeerMaxRanks; ++r) {
+          if (r >= a.nranks) continue;
           const float w = expf(lr[r] - m);
           if (w == 0.f) continue;  // a part with no keys (lse -inf) adds nothing
-          const float4 o = __ldcg(reinterpret_cast<const float4*>(
-                                      a.regions[r] + a.out_offset + row * 2048) + threadIdx.x);
-          acc.x += w * o.x;
-          acc.y += w * o.y;
-          acc.z += w * o.z;
-          acc.w += w * o.w;
+          acc.x += w * o[r].x;
+          acc.y += w * o[r].y;
+          acc.z += w * o[r].z;
+          acc.w += w * o[r].w;
           wsum += w;
         }
       }
@@ -138,7 +151,7 @@ __global__ void __launch_bounds__(128) peer_merge_kernel(Args a) {
         *reinterpret_cast<float4*>(dst + c * 4) =
             make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
       }
-      if (threadIdx.x == 0) a.lse[row] = wsum > 0.f ? m + logf(wsum) : -INFINITY;
+      if (tr == 0) a.lse[row] = wsum > 0.f ? m + logf(wsum) : -INFINITY;
     }
   }
   // The last block to finish tells every peer this rank has read its partials, then waits for
@@ -149,7 +162,7 @@ __global__ void __launch_bounds__(128) peer_merge_kernel(Args a) {
     const uint32_t n = atomicAdd(h + kPeerHdrBlocks, 1u);
     if (n == gridDim.x - 1) {
       *reinterpret_cast<volatile uint32_t*>(h + kPeerHdrBlocks) = 0;
-      __threadfence_system();
+      // Every block's loads of peer memory returned before its fence and count above.
       for (int r = 0; r < a.nranks; ++r)
         if (r != a.rank) st_release_sys(a.peer_headers[r] + kPeerHdrDone + a.rank, k + 1);
       if (!wait_all(h + kPeerHdrDone, a.nranks, a.rank, k + 1))
@@ -185,10 +198,11 @@ int32_t peer_merge_launch(const PeerMergeLaunch& L, void* stream_handle) {
   if (cudaGetDevice(&dev) != cudaSuccess ||
       cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
     return TQ_ERR_CUDA;
-  const uint64_t want = a.rows < uint64_t(4 * sms) ? a.rows : uint64_t(4 * sms);
+  const uint64_t quads = (a.rows + 3) / 4;
+  const uint64_t want = quads < uint64_t(sms) ? quads : uint64_t(sms);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(unsigned(want ? want : 1), 1, 1);
-  cfg.blockDim = dim3(128, 1, 1);
+  cfg.blockDim = dim3(512, 1, 1);
   cfg.dynamicSmemBytes = 0;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
