@@ -607,6 +607,23 @@ def run_prologue(args, world, rank, local_rank):
     barrier()
     times = [a.elapsed_time(b) for a, b in evs]
     ms_step = max_over_ranks(sum(times) / len(times))
+    # The same step captured once in a CUDA graph and replayed (launch gaps removed), L2 flushed
+    # before each replay as above.
+    graph = torch.cuda.CUDAGraph()
+    cap = torch.cuda.Stream(dev)
+    with torch.cuda.graph(graph, stream=cap):
+        pro(flags=flags, stream=cap)
+    torch.cuda.synchronize(dev)
+    gevs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+            for _ in range(args.steps)]
+    for a, b in gevs:
+        flush.fill_(1)
+        a.record(stream)
+        graph.replay()
+        b.record(stream)
+    torch.cuda.synchronize(dev)
+    graph_ms = max_over_ranks(sum(a.elapsed_time(b) for a, b in gevs) / len(gevs))
+    del graph
     # End to end: x, positions and sequence ids copied in from pinned host memory, the device
     # flags read back (q stays on the device for the attention step that consumes it).
     h_flags = torch.zeros(1, dtype=torch.int32).pin_memory()
@@ -659,6 +676,10 @@ def run_prologue(args, world, rank, local_rank):
                      "peak_source": f"{src_name} (MEASURED_PEAKS.json)",
                      "algorithmic_bytes_per_step": nbytes},
         "self_check": {"q_within_tolerance": ok, "tokens": t},
+        "graph": {"ms_per_step": graph_ms, "value": world * t / (graph_ms * 1e-3),
+                  "frac": nbytes / (graph_ms * 1e-3) / 1e9 / hbm,
+                  "what": "the step captured in one CUDA graph, replayed; L2 flushed before "
+                          "each replay"},
         "clocks": clock.summary(),
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
