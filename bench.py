@@ -672,7 +672,7 @@ def run_prologue(args, world, rank, local_rank):
         "library_launches_per_step": 4,
         "roofline": {"bound": "hbm", "achieved": ach, "peak": hbm, "unit": "GB/s",
                      "frac": ach / hbm, "traffic": None,
-                     "kernel": "whole prologue step (4 cuBLAS GEMMs + norm, RoPE, writer)",
+                     "kernel": "whole prologue step (q_a, q_b and kv_a projections, absorption, norms, RoPE, writer)",
                      "peak_source": f"{src_name} (MEASURED_PEAKS.json)",
                      "algorithmic_bytes_per_step": nbytes},
         "self_check": {"q_within_tolerance": ok, "tokens": t},

@@ -47,4 +47,21 @@ struct PeerMergeLaunch {
 };
 int32_t peer_merge_launch(const PeerMergeLaunch& launch, void* stream);
 
+// Weight-streaming projection out[T, N] = bf16(x[T, K] . w[N, K]^T) for T <= 128 tokens
+// (tq_proj.cu): K split over the `splits` CTAs of a cluster per 128-row weight tile, their f32
+// partial tiles added in split order through distributed shared memory.
+struct ProjLaunch {
+  const uint16_t* x;  // bf16 [T, K], packed
+  const uint16_t* w;  // bf16 [N, K], packed
+  int t, k, n;
+  int splits;         // K splits (CTAs of one cluster), 1 to kProjMaxSplits; 0 picks them
+  uint16_t* out;      // bf16 [T, N]
+  int* flags;         // device error flags, may be null
+};
+constexpr int kProjMaxTokens = 128;
+constexpr int kProjMaxSplits = 8;
+// The K split of an N x K projection that balances the weight bytes over `sms` SMs.
+int proj_splits(int n, int k, int t, int sms);
+int32_t proj_launch(const ProjLaunch& launch, void* stream);
+
 }  // namespace tq

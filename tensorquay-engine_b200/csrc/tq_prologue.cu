@@ -184,6 +184,16 @@ Layout layout_of(const TqPrologueSpec& s) {
   return l;
 }
 
+// Decode-sized batches (T <= 128 tokens) take the weight-streaming projections of tq_proj.cu
+// for the narrow projections (q_a, kv_a: at most one 128-row weight tile per two SMs, so K is
+// split over a cluster); wide ones (q_b) stay with the library GEMM, which streams them faster.
+bool use_proj(const TqPrologueSpec& s) {
+  return s.x.shape[0] >= 1 && s.x.shape[0] <= uint64_t(kProjMaxTokens) &&
+         s.x.shape[1] >= 128 && s.w_qa.shape[0] >= 128;
+}
+
+bool narrow(int n, int sms) { return 2 * ((n + 127) / 128) <= sms; }
+
 int sm_count(int device) {
   static std::mutex mu;
   static int cached[128] = {0};
@@ -314,13 +324,31 @@ extern "C" int32_t tq_mla_prologue(const TqPrologueSpec* spec, void* workspace,
     const char* bad = nullptr;
     int32_t status = TQ_OK;
     constexpr uint64_t kHalf = kCublasScratch / 2;
+    const bool proj = use_proj(s);
+    // Decode sizes: the weight-streaming projections, K splits balanced for this device.
+    auto project = [&](const void* in, uint64_t wt, uint16_t* out, int k, int n,
+                       cudaStream_t st) {
+      tq::ProjLaunch P;
+      P.x = static_cast<const uint16_t*>(in);
+      P.w = reinterpret_cast<const uint16_t*>(wt);
+      P.t = T;
+      P.k = k;
+      P.n = n;
+      P.splits = tq::proj_splits(n, k, T, sms);
+      P.out = out;
+      P.flags = device_flags;
+      return tq::proj_launch(P, st) == TQ_OK;
+    };
     // 6: kvf = x . w_kva^T, its RoPE slice rotated in place; 7: norm and paged write.
-    if (b->set_stream(h, sd->stream) != CUBLAS_STATUS_SUCCESS ||
-        b->set_workspace(h, ws + l.scratch + kHalf, kHalf) != CUBLAS_STATUS_SUCCESS)
+    if (proj && narrow(width, sms)) {
+      if (!project(x, s.w_kva.device_address, kvf, dm, width, sd->stream)) bad = "proj_kv_a";
+    } else if (b->set_stream(h, sd->stream) != CUBLAS_STATUS_SUCCESS ||
+               b->set_workspace(h, ws + l.scratch + kHalf, kHalf) != CUBLAS_STATUS_SUCCESS) {
       bad = "cublas_setup";
-    else if (gemm_nt(b, h, x, reinterpret_cast<const void*>(s.w_kva.device_address), kvf, T,
-                     width, dm) != CUBLAS_STATUS_SUCCESS)
+    } else if (gemm_nt(b, h, x, reinterpret_cast<const void*>(s.w_kva.device_address), kvf, T,
+                       width, dm) != CUBLAS_STATUS_SUCCESS) {
       bad = "gemm_kv_a";
+    }
     if (!bad && dr) {
       const long long kblocks = ((long long)T + 7) / 8;
       rope_rows_kernel<<<int(kblocks < cap ? kblocks : cap), 256, 0, sd->stream>>>(
@@ -335,14 +363,17 @@ extern "C" int32_t tq_mla_prologue(const TqPrologueSpec* spec, void* workspace,
     if (!bad && (b->set_stream(h, cs) != CUBLAS_STATUS_SUCCESS ||
                  b->set_workspace(h, ws + l.scratch, kHalf) != CUBLAS_STATUS_SUCCESS))
       bad = "cublas_setup";
-    if (!bad && gemm_nt(b, h, x, reinterpret_cast<const void*>(s.w_qa.device_address), cq, T,
-                        rq, dm) != CUBLAS_STATUS_SUCCESS)
+    if (!bad && (proj && narrow(rq, sms) ? !project(x, s.w_qa.device_address, cq, dm, rq, cs)
+                      : gemm_nt(b, h, x, reinterpret_cast<const void*>(s.w_qa.device_address), cq,
+                                T, rq, dm) != CUBLAS_STATUS_SUCCESS))
       bad = "gemm_q_a";
     if (!bad) {
       rms_rows_kernel<<<int(T < cap ? T : cap), 256, 0, cs>>>(
           cq, rq, T, reinterpret_cast<const uint16_t*>(s.q_norm.device_address), s.q_eps);
-      if (gemm_nt(b, h, cq, reinterpret_cast<const void*>(s.w_qb.device_address), qf, T,
-                  H * (dn + dr), rq) != CUBLAS_STATUS_SUCCESS)
+      if (proj && narrow(H * (dn + dr), sms)
+              ? !project(cq, s.w_qb.device_address, qf, rq, H * (dn + dr), cs)
+               : gemm_nt(b, h, cq, reinterpret_cast<const void*>(s.w_qb.device_address), qf, T,
+                         H * (dn + dr), rq) != CUBLAS_STATUS_SUCCESS)
         bad = "gemm_q_b";
     }
     // 4: per head h, row-major q[:, h, :512] = qf[:, h, :Dn] . w_uk[h]; column-major that is

@@ -8,7 +8,7 @@ from pathlib import Path
 
 PKG = Path(__file__).resolve().parent
 CSRC = PKG.parent / "csrc"
-SOURCES = ["tq_mla_kernels.cu", "tq_kv_write.cu", "tq_prologue.cu", "tq_peer_merge.cu",
+SOURCES = ["tq_mla_kernels.cu", "tq_kv_write.cu", "tq_prologue.cu", "tq_proj.cu", "tq_peer_merge.cu",
            "tq_contracts.cpp", "tq_comm.cpp"]
 HEADERS = ["tq_ptx.cuh", "tq_mla_layout.h", "tq_contracts.h"]
 TARGET = PKG / "libtq_mla.so"

@@ -80,7 +80,7 @@ def _case(device, *, tokens, dm, rq, heads, dn, dr, fmt, seqs=5, slots=40, pool_
 def _check_q(q, q_ref):
     """Within two bf16 steps of the value plus 2^-6 of the head row's RMS, relative L2 within
     2^-8, and at least half of the values bit-equal. The device accumulates its GEMMs in f32 in
-    cuBLAS's order: a bf16 rounding of cq or qf that lands on the other side moves every value
+    its own order (cuBLAS's, or the projection kernel's K boxes and splits): a bf16 rounding of cq or qf that lands on the other side moves every value
     after it by ~6e-4 of the row's scale (the same chain in PyTorch's bf16 matmuls gives this
     library's bits exactly). A wrong head, transpose, sign or rotation is off by the row's scale."""
     rms = np.sqrt(np.mean(q_ref ** 2, axis=-1, keepdims=True))
@@ -143,6 +143,19 @@ def test_rope_576_sizes_and_large_positions(cuda_device):
     assert r["q"].shape == (40, 128, 576)
     _check_q(r["q"], r["q_ref"])
     _check_rows(r)
+
+
+@pytest.mark.parametrize("tokens,dm", [(1, 1000), (33, 1536), (128, 1000), (129, 1536)])
+def test_token_counts_and_ragged_tiles(cuda_device, tokens, dm):
+    """Decode batches of 1 to 128 tokens take the weight-streaming projections (token tiles of
+    16, 48 and 128 rows; a hidden size that ends inside a 64-wide chunk; Q rank and head widths
+    that end inside a 128-row weight tile); 129 tokens take the library GEMMs."""
+    r = _case(cuda_device, tokens=tokens, dm=dm, rq=320, heads=12, dn=128, dr=64,
+              fmt=_abi.KV_BF16_ROPE576, slots=64, pool_pages=200, seed=10 + tokens)
+    assert r["q"].shape == (tokens, 12, 576)
+    _check_q(r["q"], r["q_ref"])
+    _check_rows(r)
+    assert r["flags"] == 0
 
 
 def test_out_of_range_token_flags_and_keeps_its_query(cuda_device):
