@@ -131,37 +131,54 @@ __global__ void __launch_bounds__(256) rms_rows_kernel(uint16_t* x, int width, l
   }
 }
 
-// Rotation of pair i of the 64 RoPE values at position `pos`: angle pos * theta^(-2i/64),
+// cos and sin of pair i of the 64 RoPE values at position `pos`: angle pos * theta^(-2i/64),
 // reduced modulo 2 pi in f64.
-__device__ __forceinline__ void rope_pair(float x0, float x1, int i, int pos, double log2_theta,
-                                          float* y0, float* y1) {
+__device__ __forceinline__ void rope_angle(int i, int pos, double log2_theta, float* c, float* s) {
   const double freq = exp2(-double(2 * i) / double(kRopeDim) * log2_theta);
   const double angle = fmod(double(pos) * freq, 6.283185307179586476925286766559);
-  double s, c;
-  sincos(angle, &s, &c);
-  const float cf = float(c), sf = float(s);
-  *y0 = x0 * cf - x1 * sf;
-  *y1 = x0 * sf + x1 * cf;
+  double sd, cd;
+  sincos(angle, &sd, &cd);
+  *c = float(cd);
+  *s = float(sd);
 }
 
-// dst[r, 2i .. 2i + 1] = rope(src[r, 2i .. 2i + 1]) at pos[r / per_token], for `rows` rows of 64
-// values at the given element offsets and row strides: one warp per row, lane i one pair. Each
-// lane reads its pair before writing it, so src may equal dst (the kv RoPE slice is rotated in
-// place). q: rows (t, h), src qf + Dn, dst q + 512; kv: rows t, src = dst = kvf + 512.
+// dst[r, 2i .. 2i + 1] = rope(src[r, 2i .. 2i + 1]) for the `per_token` rows r of each of
+// `tokens` tokens (row r = t * per_token + j, position pos[t]), rows of 64 values at the given
+// element offsets and row strides. Block (x, y) takes rows 64 y .. 64 y + 63 of tokens x,
+// x + gridDim.x, ...: the first warp computes the token's 32 (cos, sin) pairs once into shared
+// memory, then each warp rotates eight whole rows (all eight loaded before any is written), lane
+// i pair i. Each lane reads its pairs before writing them, so src may equal dst (the kv RoPE
+// slice is rotated in place). q: per_token H, src qf + Dn, dst q + 512; kv: per_token 1,
+// src = dst = kvf + 512.
 __global__ void __launch_bounds__(256) rope_rows_kernel(const uint16_t* src, long long src_stride,
                                                         uint16_t* dst, long long dst_stride,
-                                                        long long rows, int per_token,
+                                                        long long tokens, int per_token,
                                                         const int* __restrict__ pos,
                                                         double log2_theta) {
-  const int lane = threadIdx.x & 31;
-  for (long long r = (blockIdx.x * 256ll + threadIdx.x) >> 5; r < rows;
-       r += (gridDim.x * 256ll) >> 5) {
-    const uint32_t in = *reinterpret_cast<const uint32_t*>(src + r * src_stride + 2 * lane);
-    float y0, y1;
-    rope_pair(bf16_to_f32(uint16_t(in & 0xFFFF)), bf16_to_f32(uint16_t(in >> 16)), lane,
-              pos[r / per_token], log2_theta, &y0, &y1);
-    *reinterpret_cast<uint32_t*>(dst + r * dst_stride + 2 * lane) =
-        uint32_t(f32_to_bf16(y0)) | (uint32_t(f32_to_bf16(y1)) << 16);
+  __shared__ float s_cos[kRopeDim / 2], s_sin[kRopeDim / 2];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  for (long long t = blockIdx.x; t < tokens; t += gridDim.x) {
+    if (warp == 0) rope_angle(lane, pos[t], log2_theta, &s_cos[lane], &s_sin[lane]);
+    __syncthreads();
+    const float c = s_cos[lane], sn = s_sin[lane];
+    const int j0 = int(blockIdx.y) * 64 + warp * 8;
+    uint32_t in[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u)
+      if (j0 + u < per_token)
+        in[u] = *reinterpret_cast<const uint32_t*>(
+            src + (t * per_token + j0 + u) * src_stride + 2 * lane);
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      if (j0 + u < per_token) {
+        const float x0 = bf16_to_f32(uint16_t(in[u] & 0xFFFF));
+        const float x1 = bf16_to_f32(uint16_t(in[u] >> 16));
+        const float y0 = x0 * c - x1 * sn, y1 = x0 * sn + x1 * c;
+        *reinterpret_cast<uint32_t*>(dst + (t * per_token + j0 + u) * dst_stride + 2 * lane) =
+            uint32_t(f32_to_bf16(y0)) | (uint32_t(f32_to_bf16(y1)) << 16);
+      }
+    }
+    __syncthreads();  // s_cos / s_sin are reused by the next token
   }
 }
 
@@ -350,8 +367,7 @@ extern "C" int32_t tq_mla_prologue(const TqPrologueSpec* spec, void* workspace,
       bad = "gemm_kv_a";
     }
     if (!bad && dr) {
-      const long long kblocks = ((long long)T + 7) / 8;
-      rope_rows_kernel<<<int(kblocks < cap ? kblocks : cap), 256, 0, sd->stream>>>(
+      rope_rows_kernel<<<int(T < cap ? T : cap), 256, 0, sd->stream>>>(
           kvf + kLatent, width, kvf + kLatent, width, T, 1, pos, log2_theta);
       if (cudaGetLastError() != cudaSuccess) bad = "launch";
     }
@@ -388,9 +404,8 @@ extern "C" int32_t tq_mla_prologue(const TqPrologueSpec* spec, void* workspace,
       bad = "gemm_absorb";
     // 5: the RoPE slices of q
     if (!bad && dr) {
-      const long long qrows = (long long)T * H, qblocks = (qrows + 7) / 8;
-      rope_rows_kernel<<<int(qblocks < cap ? qblocks : cap), 256, 0, cs>>>(
-          qf + dn, dn + dr, q + kLatent, width, qrows, H, pos, log2_theta);
+      rope_rows_kernel<<<dim3(unsigned(T < cap ? T : cap), unsigned((H + 63) / 64)), 256, 0, cs>>>(
+          qf + dn, dn + dr, q + kLatent, width, T, H, pos, log2_theta);
     }
     if (!bad && cudaGetLastError() != cudaSuccess) bad = "launch";
     // Join.
