@@ -14,8 +14,9 @@
 //   7. tq_kv_write: bf16(rms(kvf[:512])) * kv_norm and the row written (FP8 rows quantized) to the
 //      token's pool slot through the page table
 // Steps 6-7 (the cache branch) run on a per-device side stream, forked from the caller's stream
-// by an event and joined back into it before the call returns, beside steps 1-5 (the query
-// branch) on the caller's stream; the pattern is graph-capturable.
+// by an event and joined back into it before the call returns, beside steps 1-4 (the query
+// branch) on the caller's stream; step 5 follows on the side stream once q_b is written, beside
+// the absorption. The pattern is graph-capturable.
 // The GEMMs are cuBLAS (opened at run time as libcublas.so.12: a process that already has it,
 // e.g. through PyTorch, shares that copy); everything else is this library's kernels. At decode
 // sizes the step is HBM-bound on the weights (w_qb and w_uk dominate). The q norm accumulates
@@ -228,6 +229,7 @@ int sm_count(int device) {
 struct Side {
   cudaStream_t stream = nullptr;
   cudaEvent_t fork = nullptr, join = nullptr;
+  cudaEvent_t qf_ready = nullptr;  // q's RoPE starts on the side stream once q_b is written
 };
 
 Side* side_for(int device) {
@@ -240,7 +242,8 @@ Side* side_for(int device) {
     Side made;
     if (cudaStreamCreateWithFlags(&made.stream, cudaStreamNonBlocking) != cudaSuccess ||
         cudaEventCreateWithFlags(&made.fork, cudaEventDisableTiming) != cudaSuccess ||
-        cudaEventCreateWithFlags(&made.join, cudaEventDisableTiming) != cudaSuccess)
+        cudaEventCreateWithFlags(&made.join, cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventCreateWithFlags(&made.qf_ready, cudaEventDisableTiming) != cudaSuccess)
       return nullptr;
     sd = made;
   }
@@ -392,6 +395,19 @@ extern "C" int32_t tq_mla_prologue(const TqPrologueSpec* spec, void* workspace,
                          H * (dn + dr), rq) != CUBLAS_STATUS_SUCCESS)
         bad = "gemm_q_b";
     }
+    // 5: the RoPE slices of q, which need only qf: on the side stream (its cache branch is
+    // queued ahead), beside the absorption, which writes the other columns of q's rows.
+    if (!bad && dr) {
+      if (cudaEventRecord(sd->qf_ready, cs) != cudaSuccess ||
+          cudaStreamWaitEvent(sd->stream, sd->qf_ready, 0) != cudaSuccess) {
+        bad = "fork";
+      } else {
+        rope_rows_kernel<<<dim3(unsigned(T < cap ? T : cap), unsigned((H + 63) / 64)), 256, 0,
+                           sd->stream>>>(qf + dn, dn + dr, q + kLatent, width, T, H, pos,
+                                         log2_theta);
+        if (cudaGetLastError() != cudaSuccess) bad = "launch";
+      }
+    }
     // 4: per head h, row-major q[:, h, :512] = qf[:, h, :Dn] . w_uk[h]; column-major that is
     // q^T = w_uk[h]^T . qf^T with w_uk[h] seen as a 512 x Dn matrix (ld 512), qf[:, h] as
     // Dn x T (ld H (Dn + Dr)) and q[:, h] as 512 x T (ld H W).
@@ -402,11 +418,6 @@ extern "C" int32_t tq_mla_prologue(const TqPrologueSpec* spec, void* workspace,
                                 dn + dr, &zero, q, CUDA_R_16BF, H * width, width, H,
                                 CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT) != CUBLAS_STATUS_SUCCESS)
       bad = "gemm_absorb";
-    // 5: the RoPE slices of q
-    if (!bad && dr) {
-      rope_rows_kernel<<<dim3(unsigned(T < cap ? T : cap), unsigned((H + 63) / 64)), 256, 0, cs>>>(
-          qf + dn, dn + dr, q + kLatent, width, T, H, pos, log2_theta);
-    }
     if (!bad && cudaGetLastError() != cudaSuccess) bad = "launch";
     // Join.
     if (cudaEventRecord(sd->join, sd->stream) != cudaSuccess ||
