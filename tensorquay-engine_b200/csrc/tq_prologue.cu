@@ -4,7 +4,7 @@
 // (rope_dim 0, docs/research/glm-5.md:163-167) and for 576-wide rows (rope_dim 64).
 //
 // Per call (T tokens, Dr = rope_dim, W = 512 + Dr):
-//   1. cq  = x . w_qa^T                 plain GEMM, bf16 in, f32 accumulate, bf16 out
+//   1. cq  = x . w_qa^T                 GEMM, bf16 in, f32 accumulate, bf16 out
 //   2. cq <- bf16(rms(cq)) * q_norm     rms_rows_kernel (in place)
 //   3. qf  = cq . w_qb^T                plain GEMM                       [T, H, Dn + Dr]
 //   4. q[:, :, :512] = qf[:, :, :Dn] . w_uk[h]   one strided-batched GEMM over the heads, written
@@ -17,8 +17,10 @@
 // by an event and joined back into it before the call returns, beside steps 1-4 (the query
 // branch) on the caller's stream; step 5 follows on the side stream once q_b is written, beside
 // the absorption. The pattern is graph-capturable.
-// The GEMMs are cuBLAS (opened at run time as libcublas.so.12: a process that already has it,
-// e.g. through PyTorch, shares that copy); everything else is this library's kernels. At decode
+// At decode sizes (T <= 128) the narrow projections (steps 1 and 6) run on tq_proj.cu's
+// weight-streaming kernel; the other GEMMs are cuBLAS (opened at run time as libcublas.so.12: a
+// process that already has it, e.g. through PyTorch, shares that copy); everything else is this
+// library's kernels. At decode
 // sizes the step is HBM-bound on the weights (w_qb and w_uk dominate). The q norm accumulates
 // squares in f32; RoPE reduces its angle pos * theta^(-2i/64) in f64 before the sine and cosine,
 // so positions up to 2^31 keep full precision.
@@ -103,7 +105,8 @@ __device__ __forceinline__ uint16_t f32_to_bf16(float x) {
 // Rows of `width` bf16 values (packed, `rows` of them): x <- bf16(bf16(x * r) * w), r = 1 /
 // sqrt(mean of squares + eps), squares summed in f32; the normalised value is rounded to bf16
 // before the weight multiplies it, as in the model's RMSNorm (weight * hidden.to(bf16)). One
-// 256-thread block per row, grid-stride.
+// 256-thread block per row, grid-stride; a thread takes eight values at a time (16-byte loads
+// and stores: width is a multiple of 8 and the rows and weights are 16-byte aligned).
 __global__ void __launch_bounds__(256) rms_rows_kernel(uint16_t* x, int width, long long rows,
                                                        const uint16_t* __restrict__ w, float eps) {
   __shared__ float part[8];
@@ -111,9 +114,15 @@ __global__ void __launch_bounds__(256) rms_rows_kernel(uint16_t* x, int width, l
   for (long long row = blockIdx.x; row < rows; row += gridDim.x) {
     uint16_t* v = x + row * width;
     float sq = 0.f;
-    for (int i = threadIdx.x; i < width; i += 256) {
-      const float f = bf16_to_f32(v[i]);
-      sq += f * f;
+    for (int i = threadIdx.x * 8; i < width; i += 256 * 8) {
+      const uint4 p = *reinterpret_cast<const uint4*>(v + i);
+      const uint32_t u[4] = {p.x, p.y, p.z, p.w};
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float f0 = bf16_to_f32(uint16_t(u[k] & 0xFFFF)), f1 = bf16_to_f32(uint16_t(u[k] >> 16));
+        sq += f0 * f0;
+        sq += f1 * f1;
+      }
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xFFFFFFFFu, sq, o);
@@ -126,8 +135,23 @@ __global__ void __launch_bounds__(256) rms_rows_kernel(uint16_t* x, int width, l
     }
     __syncthreads();
     const float r = s_r;
-    for (int i = threadIdx.x; i < width; i += 256)
-      v[i] = f32_to_bf16(bf16_to_f32(f32_to_bf16(bf16_to_f32(v[i]) * r)) * bf16_to_f32(w[i]));
+    for (int i = threadIdx.x * 8; i < width; i += 256 * 8) {
+      const uint4 p = *reinterpret_cast<const uint4*>(v + i);
+      const uint4 q = *reinterpret_cast<const uint4*>(w + i);
+      const uint32_t u[4] = {p.x, p.y, p.z, p.w}, g[4] = {q.x, q.y, q.z, q.w};
+      uint32_t o[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const uint16_t lo = f32_to_bf16(
+            bf16_to_f32(f32_to_bf16(bf16_to_f32(uint16_t(u[k] & 0xFFFF)) * r)) *
+            bf16_to_f32(uint16_t(g[k] & 0xFFFF)));
+        const uint16_t hi = f32_to_bf16(
+            bf16_to_f32(f32_to_bf16(bf16_to_f32(uint16_t(u[k] >> 16)) * r)) *
+            bf16_to_f32(uint16_t(g[k] >> 16)));
+        o[k] = uint32_t(lo) | (uint32_t(hi) << 16);
+      }
+      *reinterpret_cast<uint4*>(v + i) = make_uint4(o[0], o[1], o[2], o[3]);
+    }
     __syncthreads();  // part / s_r are reused by the next row
   }
 }
