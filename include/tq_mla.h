@@ -319,9 +319,11 @@ int32_t tq_kv_write(const TqKvWriteSpec* spec, int32_t* device_flags, void* stre
  * and `row` is written (as tq_kv_write writes it, FP8 rows quantized) to pool row
  * page_table[seq_id[t]][pos[t] / 64] * 64 + pos[t] % 64.
  * rms(v) = v / sqrt(mean(v^2) + eps), computed in f32. rope rotates pairs (2i, 2i + 1) by the
- * angle pos * theta^(-2i / Dr) (angle reduced in f64). The projections are plain bf16 GEMMs with
- * f32 accumulation (cuBLAS, opened at run time as libcublas.so.12); the norms, RoPE, the
- * assembly of q and the row writes are this library's kernels.
+ * angle pos * theta^(-2i / Dr) (angle reduced in f64). The projections are bf16 GEMMs with f32
+ * accumulation: for T <= 128 the narrow ones (q_a and kv_a, at most one 128-row weight tile per
+ * two SMs) on this library's weight-streaming tcgen05 kernel, the others on cuBLAS (opened at
+ * run time as libcublas.so.12); the norms, RoPE, the assembly of q and the row writes are this
+ * library's kernels.
  *   x        bf16 [T, Dm]              w_qa  bf16 [Rq, Dm]          q_norm  bf16 [Rq]
  *   w_qb     bf16 [H * (Dn + Dr), Rq]  w_uk  bf16 [H, Dn, 512]      w_kva   bf16 [W, Dm]
  *   kv_norm  bf16 [512]                pos, seq_id i32 [T]          page_table i32 [S, L]
@@ -332,8 +334,10 @@ int32_t tq_kv_write(const TqKvWriteSpec* spec, int32_t* device_flags, void* stre
  * may be null); its q is still produced. The workspace (tq_mla_prologue_workspace_bytes, 256-byte
  * aligned) holds the intermediates and cuBLAS's scratch; the first call on a device creates
  * that device's cuBLAS handle and the side stream on which the cache branch (kv_a projection,
- * RoPE, write) runs beside the query branch (forked from and joined back into `stream` with
- * events), so make it before capturing a stream. Calls are serialised on
+ * RoPE, write) and then q's RoPE run beside the query branch (forked from and joined back into
+ * `stream` with events), and the first call with a given token count asks the occupancy
+ * calculator for the projection kernel's grid, so make those calls before capturing a stream.
+ * Calls are serialised on
  * the host (one cuBLAS handle per device). No reference counterpart exists beyond the plan
  * line above. */
 typedef struct {
